@@ -1,0 +1,435 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 row-op hot path (libtb_b200.so), one JSON line.
+
+Workload: one pass of the per-token row ops of a Llama-7B-shape prefill of
+4096 tokens -- the reference engine's layer ops batched over rows:
+  embedding gather          ids [4096] -> rows of a [32000, 4096] table
+  residual + RMSNorm        [4096, 4096]                    } one fused
+  RoPE on Q and K           [4096, 32, 128] x 2, pos 0..4095 } layer-chain
+  SwiGLU silu(gate)*up      [4096, 11008]                    } launch
+  row softmax               logits [4096, 32000] f32
+  greedy argmax             logits [4096, 32000] f32 (own buffer)
+Activations bf16 (f32 arithmetic), logits f32; synthetic seeded inputs with
+the reference config's distributions.  Every op reads distinct buffers and a
+step moves ~2.2 GB, far more than the 126 MB L2, so nothing is served from
+L2 across steps.
+
+metric: algorithmic HBM bytes of the step (each input read once, each
+output written once) / device time, in GB/s, over all ranks; rows/s beside
+it.  --gpus N (torchrun) runs the same per-GPU workload on every rank (weak
+scaling, no collective in the data path) and takes the max time over ranks.
+
+--impl reference times the reference's own CPU kernels (oracle/_ref, the
+reference's src/ops/*.c) on the host's cores over a bounded row sample of
+the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "tensorbit-run_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import workloads as W  # noqa: E402
+
+CFG = W.CONFIGS["7b"]
+METRIC = "fused layer-op HBM GB/s"
+WORKLOAD = "llama7b-prefill-4096 row ops (embedding, residual+RMSNorm, RoPE, SwiGLU, " \
+           "softmax, argmax)"
+
+
+def step_bytes(rows, act_s):
+    c = CFG
+    parts = {
+        "embedding": W.bytes_embedding(rows, c.hidden, act_s),
+        "layer_chain": (W.bytes_res_rms(rows, c.hidden, act_s)
+                        + W.bytes_rope(rows, c.n_q_heads, c.n_kv_heads, c.head_dim, act_s)
+                        + W.bytes_swiglu(rows, c.intermediate, act_s)),
+        "softmax": W.bytes_softmax(rows, c.vocab, 4),
+        "argmax": W.bytes_argmax(rows, c.vocab, 4),
+    }
+    return parts
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples SM clock and clock-event reasons with NVML while running."""
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, index, uuid=None):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        try:
+            import pynvml as N
+            N.nvmlInit()
+            self.N = N
+            self.h = None
+            if uuid:
+                try:
+                    self.h = N.nvmlDeviceGetHandleByUUID(uuid)
+                except Exception:
+                    self.h = None
+            if self.h is None:
+                self.h = N.nvmlDeviceGetHandleByIndex(index)
+            self.get_reasons = getattr(N, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                N.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM)
+        except Exception as e:  # no NVML: report it, do not guess
+            self.N, self.err = None, str(e)
+
+    def _run(self):
+        N = self.N
+        while not self._stop.is_set():
+            try:
+                self.samples.append(N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM))
+                bits = self.get_reasons(self.h)
+                for b, name in self.REASONS.items():
+                    if bits & b:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.005)
+
+    def __enter__(self):
+        if self.N:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self.N:
+            self.t.join()
+
+    def summary(self):
+        if not self.N:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": self.err}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons - {"gpu_idle"}),
+                "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------- CPU baseline
+def cpu_sample(rows=256):
+    """One pass of the step over `rows` rows of every op, on the host cores,
+    through the reference's own kernels (oracle/_ref; the restatement if the
+    reference build is absent).  Returns (run, bytes, kind, cores)."""
+    import numpy as np
+    from oracle import oracle as O
+    O.lib()
+    impl, kind = (O.REF, "reference") if O.ref_available() else (O.PORT, "port")
+    cores = os.cpu_count() or 1
+    c = CFG
+    li = W.layer_inputs(c, rows=rows)
+    bf = O.f32_to_bf16
+    x, res, gam = bf(li["x"]), bf(li["res"]), bf(li["gamma"])
+    q, k = bf(li["q"]), bf(li["k"])
+    gate, up = bf(li["gate"]), bf(li["up"])
+    rng = np.random.default_rng(c.seed + 7)
+    table = bf(rng.standard_normal((c.vocab, c.hidden), dtype=np.float32) * np.float32(0.02))
+    ids = rng.integers(0, c.vocab, rows).astype(np.int32)
+    lg_s = W.logits(c, rows=rows)
+    lg_a = W.normal(c, 10, (rows, c.vocab), std=c.logit_std)
+
+    def run():
+        O.embedding(ids, table, impl, cores)
+        O.residual_rms_norm(x, res, gam, c.eps, impl, cores)
+        O.rope(q, k, li["pos"], c.theta, impl, cores)
+        O.swiglu(gate, up, impl, cores)
+        O.softmax(lg_s, None, impl, cores)
+        O.argmax(lg_a, impl, cores)
+
+    return run, sum(step_bytes(rows, 2).values()), kind, cores
+
+
+def cpu_baseline(seconds=12.0, rows=256):
+    """Reported CPU baseline: repeat the sample for about `seconds`."""
+    run, nbytes, kind, cores = cpu_sample(rows)
+    run()  # warm-up: page faults, thread start-up
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        run()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or reps >= 500:
+            break
+    return {"value": round(nbytes * reps / el / 1e9, 3), "unit": "GB/s", "cores": cores,
+            "kind": kind,
+            "sample": f"{rows} of {CFG.rows} rows of every op of the step, x{reps} "
+                      f"({el:.1f} s on {cores} threads)",
+            "rows_per_s": round(rows * reps / el, 1)}
+
+
+def run_reference(args, world):
+    """--impl reference: the reference's CPU kernels on this host's cores.
+    Each step is one pass of the step's ops over a 256-row sample."""
+    rows = 256
+    run, nbytes, kind, cores = cpu_sample(rows)
+    for _ in range(args.warmup):
+        run()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    v = round(nbytes / sec / 1e9, 3)
+    return {"metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded, reference config distributions)", "impl": "reference",
+            "config": {"workload": WORKLOAD, "rows_sampled": rows, "rows_per_step": CFG.rows},
+            "rows_per_s": round(rows / sec, 1),
+            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": cores, "kind": kind,
+                             "sample": f"{rows} of {CFG.rows} rows of every op per step, "
+                                       f"median of {args.steps} steps on {cores} threads"},
+            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+# ------------------------------------------------------------------ GPU arm
+def build_inputs(torch, dev, seed, rows=None):
+    c = CFG
+    g = torch.Generator(device=dev)
+
+    def randn(shape, std=1.0, mean=0.0, dtype=torch.bfloat16, k=0):
+        g.manual_seed(seed + k)
+        return (torch.randn(shape, generator=g, device=dev) * std + mean).to(dtype)
+
+    R = c.rows if rows is None else rows
+    t = {
+        "table": randn((c.vocab, c.hidden), 0.02, k=7),
+        "ids": torch.randint(0, c.vocab, (R,), generator=g, device=dev, dtype=torch.int32),
+        "x": randn((R, c.hidden), k=0), "res": randn((R, c.hidden), k=1),
+        "gamma": randn((c.hidden,), 0.1, 1.0, k=2),
+        "q": randn((R, c.n_q_heads, c.head_dim), k=3), "k": randn((R, c.n_kv_heads, c.head_dim), k=4),
+        "gate": randn((R, c.intermediate), k=5), "up": randn((R, c.intermediate), k=6),
+        "pos": torch.arange(R, dtype=torch.int32, device=dev),
+        "logits_s": randn((R, c.vocab), c.logit_std, dtype=torch.float32, k=9),
+        "logits_a": randn((R, c.vocab), c.logit_std, dtype=torch.float32, k=10),
+    }
+    o = {
+        "emb": torch.empty((R, c.hidden), dtype=torch.bfloat16, device=dev),
+        "h": torch.empty_like(t["x"]), "y": torch.empty_like(t["x"]),
+        "act": torch.empty_like(t["gate"]),
+        "probs": torch.empty_like(t["logits_s"]),
+        "tok": torch.empty(R, dtype=torch.int32, device=dev),
+    }
+    return t, o
+
+
+def run_gpu(args, rank, world, local):
+    import torch
+    import torch.distributed as dist
+    import tb_b200 as T
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    L = T.lib()
+    R, c = args.rows, CFG
+    t, o = build_inputs(torch, dev, 12345 + 1000 * rank, R)
+    table = T.rope_table(CFG.theta, CFG.head_dim, R)
+    stream = torch.cuda.current_stream()
+    sp = C.c_void_p(stream.cuda_stream)
+    chain = T.make_chain(t["x"], t["res"], t["gamma"], o["h"], o["y"], CFG.eps, t["q"], t["k"],
+                         t["pos"], CFG.theta, table, t["gate"], t["up"], o["act"])
+
+    ops = {
+        "embedding": lambda: T.check(L.tb_b200_embedding(T.BF16, R, c.hidden, c.vocab, T.ptr(t["ids"]),
+                                                         T.ptr(t["table"]), T.ptr(o["emb"]), sp),
+                                     "embedding"),
+        "layer_chain": lambda: T.check(L.tb_b200_layer_chain(C.byref(chain), sp), "layer_chain"),
+        "softmax": lambda: T.check(L.tb_b200_softmax(T.F32, R, c.vocab, T.ptr(t["logits_s"]), None,
+                                                     T.ptr(o["probs"]), sp), "softmax"),
+        "argmax": lambda: T.check(L.tb_b200_argmax(T.F32, R, c.vocab, T.ptr(t["logits_a"]),
+                                                   T.ptr(o["tok"]), sp), "argmax"),
+    }
+
+    def step():
+        for f in ops.values():
+            f()
+
+    if args.profile_op:
+        for _ in range(args.warmup + args.steps):
+            ops[args.profile_op]()
+        torch.cuda.synchronize()
+        return None
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        x = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(x, op=dist.ReduceOp.MAX)
+        return float(x.item())
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = L.tb_b200_launch_count()
+    uuid = getattr(torch.cuda.get_device_properties(dev), "uuid", None)
+    uuid = f"GPU-{uuid}" if uuid is not None else None
+    with ClockSampler(local, uuid) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        e1.synchronize()
+    launches = L.tb_b200_launch_count() - l0
+    torch.cuda.synchronize()
+    barrier()
+    ms_total = max_over_ranks(e0.elapsed_time(e1))
+    ms = ms_total / args.steps
+
+    # per-kernel device time inside full steps (for the roofline)
+    names = list(ops)
+    evs = {n: [] for n in names}
+    for _ in range(max(3, min(args.steps, 50))):
+        for n in names:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            ops[n]()
+            b.record(stream)
+            evs[n].append((a, b))
+    torch.cuda.synchronize()
+    per_op_ms = {n: statistics.mean(a.elapsed_time(b) for a, b in evs[n]) for n in names}
+    parts = step_bytes(R, 2)
+    step_b = sum(parts.values())
+    peak, peak_kind = peaks()
+    dom = max(per_op_ms, key=per_op_ms.get)
+    achieved = parts[dom] / (per_op_ms[dom] / 1e3) / 1e9
+    per_op = {n: {"ms": round(per_op_ms[n], 4), "GB/s": round(parts[n] / per_op_ms[n] / 1e6, 1),
+                  "frac": round(parts[n] / per_op_ms[n] / 1e6 / peak, 3),
+                  "bytes": parts[n]} for n in names}
+
+    # end to end through the C ABI: pinned host inputs in, outputs back out
+    ins = ["ids", "x", "res", "q", "k", "gate", "up", "logits_s", "logits_a"]
+    outs = ["emb", "h", "y", "q", "k", "act", "probs", "tok"]
+    host_in = {n: torch.empty_like(t[n], device="cpu").pin_memory() for n in ins}
+    for n in ins:
+        host_in[n].copy_(t[n])
+    host_out = {n: torch.empty_like((o.get(n) if n in o else t[n]), device="cpu").pin_memory()
+                for n in outs}
+    bi = sum(host_in[n].numel() * host_in[n].element_size() for n in ins)
+    bo = sum(host_out[n].numel() * host_out[n].element_size() for n in outs)
+
+    def e2e_step():
+        for n in ins:
+            T.check(L.tb_b200_memcpy_h2d(T.ptr(t[n]), C.c_void_p(host_in[n].data_ptr()),
+                                         host_in[n].numel() * host_in[n].element_size(), sp), "h2d")
+        step()
+        for n in outs:
+            src = o[n] if n in o else t[n]
+            T.check(L.tb_b200_memcpy_d2h(C.c_void_p(host_out[n].data_ptr()), T.ptr(src),
+                                         host_out[n].numel() * host_out[n].element_size(), sp),
+                    "d2h")
+
+    e2e_steps = max(3, min(args.steps, 10))
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    b.record(stream)
+    b.synchronize()
+    e2e_ms = max_over_ranks(a.elapsed_time(b)) / e2e_steps
+
+    total_bytes = step_b * world
+    line = {
+        "metric": METRIC, "value": round(total_bytes / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded, reference config distributions)",
+        "config": {"workload": WORKLOAD, "rows_per_gpu": R, "hidden": c.hidden,
+                   "heads": [c.n_q_heads, c.n_kv_heads, c.head_dim],
+                   "intermediate": c.intermediate, "vocab": c.vocab,
+                   "activations": "bf16 (f32 arithmetic)", "logits": "f32",
+                   "bytes_per_step_per_gpu": step_b,
+                   "l2": "inputs larger than L2: ~2.2 GB of distinct buffers per step",
+                   "parallelism": f"row-sharded x{world}, no data-path collective"},
+        "rows_per_s": round(R * world / (ms / 1e3), 1),
+        "per_op": per_op,
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1),
+                     "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
+                     "frac": round(achieved / peak, 3), "traffic": None},
+        "e2e": {"value": round(total_bytes / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": bi,
+                "d2h_bytes_per_step": bo, "api": "tb_b200_* C ABI, pinned host buffers"},
+        "gpu_launches": int(launches),
+        "clocks": clocks.summary(),
+    }
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-op", choices=["embedding", "layer_chain", "softmax", "argmax"],
+                    help="only launch this op (warmup + steps times) on --rows rows: a small "
+                         "case for ncu captures")
+    ap.add_argument("--rows", type=int, default=CFG.rows)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args, world)))
+        return
+
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    try:
+        line = run_gpu(args, rank, world, local)
+        if line is None:
+            return
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline()
+        if rank == 0:
+            print(json.dumps(line))
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,252 @@
+/*
+ * tb_b200.h -- C ABI of the B200 (sm_100a) row-op library, libtb_b200.so.
+ *
+ * Plain pointers and sizes only.  Every data pointer below is CUDA device
+ * memory unless stated otherwise; `stream` is a cudaStream_t passed as void*
+ * (NULL selects the library's current stream, see tb_b200_set_stream).  All
+ * kernel entry points are asynchronous on that stream and return a TbError
+ * code (include/tb_types.h): TB_OK, TB_ERR_INVALID_ARG / TB_ERR_INVALID_SHAPE
+ * for rejected arguments (nothing is launched), TB_ERR_UNSUPPORTED_DTYPE, or
+ * TB_ERR_DEVICE when a CUDA call fails (tb_b200_last_error() has the text).
+ *
+ * dtype is a TbDtype value: TB_DTYPE_F32 or TB_DTYPE_BF16.  bf16 variants
+ * read and write bf16 and compute in f32.
+ *
+ * Row layout: a [rows, cols] buffer is dense row-major (row stride = cols).
+ *
+ * Each kernel entry point replaces the reference's per-vector CPU kernel
+ * (include/tensorbit/run/ops.h) applied once per row; the citation on each
+ * declaration names the reference function whose arithmetic it reproduces.
+ * The registry-level route (TbOpFn adapters behind tb_dispatch_*) is in
+ * include/tb_backend.h.
+ */
+#ifndef TB_B200_H
+#define TB_B200_H
+
+#include "tb_types.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TB_B200_ABI_VERSION 1
+
+/* ======================================================================
+ * Runtime: devices, memory, streams, status
+ * (the reference has no device layer; its CUDA adapters passed host memory
+ *  to kernels, src/backend/cuda/registry.c:68-78.  These are new.)
+ * ====================================================================== */
+
+/* ABI version of the loaded library (TB_B200_ABI_VERSION it was built with). */
+int tb_b200_version(void);
+/* Text of the last CUDA/NCCL failure seen on the calling thread ("" if none). */
+const char* tb_b200_last_error(void);
+
+/* Kernels launched by this library since it was loaded (all threads). */
+unsigned long long tb_b200_launch_count(void);
+
+int tb_b200_device_count(int* count);
+int tb_b200_set_device(int device);
+int tb_b200_get_device(int* device);
+
+int tb_b200_malloc(void** ptr, size_t bytes);
+int tb_b200_free(void* ptr);
+/* Page-locked host memory, for fast and asynchronous host<->device copies. */
+int tb_b200_malloc_host(void** ptr, size_t bytes);
+int tb_b200_free_host(void* ptr);
+int tb_b200_memcpy_h2d(void* dst_dev, const void* src_host, size_t bytes, void* stream);
+int tb_b200_memcpy_d2h(void* dst_host, const void* src_dev, size_t bytes, void* stream);
+int tb_b200_memcpy_d2d(void* dst_dev, const void* src_dev, size_t bytes, void* stream);
+int tb_b200_memset(void* dst_dev, int value, size_t bytes, void* stream);
+
+/* Current stream of the calling thread for calls given stream == NULL.
+ * Initially NULL, i.e. the CUDA legacy default stream. */
+int tb_b200_set_stream(void* stream);
+void* tb_b200_get_stream(void);
+int tb_b200_stream_sync(void* stream);
+int tb_b200_sync(void);
+
+/* Stream-ordered scratch: copy `bytes` of host memory into a new device
+ * buffer allocated on `stream` (cudaMallocAsync), and release such a buffer
+ * on `stream` once the work queued after it has used it. */
+int tb_b200_stage_h2d(const void* src_host, size_t bytes, void** dst_dev, void* stream);
+int tb_b200_stage_release(void* dev, void* stream);
+
+/* *is_device = 1 if p is device (or managed) memory of any GPU, else 0. */
+int tb_b200_is_device_ptr(const void* p, int* is_device);
+
+/* Kernels record rejected data (for example a token id outside [0, vocab))
+ * in a per-device status word instead of faulting.  This synchronises
+ * `stream`, returns TB_ERR_INVALID_ARG if any flag was raised since the
+ * last check (TB_OK otherwise), optionally reports the raw flags, and
+ * clears them. */
+int tb_b200_check_status(void* stream, unsigned int* flags_out);
+#define TB_B200_FLAG_TOKEN_RANGE 0x1u   /* embedding: id < 0 or id >= vocab */
+
+/* ======================================================================
+ * Row kernels
+ * ====================================================================== */
+
+/* Fused residual add + RMSNorm over [rows, cols]:
+ *   h = x + residual                     (src/ops/residual.c:4-13)
+ *   y = (h * (1/sqrtf((eps + sum h^2)/cols))) * weight   (src/ops/norm.c:4-26)
+ * h_out receives h (may be NULL; may alias x or residual for an in-place
+ * residual-stream update); weight may be NULL (no scaling, norm.c:20-22).
+ * The normalisation uses the f32 sum, not the rounded h, in bf16 mode.  */
+int tb_b200_residual_rms_norm(int dtype, int64_t rows, int64_t cols, const void* x,
+                              const void* residual, const void* weight, void* h_out, void* y,
+                              float eps, void* stream);
+
+/* RMSNorm of each row (tb_cpu_rms_norm_f32, src/ops/norm.c:4-26). */
+int tb_b200_rms_norm(int dtype, int64_t rows, int64_t cols, const void* x, const void* weight,
+                     void* y, float eps, void* stream);
+
+/* y = x + residual over n elements (tb_cpu_residual_add_f32, src/ops/residual.c:4-13). */
+int tb_b200_residual_add(int dtype, int64_t n, const void* x, const void* residual, void* y,
+                         void* stream);
+
+/* y = x / (1 + expf(-x)) (tb_cpu_silu_f32, src/ops/activation.c:18-27). */
+int tb_b200_silu(int dtype, int64_t n, const void* x, void* y, void* stream);
+
+/* tanh-GELU (tb_cpu_gelu_f32, src/ops/activation.c:4-16). */
+int tb_b200_gelu(int dtype, int64_t n, const void* x, void* y, void* stream);
+
+/* out = silu(gate) * up, the engine's SwiGLU composition
+ * (include/tensorbit/run/ops.hpp:246-248). */
+int tb_b200_swiglu(int dtype, int64_t n, const void* gate, const void* up, void* out,
+                   void* stream);
+
+/* Rotary table: table[p][i] = {cosf(p*f_i), sinf(p*f_i)} for p < n_positions,
+ * i < head_dim/2, f_i = 1.0f/powf(theta, (2.0f*i)/(float)head_dim), all
+ * computed on the host with the C library exactly as src/ops/rope.c:52-54
+ * does, then copied to table_dev (n_positions*head_dim floats). */
+int tb_b200_rope_table(float theta, int head_dim, int n_positions, float* table_dev,
+                       void* stream);
+
+/* In-place interleaved-pair RoPE of q [rows, n_q_heads, head_dim] and
+ * k [rows, n_kv_heads, head_dim], row r at positions[r] (device int32)
+ * (tb_cpu_rope_gqa_f32, src/ops/rope.c:43-81, once per token).
+ * table/table_positions: a tb_b200_rope_table for this theta and head_dim;
+ * rows whose position is outside [0, table_positions), or all rows when
+ * table is NULL, compute the angle's cos/sin on the device instead
+ * (within 2 ulp of the C library rather than identical). */
+int tb_b200_rope_rows(int dtype, int64_t rows, int n_q_heads, int n_kv_heads, int head_dim,
+                      void* q, void* k, const int32_t* positions, float theta,
+                      const float* table, int table_positions, void* stream);
+
+/* Single-token RoPE at one position (the TB_OP_ROPE contract,
+ * src/backend/cpu/rope.c:4-19): q [n_q_heads, head_dim], k [n_kv_heads,
+ * head_dim].  cos/sin come from the host C library for that position. */
+int tb_b200_rope(int dtype, int n_q_heads, int n_kv_heads, int head_dim, void* q, void* k,
+                 int position, float theta, void* stream);
+
+/* Row softmax over [rows, cols] with an optional additive mask of the same
+ * shape (tb_cpu_softmax_f32, src/ops/softmax.c:4-32).  The row sum is the
+ * reference's left-to-right f32 sum, reproduced exactly (not a tree sum). */
+int tb_b200_softmax(int dtype, int64_t rows, int64_t cols, const void* x, const void* mask,
+                    void* y, void* stream);
+
+/* out[r] = index of the first maximum of row r; NaN never wins; a NaN at
+ * index 0 keeps 0 (sample_argmax, src/main.cpp:79-89).  Bit-exact. */
+int tb_b200_argmax(int dtype, int64_t rows, int64_t cols, const void* x, int32_t* out,
+                   void* stream);
+
+/* y[t] = table[ids[t]] for t < n_tokens; table [vocab, dim]; ids device
+ * int32 (tb_cpu_embedding_f32, src/ops/embedding.c:4-14).  Bit-exact copy.
+ * An id outside [0, vocab) zero-fills its row and raises
+ * TB_B200_FLAG_TOKEN_RANGE (the reference reads out of bounds there). */
+int tb_b200_embedding(int dtype, int64_t n_tokens, int64_t dim, int64_t vocab, const int32_t* ids,
+                      const void* table, void* y, void* stream);
+
+/* The same gather with the ids in host memory, as the engine passes them
+ * (tb_dispatch_embedding, src/backend/cpu/registry.c:186-192): ids are
+ * range-checked on the host (TB_ERR_INVALID_ARG, nothing queued, on any id
+ * outside [0, vocab)) and staged to the device on `stream`. */
+int tb_b200_embedding_host_ids(int dtype, int64_t n_tokens, int64_t dim, int64_t vocab,
+                               const int32_t* ids_host, const void* table, void* y,
+                               void* stream);
+
+/* One launch that runs a transformer layer's three row-op groups on their
+ * own tensors: residual+RMSNorm [rows, hidden]; RoPE on q/k at per-row
+ * positions; SwiGLU over [rows, intermediate] (the per-layer row ops of
+ * TransformerRunner::forward, include/tensorbit/run/ops.hpp:120-248).
+ * Results are identical to the three separate entry points.  A group whose
+ * size is 0 (hidden, n_q_heads+n_kv_heads, or intermediate) is skipped. */
+typedef struct {
+    int dtype;
+    int64_t rows;
+    /* residual + RMSNorm */
+    int64_t hidden;
+    const void* x;
+    const void* residual;
+    const void* norm_weight;
+    void* h_out;
+    void* y;
+    float eps;
+    /* RoPE */
+    int n_q_heads;
+    int n_kv_heads;
+    int head_dim;
+    void* q;
+    void* k;
+    const int32_t* positions;
+    float theta;
+    const float* rope_table;
+    int rope_table_positions;
+    /* SwiGLU */
+    int64_t intermediate;
+    const void* gate;
+    const void* up;
+    void* act_out;
+} TbB200LayerChain;
+
+int tb_b200_layer_chain(const TbB200LayerChain* chain, void* stream);
+
+/* ======================================================================
+ * Multi-GPU (one process per GPU)
+ * ====================================================================== */
+
+/* Contiguous split of `total` items over `parts`: part p gets
+ * [lo, hi); the first total%parts parts get one extra item. */
+int tb_b200_partition(int64_t total, int parts, int part, int64_t* lo, int64_t* hi);
+
+/* The exchange plan of tb_b200_embedding_sharded for `rank` (host only,
+ * no device work): with ids (n_tokens host int32, all in [0, vocab)),
+ *   send_counts[d]  rows this rank sends to rank d (0 for d == rank);
+ *   send_rows       this rank's table-shard rows to send, destination-major,
+ *                   token order within a destination (capacity n_tokens);
+ *   recv_counts[s]  rows this rank receives from rank s;
+ *   recv_rows       output rows (within this rank's token part) the received
+ *                   rows go to, source-major, token order (capacity n_tokens);
+ *   local_dst/src   (output row, table-shard row) of tokens this rank owns
+ *                   both ends of; *n_local of them (capacity n_tokens). */
+int tb_b200_shard_plan(int64_t n_tokens, int64_t vocab, int nranks, int rank,
+                       const int32_t* ids_host, int64_t* send_counts, int64_t* recv_counts,
+                       int32_t* send_rows, int32_t* recv_rows, int32_t* local_dst,
+                       int32_t* local_src, int64_t* n_local);
+
+/* NCCL communicator of this process.  Rank 0 calls tb_b200_comm_unique_id
+ * and shares the 128 bytes with the other ranks out of band; every rank
+ * then calls tb_b200_comm_init with its own rank on its own device. */
+#define TB_B200_COMM_ID_BYTES 128
+int tb_b200_comm_unique_id(void* id_out);
+int tb_b200_comm_init(int nranks, int rank, const void* unique_id, int device);
+int tb_b200_comm_destroy(void);
+int tb_b200_comm_info(int* rank, int* nranks);
+
+/* Vocab-sharded embedding gather over the communicator.  Every rank holds
+ * the same n_tokens ids (host int32), the table rows of its vocab part
+ * (tb_b200_partition(vocab, nranks, rank)) in table_shard, and receives the
+ * rows of its token part (tb_b200_partition(n_tokens, nranks, rank)) in
+ * y_local.  Owned rows are copied locally; the rest arrive from their
+ * owners through one grouped NCCL send/recv exchange.  Bit-exact with
+ * tb_cpu_embedding_f32 over the full table.  Ids outside [0, vocab) return
+ * TB_ERR_INVALID_ARG before any work is queued. */
+int tb_b200_embedding_sharded(int dtype, int64_t n_tokens, int64_t dim, int64_t vocab,
+                              const int32_t* ids_host, const void* table_shard, void* y_local,
+                              void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TB_B200_H */

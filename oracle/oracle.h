@@ -1,0 +1,89 @@
+/*
+ * oracle.h -- CPU oracle for the tensorbit-run row-op hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  Nothing in the shipped library links, loads or
+ * calls this code; it exists so the parity tests, the smoke check and the
+ * CPU-baseline leg of bench.py have an independent CPU answer to compare the
+ * sm_100a kernels against.
+ *
+ * Two implementations sit behind the same row-batched driver API:
+ *   ORC_IMPL_PORT  -- port.c, a restatement of the reference's per-vector C
+ *                     kernels (each function cites the file:line it follows),
+ *                     compiled with the reference's own Release/SIMD flags
+ *                     (-O3 -mavx2 -mfma, gnu11) so FMA contraction matches;
+ *   ORC_IMPL_REF   -- the reference's own src/ops/*.c, compiled unmodified
+ *                     from the reference tree into oracle/_ref/libtbref.so by
+ *                     oracle/Makefile and resolved at run time with dlopen.
+ * The port is pinned to the reference by tests/test_oracle.py (bit-exact on
+ * seeded inputs) and by the committed golden checksums in tests/golden/.
+ *
+ * Row semantics (both implementations): a [rows, cols] row-major buffer is
+ * processed by calling the reference's per-vector kernel once per row.
+ */
+#ifndef TB_ORACLE_H
+#define TB_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { ORC_IMPL_PORT = 0, ORC_IMPL_REF = 1 };
+/* dtype codes follow TbDtype (include/tensorbit/run/common.h:89-99). */
+enum { ORC_F32 = 0, ORC_BF16 = 2 };
+
+/* ---- per-vector restatements (port.c) ---------------------------------- */
+int orc_rms_norm_f32(size_t n, const float* x, const float* weight, float* y, float eps);
+int orc_residual_add_f32(size_t n, const float* x, const float* residual, float* y);
+int orc_gelu_f32(size_t n, const float* x, float* y);
+int orc_silu_f32(size_t n, const float* x, float* y);
+int orc_rope_gqa_f32(int n_q_heads, int n_kv_heads, int head_dim, float* q, float* k,
+                     int position, float theta_base);
+int orc_softmax_f32(size_t n, const float* x, const float* mask, float* y);
+int orc_embedding_f32(const int* token_ids, int n_tokens, int embedding_dim, const float* table,
+                      float* y);
+int orc_argmax_f32(const float* logits, int n);
+int orc_swiglu_f32(size_t n, const float* gate, const float* up, float* out);
+
+/* bf16 <-> f32 (round to nearest even; NaN stays a quiet NaN). */
+uint16_t orc_f32_to_bf16(float f);
+float orc_bf16_to_f32(uint16_t h);
+
+/* ---- reference library ------------------------------------------------- */
+/* Load oracle/_ref/libtbref.so (the reference's own kernels).  0 on success. */
+int orc_load_ref(const char* path);
+int orc_ref_loaded(void);
+
+/* ---- row-batched drivers (rows.c) --------------------------------------
+ * impl: ORC_IMPL_PORT / ORC_IMPL_REF.  dtype: ORC_F32 / ORC_BF16 (bf16 rows
+ * are widened to f32, computed by the f32 kernel, rounded back RNE).
+ * nthreads <= 1 runs on the calling thread; more splits rows into contiguous
+ * blocks, one pthread each.  Return 0, or a nonzero TbError-style code.   */
+int orc_rows_residual_rms_norm(int impl, int dtype, int64_t rows, int64_t cols, const void* x,
+                               const void* residual, const void* weight, void* h_out, void* y,
+                               float eps, int nthreads);
+int orc_rows_rms_norm(int impl, int dtype, int64_t rows, int64_t cols, const void* x,
+                      const void* weight, void* y, float eps, int nthreads);
+int orc_rows_residual_add(int impl, int dtype, int64_t rows, int64_t cols, const void* x,
+                          const void* residual, void* y, int nthreads);
+int orc_rows_gelu(int impl, int dtype, int64_t rows, int64_t cols, const void* x, void* y,
+                  int nthreads);
+int orc_rows_silu(int impl, int dtype, int64_t rows, int64_t cols, const void* x, void* y,
+                  int nthreads);
+int orc_rows_swiglu(int impl, int dtype, int64_t rows, int64_t cols, const void* gate,
+                    const void* up, void* out, int nthreads);
+int orc_rows_rope(int impl, int dtype, int64_t rows, int n_q_heads, int n_kv_heads, int head_dim,
+                  void* q, void* k, const int32_t* positions, float theta, int nthreads);
+int orc_rows_softmax(int impl, int dtype, int64_t rows, int64_t cols, const void* x,
+                     const void* mask, void* y, int nthreads);
+int orc_rows_argmax(int impl, int dtype, int64_t rows, int64_t cols, const void* x, int32_t* out,
+                    int nthreads);
+int orc_rows_embedding(int impl, int dtype, int64_t n_tokens, int64_t dim, const int32_t* ids,
+                       const void* table, void* y, int nthreads);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TB_ORACLE_H */

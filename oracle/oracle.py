@@ -1,0 +1,215 @@
+"""CPU oracle for the tensorbit-run row-op hot path -- TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
+``bench.py`` use this module, and only as the checker or the timed CPU
+reference; the shipped library never loads it.
+
+It wraps ``oracle/liboracle.so`` (the C restatement in ``port.c`` plus the
+row-batched drivers in ``rows.c``) and, when present, ``oracle/_ref/libtbref.so``
+(the reference's own ``src/ops/*.c`` compiled unmodified by ``oracle/Makefile``).
+Arrays are numpy; bf16 arrays are carried as ``np.uint16`` bit patterns.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PORT_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libtbref.so")
+
+PORT, REF = 0, 1
+F32, BF16 = 0, 2  # TbDtype codes (include/tensorbit/run/common.h:89-99)
+
+_lib = None
+
+
+def build(quiet: bool = True) -> None:
+    """Compile liboracle.so (and _ref/ when the reference tree is present)."""
+    out = subprocess.run(["make", "-C", HERE, "all"], capture_output=True, text=True)
+    if out.returncode != 0:
+        raise RuntimeError("oracle build failed:\n" + out.stdout + out.stderr)
+    if not quiet:
+        print(out.stdout)
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(PORT_SO):
+            build()
+        _lib = C.CDLL(PORT_SO)
+        _declare(_lib)
+        if os.path.exists(REF_SO):
+            _lib.orc_load_ref(REF_SO.encode())
+    return _lib
+
+
+def ref_available() -> bool:
+    return bool(lib().orc_ref_loaded())
+
+
+def _declare(L: C.CDLL) -> None:
+    vp, i64, i32, f32 = C.c_void_p, C.c_int64, C.c_int, C.c_float
+    L.orc_load_ref.argtypes = [C.c_char_p]
+    L.orc_rows_residual_rms_norm.argtypes = [i32, i32, i64, i64, vp, vp, vp, vp, vp, f32, i32]
+    L.orc_rows_rms_norm.argtypes = [i32, i32, i64, i64, vp, vp, vp, f32, i32]
+    L.orc_rows_residual_add.argtypes = [i32, i32, i64, i64, vp, vp, vp, i32]
+    L.orc_rows_gelu.argtypes = [i32, i32, i64, i64, vp, vp, i32]
+    L.orc_rows_silu.argtypes = [i32, i32, i64, i64, vp, vp, i32]
+    L.orc_rows_swiglu.argtypes = [i32, i32, i64, i64, vp, vp, vp, i32]
+    L.orc_rows_rope.argtypes = [i32, i32, i64, i32, i32, i32, vp, vp, vp, f32, i32]
+    L.orc_rows_softmax.argtypes = [i32, i32, i64, i64, vp, vp, vp, i32]
+    L.orc_rows_argmax.argtypes = [i32, i32, i64, i64, vp, vp, i32]
+    L.orc_rows_embedding.argtypes = [i32, i32, i64, i64, vp, vp, vp, i32]
+    L.orc_rms_norm_f32.argtypes = [C.c_size_t, vp, vp, vp, f32]
+    L.orc_softmax_f32.argtypes = [C.c_size_t, vp, vp, vp]
+    L.orc_argmax_f32.argtypes = [vp, i32]
+
+
+# ---------------------------------------------------------------- helpers
+def _p(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def _dt(a: np.ndarray) -> int:
+    if a.dtype == np.float32:
+        return F32
+    if a.dtype == np.uint16:
+        return BF16
+    raise TypeError(f"oracle: unsupported dtype {a.dtype}")
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"oracle {what} failed with code {rc}")
+
+
+def _c(a):
+    return None if a is None else np.ascontiguousarray(a)
+
+
+def f32_to_bf16(a: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even f32 -> bf16 bits (NaN kept quiet)."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    r[nan] = ((u[nan] >> 16) | 0x0040).astype(np.uint16)
+    return r
+
+
+def bf16_to_f32(a: np.ndarray) -> np.ndarray:
+    return (np.ascontiguousarray(a, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+# ---------------------------------------------------------------- row ops
+def residual_rms_norm(x, res, weight, eps, impl=PORT, threads=1):
+    x, res, weight = _c(x), _c(res), _c(weight)
+    rows, cols = x.shape
+    h = np.empty_like(x)
+    y = np.empty_like(x)
+    _check(lib().orc_rows_residual_rms_norm(impl, _dt(x), rows, cols, _p(x), _p(res), _p(weight),
+                                            _p(h), _p(y), eps, threads), "residual_rms_norm")
+    return h, y
+
+
+def rms_norm(x, weight, eps, impl=PORT, threads=1):
+    x, weight = _c(x), _c(weight)
+    rows, cols = x.shape
+    y = np.empty_like(x)
+    _check(lib().orc_rows_rms_norm(impl, _dt(x), rows, cols, _p(x), _p(weight), _p(y), eps,
+                                   threads), "rms_norm")
+    return y
+
+
+def residual_add(x, res, impl=PORT, threads=1):
+    x, res = _c(x), _c(res)
+    rows, cols = x.shape
+    y = np.empty_like(x)
+    _check(lib().orc_rows_residual_add(impl, _dt(x), rows, cols, _p(x), _p(res), _p(y), threads),
+           "residual_add")
+    return y
+
+
+def gelu(x, impl=PORT, threads=1):
+    x = _c(x)
+    rows, cols = x.shape
+    y = np.empty_like(x)
+    _check(lib().orc_rows_gelu(impl, _dt(x), rows, cols, _p(x), _p(y), threads), "gelu")
+    return y
+
+
+def silu(x, impl=PORT, threads=1):
+    x = _c(x)
+    rows, cols = x.shape
+    y = np.empty_like(x)
+    _check(lib().orc_rows_silu(impl, _dt(x), rows, cols, _p(x), _p(y), threads), "silu")
+    return y
+
+
+def swiglu(gate, up, impl=PORT, threads=1):
+    gate, up = _c(gate), _c(up)
+    rows, cols = gate.shape
+    out = np.empty_like(gate)
+    _check(lib().orc_rows_swiglu(impl, _dt(gate), rows, cols, _p(gate), _p(up), _p(out), threads),
+           "swiglu")
+    return out
+
+
+def rope(q, k, positions, theta, impl=PORT, threads=1):
+    """q [R, Hq, d], k [R, Hkv, d]; returns rotated copies."""
+    q = np.array(q, copy=True, order="C")
+    k = np.array(k, copy=True, order="C")
+    pos = np.ascontiguousarray(positions, dtype=np.int32)
+    rows, hq, d = q.shape
+    hkv = k.shape[1]
+    _check(lib().orc_rows_rope(impl, _dt(q), rows, hq, hkv, d, _p(q), _p(k), _p(pos), theta,
+                               threads), "rope")
+    return q, k
+
+
+def softmax(x, mask=None, impl=PORT, threads=1):
+    x, mask = _c(x), _c(mask)
+    rows, cols = x.shape
+    y = np.empty_like(x)
+    _check(lib().orc_rows_softmax(impl, _dt(x), rows, cols, _p(x), _p(mask), _p(y), threads),
+           "softmax")
+    return y
+
+
+def argmax(x, impl=PORT, threads=1):
+    x = _c(x)
+    rows, cols = x.shape
+    out = np.empty(rows, dtype=np.int32)
+    _check(lib().orc_rows_argmax(impl, _dt(x), rows, cols, _p(x), _p(out), threads), "argmax")
+    return out
+
+
+def embedding(ids, table, impl=PORT, threads=1):
+    ids, table = np.ascontiguousarray(ids, dtype=np.int32), _c(table)
+    dim = table.shape[1]
+    y = np.empty((ids.shape[0], dim), dtype=table.dtype)
+    _check(lib().orc_rows_embedding(impl, _dt(table), ids.shape[0], dim, _p(ids), _p(table),
+                                    _p(y), threads), "embedding")
+    return y
+
+
+# ---------------------------------------------------------------- vectors
+def rms_norm_vec(x, weight, eps):
+    """The per-vector kernel itself (one call, one vector)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = None if weight is None else np.ascontiguousarray(weight, dtype=np.float32)
+    y = np.empty_like(x)
+    _check(lib().orc_rms_norm_f32(x.size, _p(x), _p(w), _p(y), eps), "rms_norm_f32")
+    return y
+
+
+def softmax_vec(x, mask=None):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    m = None if mask is None else np.ascontiguousarray(mask, dtype=np.float32)
+    y = np.empty_like(x)
+    _check(lib().orc_softmax_f32(x.size, _p(x), _p(m), _p(y)), "softmax_f32")
+    return y

@@ -1,0 +1,335 @@
+// comm.cu -- NCCL communicator and the vocab-sharded embedding gather.
+//
+// The reference engine is single-process and has no communication layer;
+// its embedding is one memcpy per token from a full table
+// (src/ops/embedding.c:4-14).  At a 128K vocabulary the table is split by
+// vocabulary rows across the GPUs of one box while the token rows are split
+// by position, so a token's row usually lives on another GPU.  Each rank:
+//   1. builds, on the host, the exchange plan from the replicated ids:
+//      which of its table rows every other rank needs (in token order) and
+//      where the rows it receives go in its output (tb_b200_shard_plan);
+//   2. gathers the rows it owns: its own tokens' rows straight into its
+//      output, other ranks' rows into one packed send buffer (one kernel);
+//   3. exchanges packed rows with every peer in one grouped NCCL
+//      send/recv (NVLink/NVSwitch), only rows that are needed;
+//   4. scatters the received rows into its output (one kernel).
+// Every step is a byte copy, so the result is bit-exact with the
+// full-table gather.  The communicator is created non-blocking and every
+// wait on it is bounded (TB_B200_COMM_TIMEOUT_S seconds, default 120): a
+// rank that never arrives makes the others return TB_ERR_DEVICE after
+// aborting the communicator, instead of hanging.
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <chrono>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <thread>
+#include <vector>
+
+#include "tb_internal.h"
+
+namespace {
+
+ncclComm_t g_comm = nullptr;
+int g_rank = 0, g_nranks = 0;
+
+double timeout_s() {
+    const char* e = getenv("TB_B200_COMM_TIMEOUT_S");
+    const double v = e ? atof(e) : 0.0;
+    return v > 0 ? v : 120.0;
+}
+
+void nccl_error(const char* what, ncclResult_t r) {
+    char buf[384];
+    snprintf(buf, sizeof buf, "%s: %s", what, ncclGetErrorString(r));
+    tbh::set_error_text(buf);
+}
+
+// Wait until the non-blocking communicator finished the last call.
+int wait_comm(const char* what) {
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        ncclResult_t st = ncclSuccess;
+        ncclResult_t r = ncclCommGetAsyncError(g_comm, &st);
+        if (r != ncclSuccess) {
+            nccl_error(what, r);
+            return TB_ERR_DEVICE;
+        }
+        if (st == ncclSuccess) return TB_OK;
+        if (st != ncclInProgress) {
+            nccl_error(what, st);
+            ncclCommAbort(g_comm);
+            g_comm = nullptr;
+            return TB_ERR_DEVICE;
+        }
+        const double el =
+            std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if (el > timeout_s()) {
+            tbh::set_error_text("NCCL call timed out; communicator aborted");
+            ncclCommAbort(g_comm);
+            g_comm = nullptr;
+            return TB_ERR_DEVICE;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+// Copy n rows of `words` W-words: dst[drow(j)] = src[srow(j)], where a NULL
+// index list means the identity.
+template <typename W>
+__global__ void __launch_bounds__(256)
+k_rows(W* __restrict__ dst, const int32_t* __restrict__ drow, const W* __restrict__ src,
+       const int32_t* __restrict__ srow, int64_t n, int64_t words) {
+    constexpr int kGroup = 64;
+    const int64_t j = (int64_t)blockIdx.x * (blockDim.x / kGroup) + threadIdx.x / kGroup;
+    if (j >= n) return;
+    const int64_t di = drow ? drow[j] : j, si = srow ? srow[j] : j;
+    const W* s = src + si * words;
+    W* d = dst + di * words;
+    for (int64_t i = threadIdx.x % kGroup; i < words; i += kGroup) d[i] = s[i];
+}
+
+int copy_rows(void* dst, const int32_t* drow, const void* src, const int32_t* srow, int64_t n,
+              int64_t row_bytes, cudaStream_t s) {
+    if (n == 0) return TB_OK;
+    const unsigned grid = (unsigned)((n + 3) / 4);
+    const uintptr_t a = reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src);
+    if (row_bytes % 16 == 0 && (a & 15) == 0)
+        k_rows<uint4><<<grid, 256, 0, s>>>(static_cast<uint4*>(dst), drow,
+                                           static_cast<const uint4*>(src), srow, n, row_bytes / 16);
+    else if (row_bytes % 4 == 0 && (a & 3) == 0)
+        k_rows<uint32_t><<<grid, 256, 0, s>>>(static_cast<uint32_t*>(dst), drow,
+                                              static_cast<const uint32_t*>(src), srow, n,
+                                              row_bytes / 4);
+    else
+        k_rows<uint16_t><<<grid, 256, 0, s>>>(static_cast<uint16_t*>(dst), drow,
+                                              static_cast<const uint16_t*>(src), srow, n,
+                                              row_bytes / 2);
+    TB_LAUNCH_CHECK("row copy kernel");
+    return TB_OK;
+}
+
+int owner_of(int64_t id, int64_t vocab, int nranks) {
+    const int64_t base = vocab / nranks, extra = vocab % nranks;
+    const int64_t big = extra * (base + 1);
+    if (id < big) return (int)(id / (base + 1));
+    return (int)(extra + (id - big) / base);
+}
+
+}  // namespace
+
+extern "C" {
+
+int tb_b200_shard_plan(int64_t n_tokens, int64_t vocab, int nranks, int rank,
+                       const int32_t* ids, int64_t* send_counts, int64_t* recv_counts,
+                       int32_t* send_rows, int32_t* recv_rows, int32_t* local_dst,
+                       int32_t* local_src, int64_t* n_local) {
+    if (n_tokens < 0 || vocab < nranks || nranks < 1 || rank < 0 || rank >= nranks)
+        return TB_ERR_INVALID_ARG;
+    if (!send_counts || !recv_counts || !send_rows || !recv_rows || !local_dst || !local_src ||
+        !n_local || (n_tokens && !ids))
+        return TB_ERR_INVALID_ARG;
+    for (int64_t t = 0; t < n_tokens; ++t)
+        if (ids[t] < 0 || ids[t] >= vocab) return TB_ERR_INVALID_ARG;
+    int64_t my_vlo, my_vhi, my_tlo, my_thi;
+    tb_b200_partition(vocab, nranks, rank, &my_vlo, &my_vhi);
+    tb_b200_partition(n_tokens, nranks, rank, &my_tlo, &my_thi);
+    int64_t ns = 0, nl = 0;
+    // Rows this rank sends: destination-major, token order within a destination.
+    for (int d = 0; d < nranks; ++d) {
+        int64_t lo, hi;
+        tb_b200_partition(n_tokens, nranks, d, &lo, &hi);
+        int64_t c = 0;
+        for (int64_t t = lo; t < hi; ++t) {
+            if (owner_of(ids[t], vocab, nranks) != rank) continue;
+            if (d == rank) {
+                local_dst[nl] = (int32_t)(t - my_tlo);
+                local_src[nl] = (int32_t)(ids[t] - my_vlo);
+                ++nl;
+            } else {
+                send_rows[ns++] = (int32_t)(ids[t] - my_vlo);
+                ++c;
+            }
+        }
+        send_counts[d] = c;
+    }
+    // Rows this rank receives: source-major, token order within a source.
+    int64_t nr = 0;
+    for (int s = 0; s < nranks; ++s) {
+        int64_t c = 0;
+        if (s != rank) {
+            for (int64_t t = my_tlo; t < my_thi; ++t) {
+                if (owner_of(ids[t], vocab, nranks) == s) {
+                    recv_rows[nr++] = (int32_t)(t - my_tlo);
+                    ++c;
+                }
+            }
+        }
+        recv_counts[s] = c;
+    }
+    *n_local = nl;
+    return TB_OK;
+}
+
+int tb_b200_comm_unique_id(void* id_out) {
+    if (!id_out) return TB_ERR_INVALID_ARG;
+    static_assert(sizeof(ncclUniqueId) == TB_B200_COMM_ID_BYTES, "NCCL id size");
+    ncclUniqueId id;
+    ncclResult_t r = ncclGetUniqueId(&id);
+    if (r != ncclSuccess) {
+        nccl_error("ncclGetUniqueId", r);
+        return TB_ERR_DEVICE;
+    }
+    memcpy(id_out, &id, sizeof id);
+    return TB_OK;
+}
+
+int tb_b200_comm_init(int nranks, int rank, const void* unique_id, int device) {
+    if (nranks < 1 || rank < 0 || rank >= nranks || !unique_id) return TB_ERR_INVALID_ARG;
+    if (g_comm) return TB_ERR_INVALID_ARG;  // one communicator per process
+    TB_CUDA_TRY(cudaSetDevice(device));
+    ncclUniqueId id;
+    memcpy(&id, unique_id, sizeof id);
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    ncclResult_t r = ncclCommInitRankConfig(&g_comm, nranks, id, rank, &cfg);
+    if (r != ncclSuccess && r != ncclInProgress) {
+        nccl_error("ncclCommInitRankConfig", r);
+        g_comm = nullptr;
+        return TB_ERR_DEVICE;
+    }
+    const int rc = wait_comm("ncclCommInitRankConfig");
+    if (rc) return rc;
+    g_rank = rank;
+    g_nranks = nranks;
+    return TB_OK;
+}
+
+int tb_b200_comm_destroy(void) {
+    if (!g_comm) return TB_OK;
+    ncclResult_t r = ncclCommFinalize(g_comm);
+    int rc = TB_OK;
+    if (r != ncclSuccess && r != ncclInProgress) {
+        nccl_error("ncclCommFinalize", r);
+        rc = TB_ERR_DEVICE;
+    } else {
+        rc = wait_comm("ncclCommFinalize");
+    }
+    if (g_comm) ncclCommDestroy(g_comm);
+    g_comm = nullptr;
+    g_rank = 0;
+    g_nranks = 0;
+    return rc;
+}
+
+int tb_b200_comm_info(int* rank, int* nranks) {
+    if (!rank || !nranks) return TB_ERR_INVALID_ARG;
+    *rank = g_comm ? g_rank : 0;
+    *nranks = g_comm ? g_nranks : 0;
+    return TB_OK;
+}
+
+int tb_b200_embedding_sharded(int dtype, int64_t n_tokens, int64_t dim, int64_t vocab,
+                              const int32_t* ids, const void* table_shard, void* y_local,
+                              void* stream) {
+    if (!g_comm) {
+        tbh::set_error_text("tb_b200_embedding_sharded: no communicator (tb_b200_comm_init)");
+        return TB_ERR_INVALID_ARG;
+    }
+    if (dtype != TB_DTYPE_F32 && dtype != TB_DTYPE_BF16) return TB_ERR_UNSUPPORTED_DTYPE;
+    if (n_tokens < 0 || dim < 0 || vocab < g_nranks || n_tokens > INT32_MAX)
+        return TB_ERR_INVALID_SHAPE;
+    if (n_tokens && (!ids || !table_shard)) return TB_ERR_INVALID_ARG;
+    const int N = g_nranks, me = g_rank;
+    const int64_t row_bytes = dim * (dtype == TB_DTYPE_F32 ? 4 : 2);
+    int64_t tlo, thi;
+    tb_b200_partition(n_tokens, N, me, &tlo, &thi);
+    if (thi > tlo && !y_local) return TB_ERR_INVALID_ARG;
+
+    // Plan on the host; one int32 block [send | recv | local dst | local src].
+    std::vector<int64_t> sc(N), rcnt(N);
+    std::vector<int32_t> idx(4 * (size_t)(n_tokens + 1));
+    int32_t* send_rows = idx.data();
+    int32_t* recv_rows = send_rows + n_tokens + 1;
+    int32_t* ldst = recv_rows + n_tokens + 1;
+    int32_t* lsrc = ldst + n_tokens + 1;
+    int64_t nl = 0;
+    int rc = tb_b200_shard_plan(n_tokens, vocab, N, me, ids, sc.data(), rcnt.data(), send_rows,
+                                recv_rows, ldst, lsrc, &nl);
+    if (rc) return rc;
+    int64_t ns = 0, nr = 0;
+    for (int p = 0; p < N; ++p) {
+        ns += sc[p];
+        nr += rcnt[p];
+    }
+    // Compact: [send_rows(ns) | recv_rows(nr) | ldst(nl) | lsrc(nl)].
+    std::vector<int32_t> packed((size_t)(ns + nr + 2 * nl) + 1);
+    memcpy(packed.data(), send_rows, ns * sizeof(int32_t));
+    memcpy(packed.data() + ns, recv_rows, nr * sizeof(int32_t));
+    memcpy(packed.data() + ns + nr, ldst, nl * sizeof(int32_t));
+    memcpy(packed.data() + ns + nr + nl, lsrc, nl * sizeof(int32_t));
+
+    cudaStream_t s = tbh::stream_of(stream);
+    void* didx = nullptr;
+    void* sendbuf = nullptr;
+    void* recvbuf = nullptr;
+    auto release = [&]() {
+        if (didx) cudaFreeAsync(didx, s);
+        if (sendbuf) cudaFreeAsync(sendbuf, s);
+        if (recvbuf) cudaFreeAsync(recvbuf, s);
+    };
+    rc = tb_b200_stage_h2d(packed.data(), packed.size() * sizeof(int32_t), &didx, s);
+    if (rc) return rc;
+    const int32_t* d_send = static_cast<const int32_t*>(didx);
+    const int32_t* d_recv = d_send + ns;
+    const int32_t* d_ldst = d_recv + nr;
+    const int32_t* d_lsrc = d_ldst + nl;
+    cudaError_t e = cudaSuccess;
+    if (ns) e = cudaMallocAsync(&sendbuf, (size_t)(ns * row_bytes), s);
+    if (e == cudaSuccess && nr) e = cudaMallocAsync(&recvbuf, (size_t)(nr * row_bytes), s);
+    if (e != cudaSuccess) {
+        tbh::set_error("sharded embedding buffers", e);
+        release();
+        return TB_ERR_DEVICE;
+    }
+    // Own rows: local tokens straight to the output, others packed.
+    if ((rc = copy_rows(y_local, d_ldst, table_shard, d_lsrc, nl, row_bytes, s)) ||
+        (rc = copy_rows(sendbuf, nullptr, table_shard, d_send, ns, row_bytes, s))) {
+        release();
+        return rc;
+    }
+    // One grouped exchange with every peer.
+    ncclResult_t r = ncclGroupStart();
+    int64_t so = 0, ro = 0;
+    for (int p = 0; p < N && r == ncclSuccess; ++p) {
+        if (p == me) continue;
+        if (sc[p])
+            r = ncclSend(static_cast<char*>(sendbuf) + so * row_bytes, (size_t)(sc[p] * row_bytes),
+                         ncclUint8, p, g_comm, s);
+        if ((r == ncclSuccess || r == ncclInProgress) && rcnt[p])
+            r = ncclRecv(static_cast<char*>(recvbuf) + ro * row_bytes,
+                         (size_t)(rcnt[p] * row_bytes), ncclUint8, p, g_comm, s);
+        if (r == ncclInProgress) r = ncclSuccess;
+        so += sc[p];
+        ro += rcnt[p];
+    }
+    ncclResult_t r2 = ncclGroupEnd();
+    if (r == ncclSuccess && r2 != ncclSuccess && r2 != ncclInProgress) r = r2;
+    if (r != ncclSuccess) {
+        nccl_error("sharded embedding exchange", r);
+        release();
+        return TB_ERR_DEVICE;
+    }
+    rc = wait_comm("sharded embedding exchange");
+    if (rc) {
+        release();
+        return rc;
+    }
+    rc = copy_rows(y_local, d_recv, recvbuf, nullptr, nr, row_bytes, s);
+    release();
+    return rc;
+}
+
+}  // extern "C"

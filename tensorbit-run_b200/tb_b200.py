@@ -1,0 +1,368 @@
+"""Python binding of libtb_b200.so over its C ABI (include/tb_b200.h,
+include/tb_backend.h), for tests, benchmarks and Python hosts.
+
+Device buffers are torch CUDA tensors (torch provides allocation, streams
+and torch.distributed; the arithmetic is the library's sm_100a kernels).
+Every call goes through ctypes to the C entry point of the same name and
+raises ``TbError`` on a nonzero TbError code.  There is no fallback path:
+if the library is missing, ``lib()`` raises.
+
+Dtype codes follow TbDtype (F32 = 0, BF16 = 2).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libtb_b200.so")
+
+F32, F16, BF16, I32 = 0, 1, 2, 4
+DEVICE_CPU, DEVICE_CUDA = 0, 1
+FLAG_TOKEN_RANGE = 0x1
+
+# TbOpType values (include/tb_backend.h)
+OP = dict(SPARSE_LINEAR=0, DENSE_LINEAR=1, RMS_NORM=2, LAYER_NORM=3, GELU=4, SILU=5, SOFTMAX=6,
+          ATTENTION_QKV=7, SCALED_DOT_PRODUCT=8, ROPE=9, RESIDUAL_ADD=10, EMBEDDING=11, CONV2D=12,
+          RESIDUAL_RMS_NORM=13, SWIGLU=14, ARGMAX=15, ROPE_ROWS=16, LAYER_CHAIN=17, COUNT=18)
+
+ERRORS = {0: "ok", 7: "out of memory", 8: "invalid argument", 9: "invalid shape",
+          10: "unsupported dtype", 14: "backend not found", 16: "device error"}
+
+
+class TbError(RuntimeError):
+    def __init__(self, code: int, what: str, detail: str = ""):
+        self.code = code
+        msg = f"{what}: TbError {code} ({ERRORS.get(code, 'error')})"
+        super().__init__(msg + (f": {detail}" if detail else ""))
+
+
+class TbTensor(C.Structure):
+    """ABI image of TbTensor (include/tb_types.h)."""
+    _fields_ = [("data", C.c_void_p), ("shape", C.c_size_t * 8), ("rank", C.c_uint8),
+                ("dtype", C.c_int), ("device", C.c_int), ("owns_data", C.c_bool)]
+
+
+class LayerChain(C.Structure):
+    """ABI image of TbB200LayerChain (include/tb_b200.h)."""
+    _fields_ = [("dtype", C.c_int), ("rows", C.c_int64),
+                ("hidden", C.c_int64), ("x", C.c_void_p), ("residual", C.c_void_p),
+                ("norm_weight", C.c_void_p), ("h_out", C.c_void_p), ("y", C.c_void_p),
+                ("eps", C.c_float),
+                ("n_q_heads", C.c_int), ("n_kv_heads", C.c_int), ("head_dim", C.c_int),
+                ("q", C.c_void_p), ("k", C.c_void_p), ("positions", C.c_void_p),
+                ("theta", C.c_float), ("rope_table", C.c_void_p),
+                ("rope_table_positions", C.c_int),
+                ("intermediate", C.c_int64), ("gate", C.c_void_p), ("up", C.c_void_p),
+                ("act_out", C.c_void_p)]
+
+
+class RopeRowsParams(C.Structure):
+    _fields_ = [("positions", C.c_void_p), ("theta", C.c_float), ("head_dim", C.c_int),
+                ("max_position", C.c_int)]
+
+
+class LayerChainParams(C.Structure):
+    _fields_ = [("eps", C.c_float), ("positions", C.c_void_p), ("theta", C.c_float),
+                ("head_dim", C.c_int), ("max_position", C.c_int)]
+
+
+_lib = None
+vp, i64, i32, f32 = C.c_void_p, C.c_int64, C.c_int, C.c_float
+P = C.POINTER
+
+# name -> (restype, argtypes); every entry point of include/tb_b200.h and tb_backend.h.
+SIGNATURES = {
+    "tb_b200_version": (i32, []),
+    "tb_b200_last_error": (C.c_char_p, []),
+    "tb_b200_launch_count": (C.c_ulonglong, []),
+    "tb_b200_device_count": (i32, [P(i32)]),
+    "tb_b200_set_device": (i32, [i32]),
+    "tb_b200_get_device": (i32, [P(i32)]),
+    "tb_b200_malloc": (i32, [P(vp), C.c_size_t]),
+    "tb_b200_free": (i32, [vp]),
+    "tb_b200_malloc_host": (i32, [P(vp), C.c_size_t]),
+    "tb_b200_free_host": (i32, [vp]),
+    "tb_b200_memcpy_h2d": (i32, [vp, vp, C.c_size_t, vp]),
+    "tb_b200_memcpy_d2h": (i32, [vp, vp, C.c_size_t, vp]),
+    "tb_b200_memcpy_d2d": (i32, [vp, vp, C.c_size_t, vp]),
+    "tb_b200_memset": (i32, [vp, i32, C.c_size_t, vp]),
+    "tb_b200_set_stream": (i32, [vp]),
+    "tb_b200_get_stream": (vp, []),
+    "tb_b200_stream_sync": (i32, [vp]),
+    "tb_b200_sync": (i32, []),
+    "tb_b200_stage_h2d": (i32, [vp, C.c_size_t, P(vp), vp]),
+    "tb_b200_stage_release": (i32, [vp, vp]),
+    "tb_b200_is_device_ptr": (i32, [vp, P(i32)]),
+    "tb_b200_check_status": (i32, [vp, P(C.c_uint)]),
+    "tb_b200_residual_rms_norm": (i32, [i32, i64, i64, vp, vp, vp, vp, vp, f32, vp]),
+    "tb_b200_rms_norm": (i32, [i32, i64, i64, vp, vp, vp, f32, vp]),
+    "tb_b200_residual_add": (i32, [i32, i64, vp, vp, vp, vp]),
+    "tb_b200_silu": (i32, [i32, i64, vp, vp, vp]),
+    "tb_b200_gelu": (i32, [i32, i64, vp, vp, vp]),
+    "tb_b200_swiglu": (i32, [i32, i64, vp, vp, vp, vp]),
+    "tb_b200_rope_table": (i32, [f32, i32, i32, vp, vp]),
+    "tb_b200_rope_rows": (i32, [i32, i64, i32, i32, i32, vp, vp, vp, f32, vp, i32, vp]),
+    "tb_b200_rope": (i32, [i32, i32, i32, i32, vp, vp, i32, f32, vp]),
+    "tb_b200_softmax": (i32, [i32, i64, i64, vp, vp, vp, vp]),
+    "tb_b200_argmax": (i32, [i32, i64, i64, vp, vp, vp]),
+    "tb_b200_embedding": (i32, [i32, i64, i64, i64, vp, vp, vp, vp]),
+    "tb_b200_embedding_host_ids": (i32, [i32, i64, i64, i64, vp, vp, vp, vp]),
+    "tb_b200_layer_chain": (i32, [P(LayerChain), vp]),
+    "tb_b200_partition": (i32, [i64, i32, i32, P(i64), P(i64)]),
+    "tb_b200_shard_plan": (i32, [i64, i64, i32, i32, vp, vp, vp, vp, vp, vp, vp, P(i64)]),
+    "tb_b200_comm_unique_id": (i32, [vp]),
+    "tb_b200_comm_init": (i32, [i32, i32, vp, i32]),
+    "tb_b200_comm_destroy": (i32, []),
+    "tb_b200_comm_info": (i32, [P(i32), P(i32)]),
+    "tb_b200_embedding_sharded": (i32, [i32, i64, i64, i64, vp, vp, vp, vp]),
+    # registry (include/tb_backend.h)
+    "tb_backend_register": (i32, [vp]),
+    "tb_backend_register_device": (i32, [vp, i32]),
+    "tb_backend_get_best": (vp, [i32]),
+    "tb_backend_get_best_device": (vp, [i32, i32]),
+    "tb_backend_count": (i32, []),
+    "tb_backend_get": (vp, [i32]),
+    "tb_backend_reset": (None, []),
+    "tb_backend_b200_init": (i32, []),
+    "tb_dispatch_sparse_linear": (i32, [vp, vp, vp, vp, vp]),
+    "tb_dispatch_dense_linear": (i32, [vp, vp, vp, vp]),
+    "tb_dispatch_rms_norm": (i32, [vp, vp, vp, f32]),
+    "tb_dispatch_layer_norm": (i32, [vp, vp, vp, vp, f32]),
+    "tb_dispatch_gelu": (i32, [vp, vp]),
+    "tb_dispatch_silu": (i32, [vp, vp]),
+    "tb_dispatch_softmax": (i32, [vp, vp, vp]),
+    "tb_dispatch_attention_qkv": (i32, [vp] * 10 + [i32, i32, i32]),
+    "tb_dispatch_scaled_dot_product": (i32, [vp, vp, vp, vp, vp, f32, C.c_bool]),
+    "tb_dispatch_rope": (i32, [vp, vp, i32, f32, i32]),
+    "tb_dispatch_residual_add": (i32, [vp, vp, vp]),
+    "tb_dispatch_embedding": (i32, [vp, vp, i32, vp]),
+    "tb_dispatch_conv2d": (i32, [vp, vp, vp, vp, i32, i32]),
+    "tb_dispatch_residual_rms_norm": (i32, [vp, vp, vp, vp, vp, f32]),
+    "tb_dispatch_swiglu": (i32, [vp, vp, vp]),
+    "tb_dispatch_argmax": (i32, [vp, vp]),
+    "tb_dispatch_rope_rows": (i32, [vp, vp, vp, f32, i32, i32]),
+    "tb_dispatch_layer_chain": (i32, [vp] * 10 + [P(LayerChainParams)]),
+}
+
+
+def build() -> None:
+    """Compile lib/libtb_b200.so (nvcc, sm_100a)."""
+    out = subprocess.run(["make", "-C", HERE, "-j8"], capture_output=True, text=True)
+    if out.returncode != 0:
+        raise RuntimeError("libtb_b200 build failed:\n" + out.stdout[-4000:] + out.stderr[-4000:])
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is not built (run __graft_entry__.build())")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    s = lib().tb_b200_last_error()
+    return s.decode() if s else ""
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise TbError(rc, what, last_error())
+
+
+# ------------------------------------------------------------- torch glue
+def _torch():
+    import torch
+    return torch
+
+
+def dtype_code(t) -> int:
+    torch = _torch()
+    if t.dtype == torch.float32:
+        return F32
+    if t.dtype == torch.bfloat16:
+        return BF16
+    if t.dtype == torch.int32:
+        return I32
+    raise TypeError(f"unsupported dtype {t.dtype}")
+
+
+def ptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def cur_stream():
+    torch = _torch()
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _dev(*ts):
+    for t in ts:
+        if t is not None and not (t.is_cuda and t.is_contiguous()):
+            raise ValueError("expected contiguous CUDA tensors")
+
+
+def residual_rms_norm(x, residual, weight, eps, h_out=None, y=None, stream=None):
+    torch = _torch()
+    y = torch.empty_like(x) if y is None else y
+    _dev(x, residual, weight, h_out, y)
+    rows, cols = (x.numel() // x.shape[-1], x.shape[-1]) if x.dim() else (1, 1)
+    check(lib().tb_b200_residual_rms_norm(dtype_code(x), rows, cols, ptr(x), ptr(residual),
+                                          ptr(weight), ptr(h_out), ptr(y), eps,
+                                          stream or cur_stream()), "residual_rms_norm")
+    return h_out, y
+
+
+def rms_norm(x, weight, eps, y=None, stream=None):
+    torch = _torch()
+    y = torch.empty_like(x) if y is None else y
+    _dev(x, weight, y)
+    rows, cols = x.numel() // x.shape[-1], x.shape[-1]
+    check(lib().tb_b200_rms_norm(dtype_code(x), rows, cols, ptr(x), ptr(weight), ptr(y), eps,
+                                 stream or cur_stream()), "rms_norm")
+    return y
+
+
+def residual_add(x, residual, y=None, stream=None):
+    torch = _torch()
+    y = torch.empty_like(x) if y is None else y
+    _dev(x, residual, y)
+    check(lib().tb_b200_residual_add(dtype_code(x), x.numel(), ptr(x), ptr(residual), ptr(y),
+                                     stream or cur_stream()), "residual_add")
+    return y
+
+
+def silu(x, y=None, stream=None):
+    torch = _torch()
+    y = torch.empty_like(x) if y is None else y
+    _dev(x, y)
+    check(lib().tb_b200_silu(dtype_code(x), x.numel(), ptr(x), ptr(y), stream or cur_stream()),
+          "silu")
+    return y
+
+
+def gelu(x, y=None, stream=None):
+    torch = _torch()
+    y = torch.empty_like(x) if y is None else y
+    _dev(x, y)
+    check(lib().tb_b200_gelu(dtype_code(x), x.numel(), ptr(x), ptr(y), stream or cur_stream()),
+          "gelu")
+    return y
+
+
+def swiglu(gate, up, out=None, stream=None):
+    torch = _torch()
+    out = torch.empty_like(gate) if out is None else out
+    _dev(gate, up, out)
+    check(lib().tb_b200_swiglu(dtype_code(gate), gate.numel(), ptr(gate), ptr(up), ptr(out),
+                               stream or cur_stream()), "swiglu")
+    return out
+
+
+def rope_table(theta, head_dim, n_positions, device=None):
+    torch = _torch()
+    t = torch.empty((n_positions, head_dim), dtype=torch.float32,
+                    device=device or torch.cuda.current_device())
+    check(lib().tb_b200_rope_table(theta, head_dim, n_positions, ptr(t), cur_stream()),
+          "rope_table")
+    return t
+
+
+def rope_rows(q, k, positions, theta, table=None, stream=None):
+    """In place on q [R, Hq, d] and k [R, Hkv, d]; positions int32 [R] on the device."""
+    _dev(q, k, positions, table)
+    rows, hq, d = q.shape
+    hkv = k.shape[1]
+    check(lib().tb_b200_rope_rows(dtype_code(q), rows, hq, hkv, d, ptr(q), ptr(k), ptr(positions),
+                                  theta, ptr(table), 0 if table is None else table.shape[0],
+                                  stream or cur_stream()), "rope_rows")
+    return q, k
+
+
+def rope(q, k, position, theta, stream=None):
+    """Single token: q [Hq, d], k [Hkv, d], in place."""
+    _dev(q, k)
+    check(lib().tb_b200_rope(dtype_code(q), q.shape[0], k.shape[0], q.shape[-1], ptr(q), ptr(k),
+                             position, theta, stream or cur_stream()), "rope")
+    return q, k
+
+
+def softmax(x, mask=None, y=None, stream=None):
+    torch = _torch()
+    y = torch.empty_like(x) if y is None else y
+    _dev(x, mask, y)
+    rows, cols = x.numel() // x.shape[-1], x.shape[-1]
+    check(lib().tb_b200_softmax(dtype_code(x), rows, cols, ptr(x), ptr(mask), ptr(y),
+                                stream or cur_stream()), "softmax")
+    return y
+
+
+def argmax(x, out=None, stream=None):
+    torch = _torch()
+    rows, cols = x.numel() // x.shape[-1], x.shape[-1]
+    out = torch.empty(rows, dtype=torch.int32, device=x.device) if out is None else out
+    _dev(x, out)
+    check(lib().tb_b200_argmax(dtype_code(x), rows, cols, ptr(x), ptr(out),
+                               stream or cur_stream()), "argmax")
+    return out
+
+
+def embedding(ids, table, y=None, stream=None):
+    torch = _torch()
+    n = ids.numel()
+    y = torch.empty((n, table.shape[1]), dtype=table.dtype, device=table.device) if y is None else y
+    _dev(ids, table, y)
+    check(lib().tb_b200_embedding(dtype_code(table), n, table.shape[1], table.shape[0], ptr(ids),
+                                  ptr(table), ptr(y), stream or cur_stream()), "embedding")
+    return y
+
+
+def check_status(stream=None):
+    flags = C.c_uint(0)
+    rc = lib().tb_b200_check_status(stream or cur_stream(), C.byref(flags))
+    return rc, flags.value
+
+
+def layer_chain(chain: LayerChain, stream=None):
+    check(lib().tb_b200_layer_chain(C.byref(chain), stream or cur_stream()), "layer_chain")
+
+
+def make_chain(x=None, residual=None, norm_weight=None, h_out=None, y=None, eps=1e-5, q=None,
+               k=None, positions=None, theta=10000.0, table=None, gate=None, up=None,
+               act_out=None) -> LayerChain:
+    c = LayerChain()
+    ref = next(t for t in (x, q, gate) if t is not None)
+    c.dtype = dtype_code(ref)
+    c.rows = ref.shape[0]
+    if x is not None:
+        c.hidden, c.x, c.residual = x.shape[-1], ptr(x), ptr(residual)
+        c.norm_weight, c.h_out, c.y, c.eps = ptr(norm_weight), ptr(h_out), ptr(y), eps
+    if q is not None:
+        c.n_q_heads, c.n_kv_heads, c.head_dim = q.shape[1], k.shape[1], q.shape[2]
+        c.q, c.k, c.positions, c.theta = ptr(q), ptr(k), ptr(positions), theta
+        c.rope_table = ptr(table)
+        c.rope_table_positions = 0 if table is None else table.shape[0]
+    if gate is not None:
+        c.intermediate, c.gate, c.up, c.act_out = gate.shape[-1], ptr(gate), ptr(up), ptr(act_out)
+    return c
+
+
+def tensor(t, device=None) -> TbTensor:
+    """TbTensor view of a torch tensor (no copy, owns_data = false)."""
+    d = TbTensor()
+    d.data = t.data_ptr()
+    for i, s in enumerate(t.shape):
+        d.shape[i] = s
+    d.rank = t.dim()
+    d.dtype = dtype_code(t)
+    d.device = (DEVICE_CUDA if t.is_cuda else DEVICE_CPU) if device is None else device
+    d.owns_data = False
+    return d

@@ -1,0 +1,264 @@
+"""C-ABI and host logic of libtb_b200.so, on the CPU (no device work).
+
+- the library loads and exports every function declared in include/*.h;
+- ABI struct layouts (TbTensor as the engine lays it out, tensor.h:47-54);
+- the device-aware registry: routing by priority and by device, with the
+  reference's own CPU adapters (oracle/_ref) registered as "cpu", and the
+  engine's dispatch packing;
+- the b200 backend rejects host tensors before touching a device;
+- row partitioning and the sharded-embedding exchange plan.
+"""
+import ctypes as C
+import os
+import re
+
+import numpy as np
+import pytest
+
+import tb_b200 as T
+from oracle import oracle as O
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    names = set()
+    for h in ("tb_b200.h", "tb_backend.h", "tb_types.h"):
+        src = open(os.path.join(ROOT, "include", h)).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        for m in re.finditer(r"^[A-Za-z_][\w \*]*?\b(tb_\w+)\s*\(", src, flags=re.M):
+            names.add(m.group(1))
+    return names
+
+
+def exported_functions():
+    import subprocess
+    out = subprocess.run(["nm", "-D", "--defined-only", T.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    return {l.split()[-1] for l in out.splitlines() if " T " in l}
+
+
+def test_library_loads_and_reports_version():
+    assert T.lib().tb_b200_version() == 1
+
+
+def test_every_declared_function_is_exported():
+    decl = declared_functions()
+    assert len(decl) > 60
+    missing = decl - exported_functions()
+    assert not missing, f"declared but not exported: {sorted(missing)}"
+    # and the Python binding knows every one of them
+    assert decl <= set(T.SIGNATURES), sorted(decl - set(T.SIGNATURES))
+
+
+def test_abi_struct_layouts():
+    assert C.sizeof(T.TbTensor) == 88
+    assert T.TbTensor.rank.offset == 72 and T.TbTensor.dtype.offset == 76
+    assert T.TbTensor.device.offset == 80 and T.TbTensor.owns_data.offset == 84
+    assert C.sizeof(T.LayerChain) == 160
+
+
+def test_no_device_is_not_an_error():
+    n = C.c_int(-1)
+    assert T.lib().tb_b200_device_count(C.byref(n)) == 0
+    assert n.value >= 0
+
+
+def test_partition_rule():
+    lo, hi = C.c_int64(), C.c_int64()
+    for total, parts in [(16384, 8), (10, 3), (5, 8), (128256, 7)]:
+        spans = []
+        for p in range(parts):
+            assert T.lib().tb_b200_partition(total, parts, p, C.byref(lo), C.byref(hi)) == 0
+            spans.append((lo.value, hi.value))
+        assert spans[0][0] == 0 and spans[-1][1] == total
+        assert all(spans[i][1] == spans[i + 1][0] for i in range(parts - 1))
+        sizes = [h - l for l, h in spans]
+        assert max(sizes) - min(sizes) <= 1 and sizes == sorted(sizes, reverse=True)
+
+
+def shard_plan(ids, vocab, nranks, rank):
+    n = len(ids)
+    sc = np.zeros(nranks, np.int64)
+    rc = np.zeros(nranks, np.int64)
+    bufs = [np.zeros(n + 1, np.int32) for _ in range(4)]
+    nl = C.c_int64()
+    ids = np.ascontiguousarray(ids, np.int32)
+    code = T.lib().tb_b200_shard_plan(n, vocab, nranks, rank, ids.ctypes.data, sc.ctypes.data,
+                                      rc.ctypes.data, *[b.ctypes.data for b in bufs], C.byref(nl))
+    assert code == 0
+    s, r, ld, ls = bufs
+    return sc, rc, s[:sc.sum()], r[:rc.sum()], ld[:nl.value], ls[:nl.value]
+
+
+def bounds(total, parts):
+    base, extra = divmod(total, parts)
+    lo = [p * base + min(p, extra) for p in range(parts)]
+    return [(l, l + base + (1 if p < extra else 0)) for p, l in enumerate(lo)]
+
+
+@pytest.mark.parametrize("n,vocab,nranks", [(64, 100, 2), (1000, 128256, 8), (7, 10, 3),
+                                            (0, 16, 4)])
+def test_shard_plan_reassembles_the_gather(n, vocab, nranks):
+    """Simulate every rank's plan and exchange in numpy; the result must be the
+    full-table gather (tb_cpu_embedding_f32, src/ops/embedding.c:4-14)."""
+    rng = np.random.default_rng(n + vocab)
+    ids = rng.integers(0, vocab, n).astype(np.int32)
+    table = rng.standard_normal((vocab, 4), dtype=np.float32)
+    vb, tb = bounds(vocab, nranks), bounds(n, nranks)
+    plans = [shard_plan(ids, vocab, nranks, r) for r in range(nranks)]
+    for me in range(nranks):
+        tlo, thi = tb[me]
+        out = np.full((thi - tlo, 4), np.nan, np.float32)
+        sc, rc, send, recv, ld, ls = plans[me]
+        shard = table[vb[me][0]:vb[me][1]]
+        out[ld] = shard[ls]
+        ro = 0
+        for src in range(nranks):
+            if src == me:
+                continue
+            ssc, _, ssend, _, _, _ = plans[src]
+            off = int(ssc[:me].sum())
+            rows = table[vb[src][0]:vb[src][1]][ssend[off:off + ssc[me]]]
+            assert rc[src] == ssc[me]
+            out[recv[ro:ro + rc[src]]] = rows
+            ro += rc[src]
+        np.testing.assert_array_equal(out, O.embedding(ids[tlo:thi], table))
+
+
+def test_shard_plan_rejects_out_of_range_ids():
+    z = np.zeros(8, np.int64)
+    b = np.zeros(8, np.int32)
+    nl = C.c_int64()
+    ids = np.array([3, 100], np.int32)
+    assert T.lib().tb_b200_shard_plan(2, 100, 2, 0, ids.ctypes.data, z.ctypes.data, z.ctypes.data,
+                                      b.ctypes.data, b.ctypes.data, b.ctypes.data, b.ctypes.data,
+                                      C.byref(nl)) == 8
+
+
+# ------------------------------------------------------------- registry
+OpFn = C.CFUNCTYPE(C.c_int, C.c_void_p, C.POINTER(C.c_void_p), C.c_int, C.c_void_p)
+
+
+class Backend(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("priority", C.c_int), ("ops", C.c_void_p * T.OP["COUNT"])]
+
+
+_alive = []  # the registry copies the vtable, not the name string it points to
+
+
+def make_backend(name, prio, slots):
+    be = Backend()
+    _alive.append(be)
+    be.name = name.encode()
+    be.priority = prio
+    for op, fn in slots.items():
+        be.ops[T.OP[op]] = C.cast(fn, C.c_void_p)
+    return be
+
+
+@pytest.fixture
+def registry():
+    L = T.lib()
+    L.tb_backend_reset()
+    yield L
+    L.tb_backend_reset()
+
+
+def test_registry_priority_and_device_routing(registry):
+    calls = []
+    fns = {n: OpFn(lambda o, i, n_, p, n=n: calls.append(n) or 0) for n in ("lo", "hi", "dev")}
+    registry.tb_backend_register(C.byref(make_backend("lo", 0, {"GELU": fns["lo"]})))
+    registry.tb_backend_register(C.byref(make_backend("hi", 50, {"GELU": fns["hi"]})))
+    registry.tb_backend_register_device(C.byref(make_backend("dev", 200, {"GELU": fns["dev"]})),
+                                        T.DEVICE_CUDA)
+    assert registry.tb_backend_count() == 3
+    best = C.cast(registry.tb_backend_get_best(T.OP["GELU"]), C.POINTER(Backend)).contents
+    assert best.name == b"dev"  # the engine's get_best is device-blind
+    host = T.TbTensor(device=T.DEVICE_CPU)
+    dev = T.TbTensor(device=T.DEVICE_CUDA)
+    assert registry.tb_dispatch_gelu(C.byref(host), C.byref(host)) == 0
+    assert registry.tb_dispatch_gelu(C.byref(dev), C.byref(dev)) == 0
+    assert calls == ["hi", "dev"]
+    # no backend has a slot: TB_ERR_BACKEND_NOT_FOUND (src/backend/cpu/registry.c:93)
+    assert registry.tb_dispatch_silu(C.byref(host), C.byref(host)) == 14
+    assert not registry.tb_backend_get_best(T.OP["COUNT"])
+
+
+def test_registry_capacity_is_eight(registry):
+    be = make_backend("x", 1, {})
+    for _ in range(8):
+        assert registry.tb_backend_register(C.byref(be)) == 0
+    assert registry.tb_backend_register(C.byref(be)) == -1
+
+
+def test_dispatch_packs_inputs_like_the_engine(registry):
+    seen = {}
+
+    def fn(out, inputs, n, params):
+        seen["n"] = n
+        seen["inputs"] = [inputs[i] for i in range(n)]
+        seen["eps"] = C.cast(params, C.POINTER(C.c_float))[0]
+        return 0
+
+    cb = OpFn(fn)
+    registry.tb_backend_register(C.byref(make_backend("spy", 0, {"RMS_NORM": cb})))
+    y, x, w = T.TbTensor(), T.TbTensor(), T.TbTensor()
+    assert registry.tb_dispatch_rms_norm(C.byref(y), C.byref(x), C.byref(w), C.c_float(0.25)) == 0
+    assert seen["n"] == 2 and seen["eps"] == 0.25
+    assert seen["inputs"] == [C.addressof(x), C.addressof(w)]
+
+
+def test_b200_backend_registers_for_cuda_and_rejects_host_tensors(registry):
+    assert registry.tb_backend_b200_init() == 0
+    assert registry.tb_backend_b200_init() == 0  # idempotent
+    assert registry.tb_backend_count() == 1
+    be = C.cast(registry.tb_backend_get(0), C.POINTER(Backend)).contents
+    assert be.name == b"b200" and be.priority == 200
+    filled = {op for op, v in T.OP.items() if op != "COUNT" and be.ops[v]}
+    assert filled == {"RMS_NORM", "RESIDUAL_ADD", "GELU", "SILU", "SOFTMAX", "ROPE", "EMBEDDING",
+                      "RESIDUAL_RMS_NORM", "SWIGLU", "ARGMAX", "ROPE_ROWS", "LAYER_CHAIN"}
+    a = np.zeros(16, np.float32)
+    host = T.TbTensor(data=a.ctypes.data, rank=1, dtype=T.F32, device=T.DEVICE_CPU)
+    host.shape[0] = 16
+    # routing: nothing serves host tensors here
+    assert registry.tb_dispatch_silu(C.byref(host), C.byref(host)) == 14
+    # the op itself refuses host memory: no CPU fallback inside the backend
+    fn = C.cast(be.ops[T.OP["SILU"]], OpFn)
+    arr = (C.c_void_p * 1)(C.addressof(host))
+    assert fn(C.addressof(host), arr, 1, None) == 8
+
+
+def _ref_cpu_backend():
+    """The reference's CPU adapters (src/backend/cpu/*.c, built into
+    oracle/_ref) as a "cpu" TbBackend -- test infrastructure."""
+    ref = C.CDLL(O.REF_SO)
+    slots = {}
+    for op, sym in [("RMS_NORM", "tb_cpu_rms_norm_dispatch"), ("GELU", "tb_cpu_gelu_dispatch"),
+                    ("SILU", "tb_cpu_silu_dispatch"), ("SOFTMAX", "tb_cpu_softmax_dispatch"),
+                    ("ROPE", "tb_cpu_rope_dispatch"),
+                    ("RESIDUAL_ADD", "tb_cpu_residual_add_dispatch"),
+                    ("EMBEDDING", "tb_cpu_embedding_dispatch")]:
+        slots[op] = C.cast(getattr(ref, sym), OpFn)
+    return ref, slots
+
+
+@pytest.mark.skipif(not os.path.exists(O.REF_SO), reason="oracle/_ref not built here")
+def test_host_tensors_reach_the_reference_cpu_backend(registry):
+    ref, slots = _ref_cpu_backend()
+    registry.tb_backend_register(C.byref(make_backend("cpu", 0, slots)))
+    assert registry.tb_backend_b200_init() == 0
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal(256).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(256)).astype(np.float32)
+    y = np.zeros_like(x)
+
+    def tt(a):
+        t = T.TbTensor(data=a.ctypes.data, rank=1, dtype=T.F32, device=T.DEVICE_CPU)
+        t.shape[0] = a.size
+        return t
+
+    ty, tx, tw = tt(y), tt(x), tt(w)
+    assert registry.tb_dispatch_rms_norm(C.byref(ty), C.byref(tx), C.byref(tw),
+                                         C.c_float(1e-5)) == 0
+    np.testing.assert_array_equal(y, O.rms_norm_vec(x, w, 1e-5))

@@ -1,0 +1,187 @@
+"""The CPU oracle, pinned to the reference.
+
+1. The reference's own known-answer tests for this path, restated:
+   tests/test_norm.c:23-57 (RMSNorm) and tests/test_softmax.c:33-68.
+2. Golden checksums made by running the reference's unmodified kernels
+   (tests/golden/make_golden.py): the restatement must reproduce them
+   bit-for-bit.
+3. Where the reference build (oracle/_ref) is present, the restatement and
+   the reference agree bit-for-bit on fresh seeded inputs, for f32 and bf16.
+4. Edge semantics of argmax (src/main.cpp:79-89) and softmax.
+"""
+import hashlib
+import importlib.util
+import json
+import math
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _golden_module():
+    spec = importlib.util.spec_from_file_location(
+        "make_golden", os.path.join(HERE, "golden", "make_golden.py"))
+    m = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(m)
+    return m
+
+
+# ---------------------------------------------------------------- 1. KATs
+def test_ref_kat_rms_norm_unit_weight():
+    # tests/test_norm.c:23-40
+    x = np.array([1, 2, 3, 4], np.float32)
+    y = O.rms_norm_vec(x, np.ones(4, np.float32), 1e-6)
+    rms = math.sqrt((1 + 4 + 9 + 16) / 4.0 + 1e-6)
+    np.testing.assert_allclose(y, x / rms, atol=1e-4)
+
+
+def test_ref_kat_rms_norm_weighted():
+    # tests/test_norm.c:43-57
+    y = O.rms_norm_vec(np.full(4, 2, np.float32), np.array([0.5, 1, 1.5, 2], np.float32), 0.0)
+    np.testing.assert_allclose(y, [0.5, 1.0, 1.5, 2.0], atol=1e-4)
+
+
+def test_ref_kat_softmax_basic():
+    # tests/test_softmax.c:33-44
+    y = O.softmax_vec(np.array([1, 2, 3], np.float32))
+    assert abs(float(y.sum()) - 1.0) <= 1e-4
+    assert y[2] > y[1] > y[0]
+
+
+def test_ref_kat_softmax_uniform():
+    # tests/test_softmax.c:47-56
+    np.testing.assert_allclose(O.softmax_vec(np.full(4, 5, np.float32)), 0.25, atol=1e-4)
+
+
+def test_ref_kat_softmax_mask():
+    # tests/test_softmax.c:59-68
+    y = O.softmax_vec(np.array([1, 2, 3], np.float32), np.array([0, 0, -100], np.float32))
+    assert abs(float(y[2])) <= 1e-3
+    assert y[1] > y[0]
+
+
+# ------------------------------------------------------------ 2. golden
+def test_golden_checksums_reproduced_by_port():
+    meta = json.load(open(os.path.join(HERE, "golden", "golden.json")))
+    mg = _golden_module()
+    names = set()
+    for name, fn in mg.cases():
+        res = fn(O.PORT)
+        for k, v in res.items():
+            want = meta["cases"][name][k]
+            assert list(v.shape) == want["shape"], (name, k)
+            got = hashlib.sha256(np.ascontiguousarray(v).tobytes()).hexdigest()
+            assert got == want["sha256"], f"{name}.{k}: port differs from the reference"
+        names.add(name)
+    assert names == set(meta["cases"]), "golden cases and generator out of sync"
+
+
+def test_golden_rows_match_checksummed_outputs():
+    rows = np.load(os.path.join(HERE, "golden", "golden_rows.npz"))
+    mg = _golden_module()
+    for name, fn in mg.cases():
+        for k, v in fn(O.PORT).items():
+            flat = v.reshape(v.shape[0], -1) if v.ndim > 1 else v.reshape(1, -1)
+            np.testing.assert_array_equal(rows[f"{name}.{k}"], flat[[0, -1], :1024])
+
+
+# ------------------------------------------------- 3. port vs reference
+needs_ref = pytest.mark.skipif(not O.ref_available(), reason="oracle/_ref not built here")
+
+
+def _same(a, b):
+    return np.array_equal(np.asarray(a).view(np.uint8), np.asarray(b).view(np.uint8))
+
+
+@needs_ref
+@pytest.mark.parametrize("rows,cols", [(7, 4096), (3, 16384), (5, 100), (2, 1), (1, 8192)])
+@pytest.mark.parametrize("bf16", [False, True])
+def test_port_equals_reference_rowops(rows, cols, bf16):
+    rng = np.random.default_rng(rows * 1000 + cols)
+    cv = O.f32_to_bf16 if bf16 else (lambda a: a)
+    x = cv(rng.standard_normal((rows, cols), dtype=np.float32))
+    r = cv(rng.standard_normal((rows, cols), dtype=np.float32))
+    w = cv((1 + 0.1 * rng.standard_normal(cols)).astype(np.float32))
+    for a, b in zip(O.residual_rms_norm(x, r, w, 1e-5, O.PORT),
+                    O.residual_rms_norm(x, r, w, 1e-5, O.REF)):
+        assert _same(a, b)
+    assert _same(O.rms_norm(x, w, 1e-6, O.PORT), O.rms_norm(x, w, 1e-6, O.REF))
+    assert _same(O.gelu(x, O.PORT), O.gelu(x, O.REF))
+    assert _same(O.silu(x, O.PORT), O.silu(x, O.REF))
+    assert _same(O.swiglu(x, r, O.PORT), O.swiglu(x, r, O.REF))
+    assert _same(O.residual_add(x, r, O.PORT), O.residual_add(x, r, O.REF))
+    xs = cv(3 * rng.standard_normal((rows, cols), dtype=np.float32))
+    assert _same(O.softmax(xs, None, O.PORT), O.softmax(xs, None, O.REF))
+    assert _same(O.softmax(xs, r, O.PORT), O.softmax(xs, r, O.REF))
+
+
+@needs_ref
+@pytest.mark.parametrize("hq,hkv,d,theta", [(4, 4, 64, 1e4), (32, 32, 128, 1e4),
+                                            (64, 8, 128, 5e5), (3, 1, 6, 1e4)])
+def test_port_equals_reference_rope(hq, hkv, d, theta):
+    rng = np.random.default_rng(hq * d)
+    q = rng.standard_normal((9, hq, d), dtype=np.float32)
+    k = rng.standard_normal((9, hkv, d), dtype=np.float32)
+    pos = rng.integers(0, 20000, 9).astype(np.int32)
+    for a, b in zip(O.rope(q, k, pos, theta, O.PORT), O.rope(q, k, pos, theta, O.REF)):
+        assert _same(a, b)
+
+
+@needs_ref
+def test_port_equals_reference_embedding():
+    rng = np.random.default_rng(5)
+    t = rng.standard_normal((1000, 48), dtype=np.float32)
+    ids = rng.integers(0, 1000, 333).astype(np.int32)
+    assert _same(O.embedding(ids, t, O.PORT), O.embedding(ids, t, O.REF))
+
+
+def test_threaded_rows_equal_single_thread():
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((37, 512), dtype=np.float32)
+    assert _same(O.softmax(x, None, O.PORT, 1), O.softmax(x, None, O.PORT, 4))
+    h1, y1 = O.residual_rms_norm(x, x, None, 1e-5, O.PORT, 1)
+    h4, y4 = O.residual_rms_norm(x, x, None, 1e-5, O.PORT, 4)
+    assert _same(y1, y4) and _same(h1, h4)
+
+
+# ------------------------------------------------------- 4. edge cases
+def test_argmax_semantics():
+    nan, inf = np.float32("nan"), np.float32("inf")
+    cases = [
+        ([1, 3, 3, 2], 1),            # first maximum wins
+        ([nan, 5, 7], 0),             # NaN at index 0 is never beaten
+        ([1, nan, 0.5], 0),           # NaN never wins
+        ([-inf, -inf], 0),            # nothing exceeds -inf
+        ([-inf, nan, -inf], 0),
+        ([-0.0, 0.0, -1], 0),         # +0 is not greater than -0
+        ([-5, -inf, inf, inf], 2),
+        ([2.0], 0),
+    ]
+    for vals, want in cases:
+        got = O.argmax(np.array([vals], np.float32))[0]
+        assert got == want, (vals, got)
+
+
+def test_softmax_degenerate_rows_keep_exponentials():
+    # softmax.c:24-29: a NaN or zero sum leaves y = exp(v - max) unnormalised.
+    nan = np.float32("nan")
+    y = O.softmax(np.array([[0.0, nan, 1.0]], np.float32))
+    assert np.isnan(y[0, 1]) and y[0, 2] == 1.0 and y[0, 0] == np.float32(math.exp(-1.0))
+    y = O.softmax(np.full((1, 3), -np.inf, np.float32))
+    assert np.isnan(y).all()
+
+
+def test_bf16_round_to_nearest_even():
+    vals = np.array([1.0, 1.00390625, 1.01171875, 1.005859375, -2.5, 3.0e38, 1e-40],
+                    np.float32)
+    b = O.f32_to_bf16(vals)
+    back = O.bf16_to_f32(b)
+    # ties go to even: 1 + 2^-8 -> 1.0, 1 + 3*2^-8 -> 1 + 2^-6
+    assert back[1] == 1.0 and back[2] == np.float32(1.015625)
+    assert back[0] == 1.0 and back[4] == -2.5
+    assert np.isnan(O.bf16_to_f32(O.f32_to_bf16(np.array([np.nan], np.float32))))[0]
