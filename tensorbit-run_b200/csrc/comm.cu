@@ -18,8 +18,16 @@
 // wait on it is bounded (TB_B200_COMM_TIMEOUT_S seconds, default 120): a
 // rank that never arrives makes the others return TB_ERR_DEVICE after
 // aborting the communicator, instead of hanging.
+//
+// NCCL is not linked: its entry points are resolved with dlopen/dlsym on
+// first use.  A process that also loads PyTorch then shares torch's NCCL
+// (dlopen of the soname returns the library already loaded), instead of a
+// second libnccl.so.2 claiming the soname before torch's and breaking it.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
 #include <nccl.h>
+
+#include <mutex>
 
 #include <chrono>
 #include <stdio.h>
@@ -32,6 +40,52 @@
 
 namespace {
 
+struct NcclApi {
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*);
+    ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*);
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*);
+    ncclResult_t (*CommAbort)(ncclComm_t);
+    ncclResult_t (*CommFinalize)(ncclComm_t);
+    ncclResult_t (*CommDestroy)(ncclComm_t);
+    const char* (*GetErrorString)(ncclResult_t);
+    ncclResult_t (*GroupStart)();
+    ncclResult_t (*GroupEnd)();
+    ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
+    ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
+};
+
+NcclApi g_nccl;
+bool g_nccl_ok = false;
+std::once_flag g_nccl_once;
+
+// Resolve NCCL once; false (with the error text set) if it is unavailable.
+bool nccl_api() {
+    std::call_once(g_nccl_once, [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return;
+        bool ok = true;
+        auto sym = [&](auto& fp, const char* name) {
+            *reinterpret_cast<void**>(&fp) = dlsym(h, name);
+            ok = ok && fp != nullptr;
+        };
+        sym(g_nccl.GetUniqueId, "ncclGetUniqueId");
+        sym(g_nccl.CommInitRankConfig, "ncclCommInitRankConfig");
+        sym(g_nccl.CommGetAsyncError, "ncclCommGetAsyncError");
+        sym(g_nccl.CommAbort, "ncclCommAbort");
+        sym(g_nccl.CommFinalize, "ncclCommFinalize");
+        sym(g_nccl.CommDestroy, "ncclCommDestroy");
+        sym(g_nccl.GetErrorString, "ncclGetErrorString");
+        sym(g_nccl.GroupStart, "ncclGroupStart");
+        sym(g_nccl.GroupEnd, "ncclGroupEnd");
+        sym(g_nccl.Send, "ncclSend");
+        sym(g_nccl.Recv, "ncclRecv");
+        g_nccl_ok = ok;
+    });
+    if (!g_nccl_ok) tbh::set_error_text("NCCL (libnccl.so.2) could not be loaded");
+    return g_nccl_ok;
+}
+
 ncclComm_t g_comm = nullptr;
 int g_rank = 0, g_nranks = 0;
 
@@ -43,7 +97,7 @@ double timeout_s() {
 
 void nccl_error(const char* what, ncclResult_t r) {
     char buf[384];
-    snprintf(buf, sizeof buf, "%s: %s", what, ncclGetErrorString(r));
+    snprintf(buf, sizeof buf, "%s: %s", what, g_nccl.GetErrorString(r));
     tbh::set_error_text(buf);
 }
 
@@ -52,7 +106,7 @@ int wait_comm(const char* what) {
     const auto t0 = std::chrono::steady_clock::now();
     for (;;) {
         ncclResult_t st = ncclSuccess;
-        ncclResult_t r = ncclCommGetAsyncError(g_comm, &st);
+        ncclResult_t r = g_nccl.CommGetAsyncError(g_comm, &st);
         if (r != ncclSuccess) {
             nccl_error(what, r);
             return TB_ERR_DEVICE;
@@ -60,7 +114,7 @@ int wait_comm(const char* what) {
         if (st == ncclSuccess) return TB_OK;
         if (st != ncclInProgress) {
             nccl_error(what, st);
-            ncclCommAbort(g_comm);
+            g_nccl.CommAbort(g_comm);
             g_comm = nullptr;
             return TB_ERR_DEVICE;
         }
@@ -68,7 +122,7 @@ int wait_comm(const char* what) {
             std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
         if (el > timeout_s()) {
             tbh::set_error_text("NCCL call timed out; communicator aborted");
-            ncclCommAbort(g_comm);
+            g_nccl.CommAbort(g_comm);
             g_comm = nullptr;
             return TB_ERR_DEVICE;
         }
@@ -175,9 +229,10 @@ int tb_b200_shard_plan(int64_t n_tokens, int64_t vocab, int nranks, int rank,
 
 int tb_b200_comm_unique_id(void* id_out) {
     if (!id_out) return TB_ERR_INVALID_ARG;
+    if (!nccl_api()) return TB_ERR_DEVICE;
     static_assert(sizeof(ncclUniqueId) == TB_B200_COMM_ID_BYTES, "NCCL id size");
     ncclUniqueId id;
-    ncclResult_t r = ncclGetUniqueId(&id);
+    ncclResult_t r = g_nccl.GetUniqueId(&id);
     if (r != ncclSuccess) {
         nccl_error("ncclGetUniqueId", r);
         return TB_ERR_DEVICE;
@@ -189,12 +244,13 @@ int tb_b200_comm_unique_id(void* id_out) {
 int tb_b200_comm_init(int nranks, int rank, const void* unique_id, int device) {
     if (nranks < 1 || rank < 0 || rank >= nranks || !unique_id) return TB_ERR_INVALID_ARG;
     if (g_comm) return TB_ERR_INVALID_ARG;  // one communicator per process
+    if (!nccl_api()) return TB_ERR_DEVICE;
     TB_CUDA_TRY(cudaSetDevice(device));
     ncclUniqueId id;
     memcpy(&id, unique_id, sizeof id);
     ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
     cfg.blocking = 0;
-    ncclResult_t r = ncclCommInitRankConfig(&g_comm, nranks, id, rank, &cfg);
+    ncclResult_t r = g_nccl.CommInitRankConfig(&g_comm, nranks, id, rank, &cfg);
     if (r != ncclSuccess && r != ncclInProgress) {
         nccl_error("ncclCommInitRankConfig", r);
         g_comm = nullptr;
@@ -209,7 +265,7 @@ int tb_b200_comm_init(int nranks, int rank, const void* unique_id, int device) {
 
 int tb_b200_comm_destroy(void) {
     if (!g_comm) return TB_OK;
-    ncclResult_t r = ncclCommFinalize(g_comm);
+    ncclResult_t r = g_nccl.CommFinalize(g_comm);
     int rc = TB_OK;
     if (r != ncclSuccess && r != ncclInProgress) {
         nccl_error("ncclCommFinalize", r);
@@ -217,7 +273,7 @@ int tb_b200_comm_destroy(void) {
     } else {
         rc = wait_comm("ncclCommFinalize");
     }
-    if (g_comm) ncclCommDestroy(g_comm);
+    if (g_comm) g_nccl.CommDestroy(g_comm);
     g_comm = nullptr;
     g_rank = 0;
     g_nranks = 0;
@@ -301,21 +357,21 @@ int tb_b200_embedding_sharded(int dtype, int64_t n_tokens, int64_t dim, int64_t 
         return rc;
     }
     // One grouped exchange with every peer.
-    ncclResult_t r = ncclGroupStart();
+    ncclResult_t r = g_nccl.GroupStart();
     int64_t so = 0, ro = 0;
     for (int p = 0; p < N && r == ncclSuccess; ++p) {
         if (p == me) continue;
         if (sc[p])
-            r = ncclSend(static_cast<char*>(sendbuf) + so * row_bytes, (size_t)(sc[p] * row_bytes),
+            r = g_nccl.Send(static_cast<char*>(sendbuf) + so * row_bytes, (size_t)(sc[p] * row_bytes),
                          ncclUint8, p, g_comm, s);
         if ((r == ncclSuccess || r == ncclInProgress) && rcnt[p])
-            r = ncclRecv(static_cast<char*>(recvbuf) + ro * row_bytes,
+            r = g_nccl.Recv(static_cast<char*>(recvbuf) + ro * row_bytes,
                          (size_t)(rcnt[p] * row_bytes), ncclUint8, p, g_comm, s);
         if (r == ncclInProgress) r = ncclSuccess;
         so += sc[p];
         ro += rcnt[p];
     }
-    ncclResult_t r2 = ncclGroupEnd();
+    ncclResult_t r2 = g_nccl.GroupEnd();
     if (r == ncclSuccess && r2 != ncclSuccess && r2 != ncclInProgress) r = r2;
     if (r != ncclSuccess) {
         nccl_error("sharded embedding exchange", r);

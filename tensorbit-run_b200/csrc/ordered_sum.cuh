@@ -36,6 +36,7 @@ struct RunSum {
     float s;         // the running sum, bit-identical to the sequential one
     uint32_t S;      // s / u (fast mode)
     float u, inv_u;  // grid spacing of s's binade and its inverse
+    int b;           // the binade: s in [2^b, 2^(b+1)) (b = -126 below that)
     bool fast;       // s >= 2^-100: integer-grid mode
     bool nan;        // sum is NaN; nothing more to do
 
@@ -43,9 +44,10 @@ struct RunSum {
         s = v;
         nan = (v != v);
         fast = false;
+        b = -127;
         if (nan) return;
         const int ex = (int)(__float_as_uint(v) >> 23) - 127;  // v >= 0
-        const int b = ex < -126 ? -126 : ex;
+        b = ex < -126 ? -126 : ex;
         if (b >= -100) {
             fast = true;
             u = __uint_as_float((uint32_t)(b - 23 + 127) << 23);
@@ -55,16 +57,42 @@ struct RunSum {
     }
 };
 
+// Binade of a positive estimate for the integer-grid mode, or kNoBinade
+// when the estimate is below 2^-100, zero, or NaN.
+constexpr int kNoBinade = -128;
+__device__ __forceinline__ int binade_of(float v) {
+    if (!(v >= 7.8886090522101181e-31f)) return kNoBinade;  // 2^-100
+    return (int)(__float_as_uint(v) >> 23) - 127;
+}
+
+// d = rne(e / u) for the grid 2^(b-23), capped at 2^25 (already an event);
+// sets *event for an exact tie (parity-dependent rounding) or a NaN term.
+__device__ __forceinline__ uint32_t grid_units(float e, float inv_u, bool* event) {
+    const float t = __fmul_rn(e, inv_u);
+    if (!(t < 33554432.0f)) {
+        if (t != t) *event = true;
+        return 1u << 25;
+    }
+    if (__fsub_rn(t, floorf(t)) == 0.5f) *event = true;
+    return __float2uint_rn(t);
+}
+
+__device__ __forceinline__ float inv_grid(int b) {
+    return __uint_as_float((uint32_t)(23 - b + 127) << 23);
+}
+
 // Consume the first `nvalid` terms of a warp tile, in order: lane l holds
 // terms l*K .. l*K+K-1 in e[].  All 32 lanes call it with identical `st`
 // and leave with identical `st`.
+// Terms before `first` are taken as already consumed.
 template <int K>
-__device__ __forceinline__ void ordered_sum_tile(RunSum& st, const float (&e)[K], int nvalid) {
+__device__ __forceinline__ void ordered_sum_tile(RunSum& st, const float (&e)[K], int nvalid,
+                                                 int first = 0) {
     constexpr uint32_t kLimit = 1u << 24;  // S reaching this leaves the binade
     constexpr uint32_t kCap = 1u << 25;    // any d >= 2^24 is an event anyway
     constexpr uint32_t kSat = 1u << 30;    // saturation of partial sums
     const int lane = threadIdx.x & 31;
-    int pos = 0;  // terms of this tile already consumed
+    int pos = first;  // terms of this tile already consumed
     while (pos < nvalid && !st.nan) {
         if (!st.fast) {
             // Tiny sum: exact one-by-one additions, in sequence order.

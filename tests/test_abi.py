@@ -262,3 +262,14 @@ def test_host_tensors_reach_the_reference_cpu_backend(registry):
     assert registry.tb_dispatch_rms_norm(C.byref(ty), C.byref(tx), C.byref(tw),
                                          C.c_float(1e-5)) == 0
     np.testing.assert_array_equal(y, O.rms_norm_vec(x, w, 1e-5))
+
+
+def test_library_before_torch_keeps_torch_importable():
+    """The library resolves NCCL at run time: loading it before torch must not
+    claim the libnccl.so.2 soname with a different NCCL than torch's."""
+    import subprocess
+    import sys
+    code = ("import sys; sys.path.insert(0, %r); import tb_b200; tb_b200.lib(); import torch; "
+            "print(torch.__version__)" % os.path.join(ROOT, "tensorbit-run_b200"))
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr[-2000:]
