@@ -166,6 +166,24 @@ int tb_b200_embedding_host_ids(int dtype, int64_t n_tokens, int64_t dim, int64_t
                                const int32_t* ids_host, const void* table, void* y,
                                void* stream);
 
+/* The same host-ids gather with no allocation.  For callers that cannot
+ * allocate device memory where they make this call -- an engine whose
+ * device memory is owned and budgeted by another allocator, or a per-token
+ * decode step that must not take the synchronisation cudaMalloc implies.
+ * Its scratch (the staged ids and the gather's status word) is one
+ * statically sized device array inside the library, held by every GPU that
+ * loads it until the process exits.  At most TB_B200_STATIC_MAX_TOKENS ids
+ * per call; more returns TB_ERR_INVALID_SHAPE with nothing queued.  The
+ * first call on a device looks up the array's device address once (make it
+ * before any stream capture on that device).  All calls share the array and
+ * each starts by clearing the status word: calls whose work can overlap on
+ * the GPU (different streams, no ordering between them) race on it.  No
+ * counterpart in the reference (its embedding is a host memcpy). */
+#define TB_B200_STATIC_MAX_TOKENS 65536
+int tb_b200_embedding_host_ids_static(int dtype, int64_t n_tokens, int64_t dim, int64_t vocab,
+                                      const int32_t* ids_host, const void* table, void* y,
+                                      void* stream);
+
 /* One launch that runs a transformer layer's three row-op groups on their
  * own tensors: residual+RMSNorm [rows, hidden]; RoPE on q/k at per-row
  * positions; SwiGLU over [rows, intermediate] (the per-layer row ops of

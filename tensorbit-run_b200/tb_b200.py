@@ -109,6 +109,7 @@ SIGNATURES = {
     "tb_b200_argmax": (i32, [i32, i64, i64, vp, vp, vp]),
     "tb_b200_embedding": (i32, [i32, i64, i64, i64, vp, vp, vp, vp]),
     "tb_b200_embedding_host_ids": (i32, [i32, i64, i64, i64, vp, vp, vp, vp]),
+    "tb_b200_embedding_host_ids_static": (i32, [i32, i64, i64, i64, vp, vp, vp, vp]),
     "tb_b200_layer_chain": (i32, [P(LayerChain), vp]),
     "tb_b200_partition": (i32, [i64, i32, i32, P(i64), P(i64)]),
     "tb_b200_shard_plan": (i32, [i64, i64, i32, i32, vp, vp, vp, vp, vp, vp, vp, P(i64)]),
