@@ -32,30 +32,25 @@ template <typename T, int VEC, int ITEMS>
 __device__ __forceinline__ void res_rms_body(const T* x, const T* res, const T* w, T* h_out, T* y,
                                              int64_t rows, int cols, float eps, int G,
                                              int64_t vblock, float* red) {
+    // Raw 16-byte vectors are kept (half the registers of f32 copies for
+    // bf16) and h = x + residual is recomputed after the reduction: the same
+    // single f32 add, so the same bits.
+    using Raw = typename Elt<T>::template Raw<VEC>;
     const int lane = threadIdx.x & (G - 1);
     const int64_t row = vblock * (blockDim.x / G) + threadIdx.x / G;
     const bool active = row < rows;
     const int nvec = cols / VEC;
     const int64_t base = row * (int64_t)cols;
 
-    float v[ITEMS][VEC];
+    Raw rx[ITEMS], rr[ITEMS];
     if (active) {
 #pragma unroll
         for (int i = 0; i < ITEMS; ++i) {
             const int vi = lane + i * G;
-            if (vi < nvec) load_vec_stream<T, VEC>(x + base + (int64_t)vi * VEC, v[i]);
-        }
-        if (res != nullptr) {
-            float r[ITEMS][VEC];
-#pragma unroll
-            for (int i = 0; i < ITEMS; ++i) {
-                const int vi = lane + i * G;
-                if (vi < nvec) load_vec_stream<T, VEC>(res + base + (int64_t)vi * VEC, r[i]);
+            if (vi < nvec) {
+                rx[i] = Elt<T>::template load_raw<VEC>(x + base + (int64_t)vi * VEC);
+                if (res != nullptr) rr[i] = Elt<T>::template load_raw<VEC>(res + base + (int64_t)vi * VEC);
             }
-#pragma unroll
-            for (int i = 0; i < ITEMS; ++i)
-#pragma unroll
-                for (int j = 0; j < VEC; ++j) v[i][j] = __fadd_rn(v[i][j], r[i][j]);
         }
     }
     float ss = 0.0f;
@@ -63,8 +58,16 @@ __device__ __forceinline__ void res_rms_body(const T* x, const T* res, const T* 
 #pragma unroll
         for (int i = 0; i < ITEMS; ++i) {
             if (lane + i * G < nvec) {
+                float h[VEC];
+                Elt<T>::template widen<VEC>(rx[i], h);
+                if (res != nullptr) {
+                    float r[VEC];
+                    Elt<T>::template widen<VEC>(rr[i], r);
 #pragma unroll
-                for (int j = 0; j < VEC; ++j) ss = __fmaf_rn(v[i][j], v[i][j], ss);
+                    for (int j = 0; j < VEC; ++j) h[j] = __fadd_rn(h[j], r[j]);
+                }
+#pragma unroll
+                for (int j = 0; j < VEC; ++j) ss = __fmaf_rn(h[j], h[j], ss);
             }
         }
     }
@@ -76,16 +79,24 @@ __device__ __forceinline__ void res_rms_body(const T* x, const T* res, const T* 
         const int vi = lane + i * G;
         if (vi >= nvec) continue;
         const int64_t off = base + (int64_t)vi * VEC;
-        if (h_out != nullptr) store_vec<T, VEC>(h_out + off, v[i]);
+        float h[VEC];
+        Elt<T>::template widen<VEC>(rx[i], h);
+        if (res != nullptr) {
+            float r[VEC];
+            Elt<T>::template widen<VEC>(rr[i], r);
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) h[j] = __fadd_rn(h[j], r[j]);
+        }
+        if (h_out != nullptr) store_vec<T, VEC>(h_out + off, h);
         float o[VEC];
         if (w != nullptr) {
             float g[VEC];
             load_vec<T, VEC>(w + (int64_t)vi * VEC, g);
 #pragma unroll
-            for (int j = 0; j < VEC; ++j) o[j] = __fmul_rn(__fmul_rn(v[i][j], scale), g[j]);
+            for (int j = 0; j < VEC; ++j) o[j] = __fmul_rn(__fmul_rn(h[j], scale), g[j]);
         } else {
 #pragma unroll
-            for (int j = 0; j < VEC; ++j) o[j] = __fmul_rn(v[i][j], scale);
+            for (int j = 0; j < VEC; ++j) o[j] = __fmul_rn(h[j], scale);
         }
         store_vec<T, VEC>(y + off, o);
     }
@@ -128,6 +139,23 @@ __device__ __forceinline__ void rope_body(T* q, T* k, const int32_t* positions, 
     if (h0 >= hstep) return;
     const int nh = hq + hkv;
 
+    T* qrow = q + row * (int64_t)hq * d;
+    T* krow = k + row * (int64_t)hkv * d;
+    // The head loads do not depend on the position: issue the first batch
+    // before the position -> table chain.  Heads stay in their raw 16-byte
+    // form until they are rotated (few registers, more CTAs per SM).
+    using Raw = typename Elt<T>::template Raw<VEC>;
+    Raw v[UNROLL];
+    T* ptr[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+        const int h = h0 + u * hstep;
+        ptr[u] = nullptr;
+        if (h < nh) {
+            ptr[u] = (h < hq ? qrow + (int64_t)h * d : krow + (int64_t)(h - hq) * d) + j * VEC;
+            v[u] = Elt<T>::template load_raw_keep<VEC>(ptr[u]);
+        }
+    }
     float c[P], s[P];
     if constexpr (MODE == kRopeConst) {
 #pragma unroll
@@ -154,26 +182,26 @@ __device__ __forceinline__ void rope_body(T* q, T* k, const int32_t* positions, 
         }
     }
 
-    T* qrow = q + row * (int64_t)hq * d;
-    T* krow = k + row * (int64_t)hkv * d;
     for (int hb = h0; hb < nh; hb += UNROLL * hstep) {
-        float v[UNROLL][VEC];
-        T* ptr[UNROLL];
+        if (hb != h0) {
 #pragma unroll
-        for (int u = 0; u < UNROLL; ++u) {
-            const int h = hb + u * hstep;
-            ptr[u] = nullptr;
-            if (h < nh) {
-                ptr[u] = (h < hq ? qrow + (int64_t)h * d : krow + (int64_t)(h - hq) * d) + j * VEC;
-                load_vec<T, VEC>(ptr[u], v[u]);
+            for (int u = 0; u < UNROLL; ++u) {
+                const int h = hb + u * hstep;
+                ptr[u] = nullptr;
+                if (h < nh) {
+                    ptr[u] = (h < hq ? qrow + (int64_t)h * d : krow + (int64_t)(h - hq) * d) + j * VEC;
+                    v[u] = Elt<T>::template load_raw_keep<VEC>(ptr[u]);
+                }
             }
         }
 #pragma unroll
         for (int u = 0; u < UNROLL; ++u) {
             if (ptr[u] == nullptr) continue;
+            float f[VEC];
+            Elt<T>::template widen<VEC>(v[u], f);
 #pragma unroll
-            for (int p = 0; p < P; ++p) rope_rotate(v[u][2 * p], v[u][2 * p + 1], c[p], s[p]);
-            store_vec<T, VEC>(ptr[u], v[u]);
+            for (int p = 0; p < P; ++p) rope_rotate(f[2 * p], f[2 * p + 1], c[p], s[p]);
+            store_vec<T, VEC>(ptr[u], f);
         }
     }
 }
@@ -211,13 +239,38 @@ constexpr bool ew_binary() {
     return OP == kSwiglu || OP == kAdd;
 }
 
-// Grid-stride over nvec vectors as virtual block `vblock` of `vgrid`;
-// UNROLL vectors per thread per round, all loads first.
+// Grid-stride over nvec vectors as virtual block `vblock` of `vgrid`.
+// UNROLL > 1: UNROLL vectors per thread per round, all loads first (cheap
+// ops).  UNROLL == 1: the next vector's load is issued before the current
+// one is computed, and vectors stay in their raw 16-byte form until then
+// (transcendental ops: few registers, two loads in flight per thread).
 template <typename T, int VEC, int OP, int UNROLL>
 __device__ __forceinline__ void ew_body(const T* a, const T* b, T* out, int64_t nvec,
                                         int64_t vblock, int64_t vgrid) {
     const int64_t stride = vgrid * blockDim.x;
     int64_t i = vblock * blockDim.x + threadIdx.x;
+    if constexpr (UNROLL == 1) {
+        using Raw = typename Elt<T>::template Raw<VEC>;
+        if (i >= nvec) return;
+        Raw na = Elt<T>::template load_raw<VEC>(a + i * VEC), nb;
+        if constexpr (ew_binary<OP>()) nb = Elt<T>::template load_raw<VEC>(b + i * VEC);
+        for (; i < nvec; i += stride) {
+            const Raw ca = na;
+            Raw cb;
+            if constexpr (ew_binary<OP>()) cb = nb;
+            const int64_t n = i + stride;
+            if (n < nvec) {
+                na = Elt<T>::template load_raw<VEC>(a + n * VEC);
+                if constexpr (ew_binary<OP>()) nb = Elt<T>::template load_raw<VEC>(b + n * VEC);
+            }
+            float va[VEC], vb[VEC], o[VEC];
+            Elt<T>::template widen<VEC>(ca, va);
+            if constexpr (ew_binary<OP>()) Elt<T>::template widen<VEC>(cb, vb);
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) o[j] = ew_apply<OP>(va[j], ew_binary<OP>() ? vb[j] : 0.0f);
+            store_vec<T, VEC>(out + i * VEC, o);
+        }
+    } else {
     for (; i + (UNROLL - 1) * stride < nvec; i += UNROLL * stride) {
         float va[UNROLL][VEC], vb[UNROLL][VEC];
 #pragma unroll
@@ -240,6 +293,7 @@ __device__ __forceinline__ void ew_body(const T* a, const T* b, T* out, int64_t 
 #pragma unroll
         for (int j = 0; j < VEC; ++j) o[j] = ew_apply<OP>(va[j], ew_binary<OP>() ? vb[j] : 0.0f);
         store_vec<T, VEC>(out + i * VEC, o);
+    }
     }
 }
 

@@ -72,7 +72,7 @@ __global__ void __launch_bounds__(kThreads) k_chain(const __grid_constant__ Chai
         return;
     }
     b -= a.rope_blocks;
-    tbk::ew_body<T, V, tbk::kSwiglu, 4>(a.gate, a.up, a.act, a.nvec, b, a.ew_blocks);
+    tbk::ew_body<T, V, tbk::kSwiglu, 1>(a.gate, a.up, a.act, a.nvec, b, a.ew_blocks);
 }
 
 template <typename T>
@@ -113,15 +113,14 @@ int launch_fused(const TbB200LayerChain* c, const tbh::DeviceState* ds, cudaStre
         a.up = static_cast<const T*>(c->up);
         a.act = static_cast<T*>(c->act_out);
         a.nvec = c->rows * c->intermediate / V;
-        a.ew_blocks = tbh::ew_grid((a.nvec + 3) / 4, kThreads, ds);
+        a.ew_blocks = tbh::ew_grid(a.nvec, kThreads, ds);
     }
     const int64_t grid = a.norm_blocks + a.rope_blocks + a.ew_blocks;
     if (grid == 0) return TB_OK;
     switch (items) {
         case 1: k_chain<T, 1><<<(unsigned)grid, kThreads, 0, s>>>(a); break;
         case 2: k_chain<T, 2><<<(unsigned)grid, kThreads, 0, s>>>(a); break;
-        case 4: k_chain<T, 4><<<(unsigned)grid, kThreads, 0, s>>>(a); break;
-        default: k_chain<T, 8><<<(unsigned)grid, kThreads, 0, s>>>(a); break;
+        default: k_chain<T, 4><<<(unsigned)grid, kThreads, 0, s>>>(a); break;
     }
     TB_LAUNCH_CHECK("layer chain kernel");
     return TB_OK;

@@ -2,8 +2,9 @@
 // elements (reference arithmetic at ew_apply, bodies.cuh).
 //
 // Data path: HBM bound (2 or 3 * n * s bytes).  A grid-stride loop over
-// 16-byte vectors, sized to fill the SMs, 4 independent vectors per thread
-// per round with every load issued before the arithmetic.  A ragged tail
+// 16-byte vectors, sized to fill the SMs: one vector per thread per round
+// for SiLU/GELU/SwiGLU (their expf/tanhf and division make register count
+// and occupancy the limit), four for the residual add.  A ragged tail
 // (n not a multiple of the vector width) goes to a one-CTA scalar launch;
 // unaligned pointers use the scalar instantiation throughout.
 #include "bodies.cuh"
@@ -14,7 +15,7 @@ namespace {
 using tbk::Elt;
 
 template <typename T, int VEC, int OP, int UNROLL>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 4)
 k_ew(const T* a, const T* b, T* out, int64_t nvec) {
     tbk::ew_body<T, VEC, OP, UNROLL>(a, b, out, nvec, blockIdx.x, gridDim.x);
 }
@@ -24,7 +25,9 @@ int launch(const void* a, const void* b, void* out, int64_t n, cudaStream_t s) {
     tbh::DeviceState* ds = tbh::current_device_state();
     if (!ds) return TB_ERR_DEVICE;
     constexpr int V = Elt<T>::kVec;
-    constexpr int kThreads = 256, kUnroll = 4;
+    // Transcendental ops issue enough arithmetic per byte that occupancy
+    // matters more than deep unrolling (registers); plain adds unroll.
+    constexpr int kThreads = 256, kUnroll = OP == tbk::kAdd ? 4 : 1;
     constexpr bool bin = tbk::ew_binary<OP>();
     const T* ap = static_cast<const T*>(a);
     const T* bp = static_cast<const T*>(b);

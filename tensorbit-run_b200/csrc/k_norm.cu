@@ -5,7 +5,7 @@
 // register-resident data path are described at res_rms_body (bodies.cuh).
 // HBM bound: 4*cols*s bytes per row (x, residual in; h, y out) plus the
 // weight row once from L2.  Rows wider than the register path (more than
-// 8 vectors per thread at 1024 threads) use a two-pass kernel that re-reads
+// 4 vectors per thread at 1024 threads) use a two-pass kernel that re-reads
 // the row, normally from L2.
 #include "bodies.cuh"
 #include "tb_internal.h"
@@ -14,8 +14,8 @@ namespace {
 
 using tbk::Elt;
 
-template <typename T, int VEC, int ITEMS>
-__global__ void __launch_bounds__(1024)
+template <typename T, int VEC, int ITEMS, int MAXT>
+__global__ void __launch_bounds__(MAXT)
 k_res_rms(const T* x, const T* res, const T* __restrict__ w, T* h_out, T* y, int64_t rows,
           int cols, float eps, int G) {
     __shared__ float red[32];
@@ -56,12 +56,20 @@ int launch_vec(const T* x, const T* res, const T* w, T* h, T* y, int64_t rows, i
     const int rows_per_cta = c.threads / c.G;
     const unsigned grid = (unsigned)((rows + rows_per_cta - 1) / rows_per_cta);
     const int n = (int)cols;
-    switch (c.items) {
-        case 1: k_res_rms<T, VEC, 1><<<grid, c.threads, 0, s>>>(x, res, w, h, y, rows, n, eps, c.G); break;
-        case 2: k_res_rms<T, VEC, 2><<<grid, c.threads, 0, s>>>(x, res, w, h, y, rows, n, eps, c.G); break;
-        case 4: k_res_rms<T, VEC, 4><<<grid, c.threads, 0, s>>>(x, res, w, h, y, rows, n, eps, c.G); break;
-        case 8: k_res_rms<T, VEC, 8><<<grid, c.threads, 0, s>>>(x, res, w, h, y, rows, n, eps, c.G); break;
-        default: k_res_rms_wide<T><<<(unsigned)rows, 1024, 0, s>>>(x, res, w, h, y, cols, eps); break;
+    if (c.items == 0) {
+        k_res_rms_wide<T><<<(unsigned)rows, 1024, 0, s>>>(x, res, w, h, y, cols, eps);
+    } else if (c.threads <= 256) {
+        switch (c.items) {
+            case 1: k_res_rms<T, VEC, 1, 256><<<grid, c.threads, 0, s>>>(x, res, w, h, y, rows, n, eps, c.G); break;
+            case 2: k_res_rms<T, VEC, 2, 256><<<grid, c.threads, 0, s>>>(x, res, w, h, y, rows, n, eps, c.G); break;
+            default: k_res_rms<T, VEC, 4, 256><<<grid, c.threads, 0, s>>>(x, res, w, h, y, rows, n, eps, c.G); break;
+        }
+    } else {
+        switch (c.items) {
+            case 1: k_res_rms<T, VEC, 1, 1024><<<grid, c.threads, 0, s>>>(x, res, w, h, y, rows, n, eps, c.G); break;
+            case 2: k_res_rms<T, VEC, 2, 1024><<<grid, c.threads, 0, s>>>(x, res, w, h, y, rows, n, eps, c.G); break;
+            default: k_res_rms<T, VEC, 4, 1024><<<grid, c.threads, 0, s>>>(x, res, w, h, y, rows, n, eps, c.G); break;
+        }
     }
     TB_LAUNCH_CHECK("residual_rms_norm kernel");
     return TB_OK;

@@ -26,7 +26,7 @@ using tbk::Elt;
 using tbk::RopeConst;
 
 template <typename T, int VEC, int MODE, int UNROLL>
-__global__ void __launch_bounds__(1024)
+__global__ void __launch_bounds__(256)
 k_rope(T* q, T* k, const int32_t* __restrict__ positions, int hq, int hkv, int d,
        const float2* __restrict__ table, int table_pos, const __grid_constant__ RopeConst rc) {
     tbk::rope_body<T, VEC, MODE, UNROLL>(q, k, positions, hq, hkv, d, table, table_pos, rc,
@@ -42,9 +42,8 @@ int launch(int64_t rows, int hq, int hkv, int d, void* q, void* k, const int32_t
     const float2* tp = reinterpret_cast<const float2*>(table);
     const bool vec_ok = (d % V == 0) && (!hq || tbh::aligned16(q)) && (!hkv || tbh::aligned16(k)) &&
                         (table == nullptr || tbh::aligned16(table));
-    const int lanes = vec_ok ? d / V : d / 2;
-    int threads = 256;
-    if (lanes > threads) threads = ((lanes + 31) / 32) * 32;
+    // d <= 512: at most 256 lanes per head, so 256 threads always cover a head.
+    const int threads = 256;
     if (vec_ok)
         k_rope<T, V, MODE, 4><<<(unsigned)rows, threads, 0, s>>>(qp, kp, positions, hq, hkv, d, tp,
                                                                  table_pos, rc);

@@ -15,6 +15,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 namespace tbk {
 
 constexpr unsigned kFull = 0xffffffffu;
@@ -23,21 +25,102 @@ constexpr unsigned kFull = 0xffffffffu;
 template <typename T>
 struct Elt;
 
+// Raw<VEC>: VEC elements kept in their storage format (one 16-byte word
+// for a full vector); load_raw streams them in (evict-first), widen turns
+// them into f32.
+template <typename T, int VEC>
+struct RawOf {
+    T e[VEC];
+};
+
 template <>
 struct Elt<float> {
     static constexpr int kVec = 4;  // elements per 16-byte access
+    template <int VEC>
+    using Raw = typename std::conditional<VEC == 4, uint4, RawOf<float, VEC>>::type;
     __device__ __forceinline__ static float load(const float* p) { return *p; }
     __device__ __forceinline__ static void store(float* p, float v) { *p = v; }
+    template <int VEC>
+    __device__ __forceinline__ static Raw<VEC> load_raw(const float* p) {
+        if constexpr (VEC == 4) {
+            return __ldcs(reinterpret_cast<const uint4*>(p));
+        } else {
+            Raw<VEC> r;
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) r.e[i] = p[i];
+            return r;
+        }
+    }
+    // Same, with the default caching (the data is read again or written back).
+    template <int VEC>
+    __device__ __forceinline__ static Raw<VEC> load_raw_keep(const float* p) {
+        if constexpr (VEC == 4) {
+            return *reinterpret_cast<const uint4*>(p);
+        } else {
+            Raw<VEC> r;
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) r.e[i] = p[i];
+            return r;
+        }
+    }
+    template <int VEC>
+    __device__ __forceinline__ static void widen(const Raw<VEC>& r, float (&v)[VEC]) {
+        if constexpr (VEC == 4) {
+            v[0] = __uint_as_float(r.x); v[1] = __uint_as_float(r.y);
+            v[2] = __uint_as_float(r.z); v[3] = __uint_as_float(r.w);
+        } else {
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) v[i] = r.e[i];
+        }
+    }
 };
 
 template <>
 struct Elt<__nv_bfloat16> {
     static constexpr int kVec = 8;
+    template <int VEC>
+    using Raw = typename std::conditional<VEC == 8, uint4, RawOf<__nv_bfloat16, VEC>>::type;
     __device__ __forceinline__ static float load(const __nv_bfloat16* p) {
         return __bfloat162float(*p);
     }
     __device__ __forceinline__ static void store(__nv_bfloat16* p, float v) {
         *p = __float2bfloat16_rn(v);
+    }
+    template <int VEC>
+    __device__ __forceinline__ static Raw<VEC> load_raw(const __nv_bfloat16* p) {
+        if constexpr (VEC == 8) {
+            return __ldcs(reinterpret_cast<const uint4*>(p));
+        } else {
+            Raw<VEC> r;
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) r.e[i] = p[i];
+            return r;
+        }
+    }
+    template <int VEC>
+    __device__ __forceinline__ static Raw<VEC> load_raw_keep(const __nv_bfloat16* p) {
+        if constexpr (VEC == 8) {
+            return *reinterpret_cast<const uint4*>(p);
+        } else {
+            Raw<VEC> r;
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) r.e[i] = p[i];
+            return r;
+        }
+    }
+    template <int VEC>
+    __device__ __forceinline__ static void widen(const Raw<VEC>& r, float (&v)[VEC]) {
+        if constexpr (VEC == 8) {
+            const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                v[2 * i] = __uint_as_float(w[i] << 16);
+                v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) v[i] = __bfloat162float(r.e[i]);
+        }
     }
 };
 

@@ -37,8 +37,8 @@ int ew_grid(int64_t work_items, int threads, const DeviceState* ds, int ctas_per
 void rope_inv_freq(float theta, int head_dim, float* out);
 
 // Thread layout of the RMSNorm bodies for rows of `nvec` vectors: G threads
-// per row (a power of two, 32..max_group), `items` vectors per thread
-// (0 means the row is too wide for registers), CTA size `threads`.
+// per row (a power of two, 32..max_group), `items` vectors per thread (at
+// most 4; 0 means the row is too wide for registers), CTA size `threads`.
 struct NormCfg {
     int G, items, threads;
 };
@@ -52,10 +52,9 @@ inline NormCfg norm_cfg(int64_t nvec, int max_group) {
         while (g < (nvec + 3) / 4) g <<= 1;
         c.G = g > max_group ? max_group : g;
         const int64_t it = (nvec + c.G - 1) / c.G;
-        c.items = it > 8 ? 0 : (int)it;
+        c.items = it > 4 ? 0 : (int)it;  // wider rows: the two-pass kernel
     }
-    if (c.items > 4) c.items = 8;
-    else if (c.items > 2) c.items = 4;
+    if (c.items > 2) c.items = 4;
     c.threads = c.G < 256 ? 256 : c.G;
     return c;
 }
