@@ -82,6 +82,7 @@ int tb_b200_is_device_ptr(const void* p, int* is_device);
  * clears them. */
 int tb_b200_check_status(void* stream, unsigned int* flags_out);
 #define TB_B200_FLAG_TOKEN_RANGE 0x1u   /* embedding: id < 0 or id >= vocab */
+#define TB_B200_FLAG_WAIT_TIMEOUT 0x2u  /* a kernel's bounded wait gave up (its output is invalid) */
 
 /* ======================================================================
  * Row kernels

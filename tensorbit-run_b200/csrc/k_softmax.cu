@@ -560,7 +560,14 @@ extern "C" int tb_b200_softmax(int dtype, int64_t rows, int64_t cols, const void
     if (rows == 0 || cols == 0) return TB_OK;
     if (!x || !y) return TB_ERR_INVALID_ARG;
     cudaStream_t s = tbh::stream_of(stream);
-    if (dtype == TB_DTYPE_F32) return launch<float>(rows, cols, x, mask, y, s);
+    if (dtype == TB_DTYPE_F32) {
+        if (!mask) {
+            const int rc = tbh::softmax_staged_f32(rows, cols, static_cast<const float*>(x),
+                                                   static_cast<float*>(y), s);
+            if (rc != 1) return rc;
+        }
+        return launch<float>(rows, cols, x, mask, y, s);
+    }
     if (dtype == TB_DTYPE_BF16) return launch<__nv_bfloat16>(rows, cols, x, mask, y, s);
     return TB_ERR_UNSUPPORTED_DTYPE;
 }

@@ -1,0 +1,772 @@
+// k_softmax_staged.cu -- f32 row softmax for rows of up to 32768 terms:
+// each row staged once in shared memory, the reference's in-order sum
+// scanned by dedicated warps while the next row streams in.
+//
+// Reference arithmetic (tb_cpu_softmax_f32, src/ops/softmax.c:4-32):
+//   m = max x (strict '>', from -inf);  e_i = expf(x_i - m);
+//   sum = ((e_0 + e_1) + e_2) + ...  (f32, in order);  y_i = e_i * (1.0f/sum) if sum > 0.
+// e here is __expf(x - m) (ex2-based; at most 2 + 1.173|x - m| ulp from exp,
+// which weighted by e itself stays below 4e-7 of the largest term), computed
+// by one expression everywhere so every pass sees the same bits.  The sum is
+// the in-order f32 sum of those terms, bit for bit (see ordered_sum.cuh for
+// the integer-grid argument).
+//
+// CTA = 16 warps, persistent over rows blockIdx.x, +gridDim.x, ... (one CTA
+// per SM at V = 32000: the row buffer is 125 KB of shared memory):
+//   warps 0-2   scanners: the ordered sum of every third row, from the tile
+//               summaries below (three summary buffers); each scan overlaps
+//               the workers' next three rows.
+//   warps 3-15  workers, per row:
+//     load   bulk asynchronous copies of the row in four chunks, one
+//            mbarrier each -- the copy engine keeps the row in flight, HBM
+//            is read once.  A chunk of the next row is issued as soon as
+//            the units pass below has finished with that chunk.
+//     max    row max over the staged row.
+//     exp    e = __expf(x - m) in place, and a float sum per 256-term tile.
+//     est    running-sum estimate at each tile start -> predicted binade b_t;
+//            tiles likely to cross a binade (or near a power of two) get a
+//            slot: their terms and prefix arrays of grid units on grids b_t
+//            and b_t + 1, with per-term tie bits.
+//     units  per tile, the integer sum of rne(e / u_b) as a function of the
+//            running sum's parity at the tile start: (D0, D1).  Only exact
+//            ties (e/u = k + 1/2) make them differ; round-to-even then
+//            depends on the parity of the partial sum.
+//     handoff the summaries go to the row's scanner.
+//     final  y = e * (1/sum) of the row three back, e recomputed from x
+//            (still in L2), streaming stores.
+//   The scanner walks 32 tiles per step: an ordered composition scan of the
+//   (D0, D1) functions gives every tile's exact start offset; the first tile
+//   that is not in the current binade, is flagged, or crosses 2^24 units is
+//   resolved -- in a slotted tile by a ballot over the prefix array (the
+//   crossing term is one real f32 addition, the rest of the tile O(1) on the
+//   next grid), otherwise term by term (ordered_sum_tile).
+// Every wait is bounded (tma.cuh); a timeout raises TB_B200_FLAG_WAIT_TIMEOUT,
+// after which the CTA skips its remaining waits and copies and ends.
+#include <math.h>
+
+#include "ordered_sum.cuh"
+#include "tb_device.cuh"
+#include "tb_internal.h"
+#include "tma.cuh"
+
+namespace {
+
+constexpr int kNT = 512;
+constexpr int kScanWarps = 3;
+constexpr int kBufs = kScanWarps;  // summary/slot buffers: row i uses i % kBufs
+constexpr int kWorkWarps = kNT / 32 - kScanWarps;
+constexpr int kWork = kWorkWarps * 32;
+constexpr int kTileN = 256;
+constexpr int kMaxCols = 32768;
+constexpr int kMaxTiles = kMaxCols / kTileN;
+constexpr int kChunks = 4;
+constexpr int kMaxSlots = 10;
+constexpr uint32_t kSat = 1u << 30;
+constexpr uint32_t kLimit = 1u << 24;
+constexpr uint32_t kExact = 1u << 16;  // meta flag: sum the tile term by term
+constexpr uint32_t kNoSlot = 0xffu;
+constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+
+// A slotted tile: its terms and, per grid g (binade b_t + g), the inclusive
+// prefix sums of the terms' grid units (floor for a tie) and the tie bits
+// (byte q: terms 4q .. 4q+3).
+struct Slot {
+    float e[kTileN];
+    uint32_t P[2][kTileN];
+    uint8_t tie[2][kTileN / 4];
+};
+
+// Hand-off from the workers to a row's scanner (double-buffered).
+struct RowSummary {
+    uint2 D[kMaxTiles];        // (D0, D1) per tile
+    uint32_t meta[kMaxTiles];  // predicted binade (int8) | kExact | slot << 24
+    float m;                   // the row max
+    float pad[3];
+};
+
+// e = 2^((x - m) * log2(e)) on the MUFU pipe (subnormal results flush to 0).
+__device__ __forceinline__ float expo(float x, float m) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(__fmul_rn(__fsub_rn(x, m), 1.44269504f)));
+    return r;
+}
+
+// Sum over the warp of nonnegative lane values v (each < 2^31 in the
+// scaled domain), to about 2^-21 relative: the largest lane value sets a
+// power-of-two scale, each lane rounds v * scale to an integer, and one
+// redux.sync adds them.
+__device__ __forceinline__ float warp_sum_est(float v) {
+    const uint32_t mx = __reduce_max_sync(tbk::kFull, __float_as_uint(v));  // v >= 0: bits order
+    if (mx == 0u) return 0.0f;
+    if (mx >= 0x7f800000u) return __uint_as_float(0x7fc00000u);  // inf or NaN
+    const int ex = (int)(mx >> 23) - 127;                 // largest lane value in [2^ex, 2^(ex+1))
+    const int sh = 25 - ex;                               // lane values < 2^26 after scaling
+    if (sh > 126) return 0.0f;                            // below 2^-100: no binade anyway
+    const float sc = __uint_as_float((uint32_t)(sh + 127) << 23);
+    const uint32_t q = __float2uint_rn(__fmul_rn(v, sc));
+    const uint32_t tot = __reduce_add_sync(tbk::kFull, q);  // < 32 * 2^26 = 2^31
+    return __fmul_rn((float)tot, __uint_as_float((uint32_t)(127 - sh) << 23));
+}
+
+__device__ __forceinline__ void work_sync() {
+    asm volatile("bar.sync 1, %0;" ::"r"(kWork) : "memory");
+}
+
+__device__ __forceinline__ bool near_pow2(float v) {
+    const uint32_t mant = __float_as_uint(v) & 0x7fffffu;
+    return mant < (1u << 13) || mant > (1u << 23) - (1u << 13);
+}
+
+// For a = t + 1.5*2^23 with 0 <= t < 2^22: rne(t) as an integer, read from
+// a's mantissa bits (an integer op instead of a float-to-int conversion).
+__device__ __forceinline__ uint32_t magic_int(float a) { return __float_as_uint(a) - 0x4B400000u; }
+
+// Grid units of one term on grid inv_u, exact for any t (slot arrays):
+// base = rne(t), or floor(t) for an exact tie; 2^25 (certainly an event)
+// for t >= 2^25 or NaN.
+__device__ __forceinline__ uint32_t units_exact(float e, float inv_u, bool* tie) {
+    const float t = __fmul_rn(e, inv_u);
+    if (t < 4194304.0f) {
+        const float a = __fadd_rn(t, kMagic);
+        const float d = __fsub_rn(t, __fsub_rn(a, kMagic));
+        *tie = fabsf(d) == 0.5f;
+        return magic_int(a) - (d < 0.0f && *tie ? 1u : 0u);
+    }
+    *tie = false;
+    if (!(t < 33554432.0f)) return 1u << 25;
+    const float fl = floorf(t);
+    *tie = __fsub_rn(t, fl) == 0.5f;
+    return *tie ? (uint32_t)fl : __float2uint_rn(t);
+}
+
+// Units added by one term given the parity of the partial sum before it.
+struct Fn {
+    uint32_t a0, a1;  // total for an even / odd running sum at the start
+};
+__device__ __forceinline__ Fn compose(Fn f, Fn g) {  // f, then g
+    Fn r;
+    r.a0 = min(f.a0 + ((f.a0 & 1u) ? g.a1 : g.a0), kSat);
+    r.a1 = min(f.a1 + (((f.a1 + 1u) & 1u) ? g.a1 : g.a0), kSat);
+    return r;
+}
+__device__ __forceinline__ Fn term_fn(float e, float inv_u) {
+    const float t = __fmul_rn(e, inv_u);
+    const float a = __fadd_rn(t, kMagic);
+    const float d = __fsub_rn(t, __fsub_rn(a, kMagic));
+    const uint32_t ri = magic_int(a);
+    if (fabsf(d) != 0.5f) return Fn{ri, ri};
+    const uint32_t base = d < 0.0f ? ri - 1u : ri;  // floor(t)
+    // round half to even: the result (start + base + extra) must be even
+    return Fn{base + (base & 1u), base + ((base + 1u) & 1u)};
+}
+// In-order reduction of the lanes' functions (lane 0 first); valid in lane 0.
+__device__ __forceinline__ Fn warp_compose(Fn f) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        Fn g;
+        g.a0 = __shfl_down_sync(tbk::kFull, f.a0, o);
+        g.a1 = __shfl_down_sync(tbk::kFull, f.a1, o);
+        if ((lane & (2 * o - 1)) == 0) f = compose(f, g);
+    }
+    return f;
+}
+
+// Saturating inclusive warp scan of u32.
+__device__ __forceinline__ uint32_t warp_incl(uint32_t v) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t n = __shfl_up_sync(tbk::kFull, v, o);
+        if (lane >= o) v = min(v + n, kSat);
+    }
+    return v;
+}
+
+struct Shared {
+    float* xbuf;
+    RowSummary* sum;  // [2]
+    float* tsum;      // [kMaxTiles]
+    Slot* slots;      // [2][nslot]
+};
+
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, unsigned* status,
+                                         volatile int* abort_flag) {
+    if (*abort_flag) return false;
+    if (tbk::mbar_wait(bar, parity, status)) return true;
+    *abort_flag = 1;
+    return false;
+}
+
+// ------------------------------------------------------------------ scanner
+// Terms of `tile` in the ordered_sum_tile layout (lane l: terms 8l .. 8l+7).
+__device__ __forceinline__ void tile_terms(const Slot* s, const float* xr, float m, int tile,
+                                           int n, float (&e)[8]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int j = lane * 8 + k;
+        e[k] = 0.0f;
+        if (j < n) e[k] = s ? s->e[j] : expo(xr[(int64_t)tile * kTileN + j], m);
+    }
+}
+
+__device__ void resolve_tile(tbk::RunSum& st, const Slot* slots, int nslot, const float* xr,
+                             float m, int tile, uint32_t meta, int cols) {
+    const int lane = threadIdx.x & 31;
+    const int tb = (int)(int8_t)(meta & 0xffu);
+    const uint32_t slot = meta >> 24;
+    const Slot* s = slot < (uint32_t)nslot ? slots + slot : nullptr;
+    const int n = min(kTileN, cols - tile * kTileN);
+    int pos = 0;
+    if (s && !(meta & kExact) && st.fast && st.b == tb) {
+        while (pos < n && !st.nan) {
+            const int g = st.fast ? st.b - tb : -1;
+            if (g != 0 && g != 1) break;
+            const uint32_t* P = s->P[g];
+            const uint32_t P0 = pos ? P[pos - 1] : 0u;
+            const uint4 pa = *reinterpret_cast<const uint4*>(P + 4 * lane);
+            const uint4 pb = *reinterpret_cast<const uint4*>(P + 128 + 4 * lane);
+            const uint32_t ta = s->tie[g][lane], tbt = s->tie[g][32 + lane];
+            const uint32_t va[4] = {pa.x, pa.y, pa.z, pa.w}, vb[4] = {pb.x, pb.y, pb.z, pb.w};
+            uint32_t ea = 0, eb = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int ja = 4 * lane + k, jb = 128 + 4 * lane + k;
+                if (ja >= pos && ja < n && (((ta >> k) & 1u) || st.S + (va[k] - P0) >= kLimit))
+                    ea |= 1u << k;
+                if (jb >= pos && jb < n && (((tbt >> k) & 1u) || st.S + (vb[k] - P0) >= kLimit))
+                    eb |= 1u << k;
+            }
+            const unsigned ba = __ballot_sync(tbk::kFull, ea != 0);
+            const unsigned bb = __ballot_sync(tbk::kFull, eb != 0);
+            if (!ba && !bb) {
+                st.S += P[n - 1] - P0;
+                st.s = __fmul_rn((float)st.S, st.u);
+                return;
+            }
+            int j;
+            if (ba) {
+                const int f = __ffs(ba) - 1;
+                j = 4 * f + __ffs(__shfl_sync(tbk::kFull, ea, f)) - 1;
+            } else {
+                const int f = __ffs(bb) - 1;
+                j = 128 + 4 * f + __ffs(__shfl_sync(tbk::kFull, eb, f)) - 1;
+            }
+            const uint32_t before = st.S + (j ? P[j - 1] - P0 : 0u);
+            st.set(__fadd_rn(__fmul_rn((float)before, st.u), s->e[j]));
+            pos = j + 1;
+        }
+        if (pos >= n || st.nan) return;
+    }
+    float e[8];
+    tile_terms(s, xr, m, tile, n, e);
+    tbk::ordered_sum_tile<8>(st, e, n, pos);
+}
+
+__device__ float scan_row(const RowSummary& R, const Slot* slots, int nslot, const float* xr,
+                          float m, int cols) {
+    const int lane = threadIdx.x & 31;
+    const int ntiles = (cols + kTileN - 1) / kTileN;
+    tbk::RunSum st;
+    {  // tile 0: one lane's in-order additions (the sum crosses many binades here)
+        const uint32_t s0 = R.meta[0] >> 24;
+        const int n0 = min(cols, kTileN);
+        float acc = 0.0f;
+        if (lane == 0) {
+            if (s0 < (uint32_t)nslot && n0 == kTileN) {
+                const float* e0 = slots[s0].e;
+#pragma unroll 16
+                for (int i = 0; i < kTileN; i += 4) {
+                    const float4 v = *reinterpret_cast<const float4*>(e0 + i);
+                    acc = __fadd_rn(acc, v.x);
+                    acc = __fadd_rn(acc, v.y);
+                    acc = __fadd_rn(acc, v.z);
+                    acc = __fadd_rn(acc, v.w);
+                }
+            } else if (s0 < (uint32_t)nslot) {
+                const float* e0 = slots[s0].e;
+                for (int i = 0; i < n0; i += 4) {
+                    const float4 v = *reinterpret_cast<const float4*>(e0 + i);
+                    acc = __fadd_rn(acc, v.x);
+                    acc = __fadd_rn(acc, v.y);
+                    acc = __fadd_rn(acc, v.z);
+                    acc = __fadd_rn(acc, v.w);
+                }
+            } else {
+                for (int i = 0; i < n0; ++i) acc = __fadd_rn(acc, expo(xr[i], m));
+            }
+        }
+        st.set(__shfl_sync(tbk::kFull, acc, 0));
+    }
+    for (int t0 = 0; t0 < ntiles && !st.nan; t0 += 32) {
+        const int cnt = min(32, ntiles - t0);
+        uint2 dl = make_uint2(0u, 0u);
+        uint32_t meta = 0;
+        if (lane < cnt) {
+            dl = R.D[t0 + lane];
+            meta = R.meta[t0 + lane];
+        }
+        const int tb = (int)(int8_t)(meta & 0xffu);
+        int pos = t0 == 0 ? 1 : 0;
+        while (pos < cnt && !st.nan) {
+            const bool valid = lane >= pos && lane < cnt;
+            const bool ok = valid && st.fast && !(meta & kExact) && tb == st.b;
+            const Fn f = ok ? Fn{dl.x, dl.y} : Fn{0u, 0u};
+            Fn inc = f;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                Fn g;
+                g.a0 = __shfl_up_sync(tbk::kFull, inc.a0, o);
+                g.a1 = __shfl_up_sync(tbk::kFull, inc.a1, o);
+                if (lane >= o) inc = compose(g, inc);
+            }
+            Fn exc;
+            exc.a0 = __shfl_up_sync(tbk::kFull, inc.a0, 1);
+            exc.a1 = __shfl_up_sync(tbk::kFull, inc.a1, 1);
+            if (lane == 0) exc = Fn{0u, 0u};
+            const uint32_t p = st.S & 1u;
+            const uint32_t ex = p ? exc.a1 : exc.a0;
+            const uint32_t mine = ((p + ex) & 1u) ? f.a1 : f.a0;
+            const bool ev = valid && (!ok || st.S + ex + mine >= kLimit);
+            const unsigned bal = __ballot_sync(tbk::kFull, ev);
+            if (bal == 0) {
+                st.S += __shfl_sync(tbk::kFull, p ? inc.a1 : inc.a0, 31);
+                st.s = __fmul_rn((float)st.S, st.u);
+                break;
+            }
+            const int fl = __ffs(bal) - 1;
+            const uint32_t pre = __shfl_sync(tbk::kFull, ex, fl);
+            if (st.fast && pre) {
+                st.S += pre;
+                st.s = __fmul_rn((float)st.S, st.u);
+            }
+            resolve_tile(st, slots, nslot, xr, m, t0 + fl, __shfl_sync(tbk::kFull, meta, fl), cols);
+            pos = fl + 1;
+        }
+    }
+    return st.s;
+}
+
+// ------------------------------------------------------------------ kernel
+__global__ void __launch_bounds__(kNT, 1)
+k_softmax_staged(const float* x, float* y, int rows, int cols, int nslot, unsigned* status) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ __align__(8) uint64_t bar_x[kChunks], bar_ready[kBufs], bar_done[kBufs];
+    __shared__ float red[kWorkWarps];
+    __shared__ float row_sum[4];           // ordered sum of row i at i & 3 (scanner -> final)
+    __shared__ uint8_t slot_tile[kMaxSlots];   // the current row's slotted tiles, slot order
+    __shared__ int n_slotted;
+    __shared__ int abort_flag;
+
+    const int ntiles = (cols + kTileN - 1) / kTileN;
+    const int xbytes = ((cols * 4 + 1023) / 1024) * 1024;
+    Shared sh;
+    sh.xbuf = reinterpret_cast<float*>(smem);
+    sh.sum = reinterpret_cast<RowSummary*>(smem + xbytes);
+    sh.tsum = reinterpret_cast<float*>(sh.sum + kBufs);
+    sh.slots = reinterpret_cast<Slot*>(sh.tsum + kMaxTiles);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nloc = rows > (int)blockIdx.x ? (rows - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const uint32_t rowbytes = (uint32_t)cols * 4u;
+    // chunk bytes: a whole number of tiles (1 KB each)
+    const uint32_t cb = ((rowbytes + kChunks - 1) / kChunks + 1023u) / 1024u * 1024u;
+    const int tpc = (int)(cb / 1024u);  // tiles per chunk
+    volatile int* abort_v = &abort_flag;
+
+    if (threadIdx.x == 0) {
+        for (int c = 0; c < kChunks; ++c) {
+            tbk::mbar_init(&bar_x[c], 1);
+        }
+        for (int k = 0; k < kBufs; ++k) {
+            tbk::mbar_init(&bar_ready[k], 1);
+            tbk::mbar_init(&bar_done[k], 1);
+        }
+        abort_flag = 0;
+        tbk::fence_mbar_init();
+    }
+    __syncthreads();
+
+    auto issue_chunk = [&](int i, int c) {  // one thread: chunk c of local row i into xbuf
+        const float* src = x + (int64_t)((int)blockIdx.x + i * (int)gridDim.x) * cols;
+        const uint32_t lo = min(rowbytes, c * cb), hi = min(rowbytes, (c + 1) * cb);
+        tbk::mbar_expect_tx(&bar_x[c], hi - lo);
+        if (hi > lo)  // x stays in L2 until the final pass reads it again
+            tbk::bulk_g2s_hint(reinterpret_cast<unsigned char*>(sh.xbuf) + lo,
+                               reinterpret_cast<const unsigned char*>(src) + lo, hi - lo, &bar_x[c],
+                               tbk::policy_evict_last());
+    };
+
+    if (warp < kScanWarps) {
+        // ---------------- scanners: warp s takes rows s, s + kBufs, ...
+        for (int i = warp; i < nloc; i += kScanWarps) {
+            wait_bar(&bar_ready[warp], (uint32_t)(i / kBufs) & 1u, status, abort_v);
+            const int row = (int)blockIdx.x + i * (int)gridDim.x;
+            const RowSummary& R = sh.sum[warp];
+            const float sum =
+                scan_row(R, sh.slots + warp * nslot, nslot, x + (int64_t)row * cols, R.m, cols);
+            if (lane == 0) row_sum[i & 3] = sum;
+            __syncwarp();
+            if (lane == 0) {
+                __threadfence_block();
+                tbk::mbar_arrive(&bar_done[warp]);
+            }
+        }
+        return;
+    }
+
+    // ---------------- workers
+    const int wt = threadIdx.x - kScanWarps * 32;
+    const int ww = wt >> 5;
+    if (wt == 0 && nloc > 0)
+        for (int c = 0; c < kChunks; ++c) issue_chunk(0, c);
+    float m_prev = 0.0f;  // row max of row i-1
+    for (int i = 0; i < nloc + 1; ++i) {
+        float m_row = 0.0f;
+        if (i < nloc) {
+            const int k = i % kBufs;
+            RowSummary& R = sh.sum[k];
+            Slot* SL = sh.slots + k * nslot;
+            const uint32_t par = (uint32_t)i & 1u;
+            // ---- max
+            float mx = -INFINITY;
+            int waited = -1;
+            for (int t = ww; t < ntiles; t += kWorkWarps) {
+                const int c = t / tpc;
+                for (; waited < c; ++waited) wait_bar(&bar_x[waited + 1], par, status, abort_v);
+                const float* xt = sh.xbuf + t * kTileN;
+                const int n = min(kTileN, cols - t * kTileN);
+                if (4 * lane < n) {
+                    const float4 a = *reinterpret_cast<const float4*>(xt + 4 * lane);
+                    mx = fmaxf(mx, fmaxf(fmaxf(a.x, a.y), fmaxf(a.z, a.w)));
+                }
+                if (128 + 4 * lane < n) {
+                    const float4 b = *reinterpret_cast<const float4*>(xt + 128 + 4 * lane);
+                    mx = fmaxf(mx, fmaxf(fmaxf(b.x, b.y), fmaxf(b.z, b.w)));
+                }
+            }
+            // every chunk's phase must be seen complete before its next copy
+            for (; waited < kChunks - 1; ++waited) wait_bar(&bar_x[waited + 1], par, status, abort_v);
+            mx = tbk::warp_max(mx);
+            if (lane == 0) red[ww] = mx;
+            work_sync();
+            float m = red[0];
+#pragma unroll
+            for (int w = 1; w < kWorkWarps; ++w) m = fmaxf(m, red[w]);
+            m_row = m;
+            // ---- exp in place + tile sums, two tiles per iteration
+            for (int t0 = ww; t0 < ntiles; t0 += 2 * kWorkWarps) {
+                const int tq[2] = {t0, t0 + kWorkWarps};
+                float s[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    s[h] = 0.0f;
+                    if (tq[h] >= ntiles) continue;
+                    float* xt = sh.xbuf + tq[h] * kTileN;
+                    const int n = min(kTileN, cols - tq[h] * kTileN);
+                    if (4 * lane < n) {
+                        float4 a = *reinterpret_cast<float4*>(xt + 4 * lane);
+                        a.x = expo(a.x, m); a.y = expo(a.y, m); a.z = expo(a.z, m); a.w = expo(a.w, m);
+                        *reinterpret_cast<float4*>(xt + 4 * lane) = a;
+                        s[h] = (a.x + a.y) + (a.z + a.w);
+                    }
+                    if (128 + 4 * lane < n) {
+                        float4 b = *reinterpret_cast<float4*>(xt + 128 + 4 * lane);
+                        b.x = expo(b.x, m); b.y = expo(b.y, m); b.z = expo(b.z, m); b.w = expo(b.w, m);
+                        *reinterpret_cast<float4*>(xt + 128 + 4 * lane) = b;
+                        s[h] += (b.x + b.y) + (b.z + b.w);
+                    }
+                }
+                s[0] = warp_sum_est(s[0]);
+                s[1] = warp_sum_est(s[1]);
+                if (lane == 0) {
+                    sh.tsum[tq[0]] = s[0];
+                    if (tq[1] < ntiles) sh.tsum[tq[1]] = s[1];
+                }
+            }
+            // buffer k last held row i - kBufs: its scan must be over
+            if (i >= kBufs)
+                wait_bar(&bar_done[k], (uint32_t)((i - kBufs) / kBufs) & 1u, status, abort_v);
+            work_sync();
+            // ---- estimate -> predicted binades, slots (first worker warp)
+            if (ww == 0) {
+                float v[4];
+                float local = 0.0f;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int t = 4 * lane + q;
+                    v[q] = t < ntiles ? sh.tsum[t] : 0.0f;
+                    local += v[q];
+                }
+                float inc = local;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const float nb = __shfl_up_sync(tbk::kFull, inc, o);
+                    if (lane >= o) inc += nb;
+                }
+                float run = __shfl_up_sync(tbk::kFull, inc, 1);
+                if (lane == 0) run = 0.0f;
+                int bq[4];
+                unsigned lk = 0;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int t = 4 * lane + q;
+                    const int b = tbk::binade_of(run);
+                    const float nxt = run + v[q];
+                    bq[q] = b;
+                    if (t < ntiles && (t == 0 || b == tbk::kNoBinade || tbk::binade_of(nxt) != b ||
+                                       near_pow2(run) || near_pow2(nxt)))
+                        lk |= 1u << q;
+                    run = nxt;
+                }
+                const uint32_t cnt = __popc(lk);
+                uint32_t sl = warp_incl(cnt) - cnt;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int t = 4 * lane + q;
+                    if (t >= ntiles) continue;
+                    uint32_t slot = kNoSlot;
+                    if ((lk >> q) & 1u) {
+                        if (sl < (uint32_t)nslot) slot = sl;
+                        ++sl;
+                    }
+                    R.meta[t] = ((uint32_t)bq[q] & 0xffu) | (slot << 24);
+                    if (slot != kNoSlot) slot_tile[slot] = (uint8_t)t;
+                }
+                if (lane == 31) n_slotted = (int)min(sl, (uint32_t)nslot);
+                if (lane == 0) R.m = m;
+            }
+            work_sync();
+            // ---- units: (D0, D1) per tile, two tiles per iteration; a slotted
+            //      tile's terms go to its slot; finished chunks are released
+            for (int t0 = ww; t0 < ntiles; t0 += 2 * kWorkWarps) {
+                const int tq[2] = {t0, t0 + kWorkWarps};
+                float e[2][8];
+                uint32_t meta[2];
+                float acc[2], dm[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int t = tq[h];
+                    const bool live = t < ntiles;
+                    const int n = live ? min(kTileN, cols - t * kTileN) : 0;
+                    const float* xt = sh.xbuf + (live ? t : 0) * kTileN;
+                    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), c = a;
+                    if (4 * lane < n) a = *reinterpret_cast<const float4*>(xt + 4 * lane);
+                    if (128 + 4 * lane < n) c = *reinterpret_cast<const float4*>(xt + 128 + 4 * lane);
+                    e[h][0] = a.x; e[h][1] = a.y; e[h][2] = a.z; e[h][3] = a.w;
+                    e[h][4] = c.x; e[h][5] = c.y; e[h][6] = c.z; e[h][7] = c.w;
+                    meta[h] = live ? R.meta[t] : (uint32_t)(uint8_t)tbk::kNoBinade | (kNoSlot << 24);
+                    const uint32_t slot = meta[h] >> 24;
+                    if (slot < (uint32_t)nslot) {
+                        Slot& S = SL[slot];
+                        if (4 * lane < n) *reinterpret_cast<float4*>(S.e + 4 * lane) = a;
+                        if (128 + 4 * lane < n) *reinterpret_cast<float4*>(S.e + 128 + 4 * lane) = c;
+                    }
+                }
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int b = (int)(int8_t)(meta[h] & 0xffu);
+                    const float iu = tbk::inv_grid(b == tbk::kNoBinade ? 0 : b);
+                    acc[h] = 0.0f;
+                    dm[h] = 0.0f;
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const float tt = __fmul_rn(e[h][q], iu);
+                        const float r = __fsub_rn(__fadd_rn(tt, kMagic), kMagic);
+                        acc[h] = __fadd_rn(acc[h], r);
+                        dm[h] = fmaxf(dm[h], fabsf(__fsub_rn(tt, r)));
+                    }
+                }
+                // acc < 2^22 - 1 implies every t < 2^22 - 1/2: the magic
+                // rounding was exact; NaN fails the test too.
+                const unsigned big = (__ballot_sync(tbk::kFull, !(acc[0] < 4194303.0f)) ? 1u : 0u) |
+                                     (__ballot_sync(tbk::kFull, !(acc[1] < 4194303.0f)) ? 2u : 0u);
+                const unsigned tie = (__ballot_sync(tbk::kFull, dm[0] == 0.5f) ? 1u : 0u) |
+                                     (__ballot_sync(tbk::kFull, dm[1] == 0.5f) ? 2u : 0u);
+                // exact integer tile sums (each lane's acc < 2^22 unless big)
+                const uint32_t sa = __reduce_add_sync(tbk::kFull, magic_int(__fadd_rn(fminf(acc[0], 4194303.0f), kMagic)));
+                const uint32_t sb = __reduce_add_sync(tbk::kFull, magic_int(__fadd_rn(fminf(acc[1], 4194303.0f), kMagic)));
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int t = tq[h];
+                    if (t >= ntiles) continue;
+                    const int b = (int)(int8_t)(meta[h] & 0xffu);
+                    uint2 D;
+                    uint32_t flags = 0;
+                    if (b == tbk::kNoBinade) {
+                        D = make_uint2(0u, 0u);
+                        flags = kExact;
+                    } else if ((big >> h) & 1u) {
+                        D = make_uint2(kSat, kSat);
+                    } else if ((tie >> h) & 1u) {
+                        const float iu = tbk::inv_grid(b);
+                        Fn fa{0u, 0u}, fb{0u, 0u};
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) fa = compose(fa, term_fn(e[h][q], iu));
+#pragma unroll
+                        for (int q = 4; q < 8; ++q) fb = compose(fb, term_fn(e[h][q], iu));
+                        fa = warp_compose(fa);
+                        fb = warp_compose(fb);
+                        const Fn ft = compose(fa, fb);
+                        D = make_uint2(ft.a0, ft.a1);
+                    } else {
+                        const uint32_t s = h == 0 ? sa : sb;
+                        D = make_uint2(s, s);
+                    }
+                    if (lane == 0) {
+                        R.D[t] = D;
+                        if (flags) R.meta[t] = meta[h] | flags;
+                    }
+                }
+            }
+            work_sync();
+            // the row buffer is free: the next row's copy starts now
+            if (wt == 0 && i + 1 < nloc && !*abort_v) {
+                tbk::fence_proxy_async_shared();
+                for (int c = 0; c < kChunks; ++c) issue_chunk(i + 1, c);
+            }
+            // ---- slot prefix arrays, one slotted tile per warp
+            for (int sidx = ww; sidx < n_slotted; sidx += kWorkWarps) {
+                const int t = slot_tile[sidx];
+                const uint32_t meta = R.meta[t];
+                const uint32_t slot = meta >> 24;
+                const int b = (int)(int8_t)(meta & 0xffu);
+                if (b == tbk::kNoBinade) continue;
+                Slot& S = SL[slot];
+                const int n = min(kTileN, cols - t * kTileN);
+                const bool va = 4 * lane < n, vb = 128 + 4 * lane < n;
+                float4 a = make_float4(0.f, 0.f, 0.f, 0.f), c = a;
+                if (va) a = *reinterpret_cast<const float4*>(S.e + 4 * lane);
+                if (vb) c = *reinterpret_cast<const float4*>(S.e + 128 + 4 * lane);
+                const float e[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+#pragma unroll
+                for (int g = 0; g < 2; ++g) {
+                    const float iug = tbk::inv_grid(b + g);
+                    uint32_t u[8], tie = 0;
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        bool tq = false;
+                        u[q] = (q < 4 ? va : vb) ? units_exact(e[q], iug, &tq) : 0u;
+                        tie |= (uint32_t)tq << q;
+                    }
+                    const uint32_t ha = min(min(u[0] + u[1], kSat) + min(u[2] + u[3], kSat), kSat);
+                    const uint32_t hb = min(min(u[4] + u[5], kSat) + min(u[6] + u[7], kSat), kSat);
+                    const uint32_t ia = warp_incl(ha);
+                    const uint32_t tot_a = __shfl_sync(tbk::kFull, ia, 31);
+                    const uint32_t ib = warp_incl(hb);
+                    uint32_t pa = ia - ha, pb = min(tot_a + (ib - hb), kSat);
+                    uint4 wa, wb;
+                    pa = min(pa + u[0], kSat); wa.x = pa;
+                    pa = min(pa + u[1], kSat); wa.y = pa;
+                    pa = min(pa + u[2], kSat); wa.z = pa;
+                    pa = min(pa + u[3], kSat); wa.w = pa;
+                    pb = min(pb + u[4], kSat); wb.x = pb;
+                    pb = min(pb + u[5], kSat); wb.y = pb;
+                    pb = min(pb + u[6], kSat); wb.z = pb;
+                    pb = min(pb + u[7], kSat); wb.w = pb;
+                    *reinterpret_cast<uint4*>(S.P[g] + 4 * lane) = wa;
+                    *reinterpret_cast<uint4*>(S.P[g] + 128 + 4 * lane) = wb;
+                    S.tie[g][lane] = (uint8_t)(tie & 0xfu);
+                    S.tie[g][32 + lane] = (uint8_t)(tie >> 4);
+                }
+            }
+            work_sync();
+            if (wt == 0) {
+                __threadfence_block();
+                tbk::mbar_arrive(&bar_ready[k]);
+            }
+        }
+        // ---- final pass of row i-1 (scanned while this row was processed;
+        //      its x is still in L2)
+        const float mp = m_prev;
+        m_prev = m_row;
+        if (i >= 1) {
+            const int ip = i - 1;
+            wait_bar(&bar_done[ip % kBufs], (uint32_t)(ip / kBufs) & 1u, status, abort_v);
+            const float sum = row_sum[ip & 3];
+            const bool norm = sum > 0.0f;
+            const float inv = __fdiv_rn(1.0f, sum);
+            const int64_t row = (int64_t)blockIdx.x + (int64_t)ip * gridDim.x;
+            const float4* xr = reinterpret_cast<const float4*>(x + row * cols);
+            float4* yr = reinterpret_cast<float4*>(y + row * cols);
+            const int nv = cols / 4;
+            constexpr int kU8 = 8;
+            const uint64_t pol = tbk::policy_evict_first();  // last use of x
+            int v = wt;
+            for (; v + (kU8 - 1) * kWork < nv; v += kU8 * kWork) {
+                float4 q[kU8];
+#pragma unroll
+                for (int u = 0; u < kU8; ++u) q[u] = tbk::ld_f4_hint(xr + v + u * kWork, pol);
+#pragma unroll
+                for (int u = 0; u < kU8; ++u) {
+                    float4 o;
+                    o.x = expo(q[u].x, mp); o.y = expo(q[u].y, mp);
+                    o.z = expo(q[u].z, mp); o.w = expo(q[u].w, mp);
+                    if (norm) {
+                        o.x = __fmul_rn(o.x, inv); o.y = __fmul_rn(o.y, inv);
+                        o.z = __fmul_rn(o.z, inv); o.w = __fmul_rn(o.w, inv);
+                    }
+                    __stcs(yr + v + u * kWork, o);
+                }
+            }
+            for (; v < nv; v += kWork) {
+                const float4 q = tbk::ld_f4_hint(xr + v, pol);
+                float4 o;
+                o.x = expo(q.x, mp); o.y = expo(q.y, mp); o.z = expo(q.z, mp); o.w = expo(q.w, mp);
+                if (norm) {
+                    o.x = __fmul_rn(o.x, inv); o.y = __fmul_rn(o.y, inv);
+                    o.z = __fmul_rn(o.z, inv); o.w = __fmul_rn(o.w, inv);
+                }
+                __stcs(yr + v, o);
+            }
+        }
+    }
+    // No copy may still be writing this CTA's shared memory when it exits
+    // (possible only after a timeout): a last bounded wait on each chunk.
+    if (wt == 0 && nloc > 0)
+        for (int c = 0; c < kChunks; ++c)
+            tbk::mbar_wait(&bar_x[c], (uint32_t)(nloc - 1) & 1u, status, 200000000ull);
+}
+
+size_t staged_smem(int cols, int nslot) {
+    const size_t xbytes = ((size_t)cols * 4 + 1023) / 1024 * 1024;
+    return xbytes + kBufs * sizeof(RowSummary) + kMaxTiles * sizeof(float) +
+           kBufs * (size_t)nslot * sizeof(Slot);
+}
+
+}  // namespace
+
+namespace tbh {
+
+// f32 softmax through k_softmax_staged.  Returns 1 (nothing launched) when
+// the shape is not one it handles: a mask, more than 32768 columns, a
+// column count that is not a multiple of 4, or unaligned rows.
+int softmax_staged_f32(int64_t rows, int64_t cols, const float* x, float* y, cudaStream_t s) {
+    if (cols > kMaxCols || cols % 4 || !aligned16(x) || !aligned16(y) || rows > INT32_MAX)
+        return 1;
+    DeviceState* ds = current_device_state();
+    if (!ds) return TB_ERR_DEVICE;
+    const int ntiles = (int)((cols + kTileN - 1) / kTileN);
+    const size_t budget = ds->smem_optin > 1024 ? ds->smem_optin - 1024 : 0;  // static shared
+    int nslot = ntiles < kMaxSlots ? ntiles : kMaxSlots;
+    while (nslot > 0 && staged_smem((int)cols, nslot) > budget) --nslot;
+    if (nslot < 2) return 1;
+    const size_t smem = staged_smem((int)cols, nslot);
+    static thread_local size_t attr_set[64];
+    if (ds->device >= 0 && ds->device < 64 && attr_set[ds->device] < smem) {
+        TB_CUDA_TRY(cudaFuncSetAttribute(k_softmax_staged,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        attr_set[ds->device] = smem;
+    }
+    int per_sm = 0;
+    TB_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_softmax_staged, kNT, smem));
+    if (per_sm < 1) return 1;
+    const int64_t cap = (int64_t)ds->sm_count * per_sm;
+    const int grid = (int)(rows < cap ? rows : cap);
+    k_softmax_staged<<<grid, kNT, smem, s>>>(x, y, (int)rows, (int)cols, nslot, ds->status);
+    TB_LAUNCH_CHECK("softmax kernel (staged)");
+    return TB_OK;
+}
+
+}  // namespace tbh

@@ -59,6 +59,10 @@ inline NormCfg norm_cfg(int64_t nvec, int max_group) {
     return c;
 }
 
+// f32 softmax staged through shared memory (k_softmax_staged.cu): TB_OK
+// after launching, 1 when the shape is not one it handles, else an error.
+int softmax_staged_f32(int64_t rows, int64_t cols, const float* x, float* y, cudaStream_t s);
+
 }  // namespace tbh
 
 #define TB_CUDA_TRY(call)                                       \

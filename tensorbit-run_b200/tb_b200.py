@@ -367,3 +367,62 @@ def tensor(t, device=None) -> TbTensor:
     d.device = (DEVICE_CUDA if t.is_cuda else DEVICE_CPU) if device is None else device
     d.owns_data = False
     return d
+
+
+# ------------------------------------------------------------ multi-GPU
+def partition(total: int, parts: int, part: int):
+    """[lo, hi) of part `part` when `total` items are split into `parts`."""
+    lo, hi = C.c_int64(), C.c_int64()
+    check(lib().tb_b200_partition(total, parts, part, C.byref(lo), C.byref(hi)), "partition")
+    return lo.value, hi.value
+
+
+def shard_plan(ids, vocab: int, nranks: int, rank: int):
+    """The exchange plan of tb_b200_embedding_sharded for `rank` (host only):
+    (send_counts, recv_counts, send_rows, recv_rows, local_dst, local_src) as
+    numpy arrays, trimmed to their counts."""
+    import numpy as np
+    ids = np.ascontiguousarray(ids, np.int32)
+    n = len(ids)
+    sc = np.zeros(nranks, np.int64)
+    rc = np.zeros(nranks, np.int64)
+    bufs = [np.zeros(n + 1, np.int32) for _ in range(4)]
+    nl = C.c_int64()
+    check(lib().tb_b200_shard_plan(n, vocab, nranks, rank, ids.ctypes.data, sc.ctypes.data,
+                                   rc.ctypes.data, *[b.ctypes.data for b in bufs], C.byref(nl)),
+          "shard_plan")
+    s, r, ld, ls = bufs
+    return sc, rc, s[:sc.sum()], r[:rc.sum()], ld[:nl.value], ls[:nl.value]
+
+
+def comm_unique_id() -> bytes:
+    buf = C.create_string_buffer(128)
+    check(lib().tb_b200_comm_unique_id(buf), "comm_unique_id")
+    return buf.raw
+
+
+def comm_init(nranks: int, rank: int, unique_id: bytes, device: int) -> None:
+    buf = C.create_string_buffer(bytes(unique_id), 128)
+    check(lib().tb_b200_comm_init(nranks, rank, buf, device), "comm_init")
+
+
+def comm_destroy() -> None:
+    check(lib().tb_b200_comm_destroy(), "comm_destroy")
+
+
+def embedding_sharded(ids_host, table_shard, vocab: int, y_local=None, stream=None):
+    """This rank's token part of the full-table gather, from its vocab shard
+    (tb_b200_embedding_sharded).  ids_host: int32 numpy array of all tokens."""
+    import numpy as np
+    torch = _torch()
+    rank, nranks = C.c_int(), C.c_int()
+    check(lib().tb_b200_comm_info(C.byref(rank), C.byref(nranks)), "comm_info")
+    ids = np.ascontiguousarray(ids_host, np.int32)
+    lo, hi = partition(len(ids), nranks.value, rank.value)
+    if y_local is None:
+        y_local = torch.empty((hi - lo, table_shard.shape[1]), dtype=table_shard.dtype,
+                              device=table_shard.device)
+    check(lib().tb_b200_embedding_sharded(dtype_code(table_shard), len(ids), table_shard.shape[1],
+                                          vocab, ids.ctypes.data, ptr(table_shard), ptr(y_local),
+                                          stream or cur_stream()), "embedding_sharded")
+    return y_local

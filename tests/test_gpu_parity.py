@@ -254,8 +254,13 @@ def test_rope_single_position_and_odd_head_dim(dev):
 
 
 # ----------------------------------------------------------------- softmax
+# f32 rows of up to 32768 columns (a multiple of 4, no mask) take the
+# shared-memory-staged kernel; "pipeline" gives every CTA several rows,
+# "staged_max" is its widest row, "past_staged" the first width beyond it.
 SOFTMAX_CASES = [("mock", 64, 100, 2.0), ("7b", 256, 32000, 3.0), ("70b", 16, 128256, 3.0),
-                 ("odd", 9, 1001, 3.0), ("one", 3, 1, 1.0), ("wide_std", 8, 5000, 20.0)]
+                 ("odd", 9, 1001, 3.0), ("one", 3, 1, 1.0), ("wide_std", 8, 5000, 20.0),
+                 ("pipeline", 600, 4096, 3.0), ("staged_max", 300, 32768, 3.0),
+                 ("past_staged", 5, 32772, 3.0), ("spiky", 40, 32000, 12.0)]
 
 
 @pytest.mark.parametrize("name,rows,cols,std", SOFTMAX_CASES)
@@ -282,6 +287,23 @@ def test_softmax_sum_is_the_sequential_sum(dev):
     sync()
     worst, _ = assert_f32(gy, y_ref, "softmax 128K")
     assert worst < 2e-6, f"softmax 128K row error {worst:.2e}: not the sequential sum"
+
+
+def test_softmax_in_place_and_nan_in_wide_rows(dev):
+    """y may alias x; a NaN term makes its row NaN, other rows unaffected."""
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((300, 32000), dtype=np.float32) * np.float32(3)
+    x[7, 20000] = np.float32("nan")
+    x[8, :] = -np.inf
+    x[9, 31999] = np.inf
+    y_ref = O.softmax(x)
+    g = gpu(x, dev)
+    T.softmax(g, y=g)
+    sync()
+    gy = to_np(g)
+    assert (np.isnan(gy) == np.isnan(y_ref)).all()
+    keep = ~np.isnan(y_ref).any(axis=1)
+    assert_f32(gy[keep], y_ref[keep], "softmax in place")
 
 
 def test_softmax_with_mask_and_special_rows(dev):

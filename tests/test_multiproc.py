@@ -1,0 +1,149 @@
+"""Multi-process paths of the vocab-sharded embedding
+(tb_b200_embedding_sharded, include/tb_b200.h), one process per rank.
+
+CPU (gloo, world sizes 2 and 3): every rank builds only its own exchange
+plan with tb_b200_shard_plan and moves its rows with torch.distributed
+send/recv in the order the NCCL path groups them; the assembled token part
+must equal the full-table gather (tb_cpu_embedding_f32,
+src/ops/embedding.c:4-14) -- the plan is consistent across processes.
+
+GPU (2 GPUs, skipped on fewer): the library's NCCL exchange itself,
+bit-exact against the oracle for f32 and bf16 tables.
+"""
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+sys.path.insert(0, os.path.join(ROOT, "tensorbit-run_b200"))
+sys.path.insert(0, ROOT)
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def problem(n, vocab, dim, seed):
+    rng = np.random.default_rng(seed)
+    ids = rng.integers(0, vocab, n).astype(np.int32)
+    table = rng.standard_normal((vocab, dim), dtype=np.float32)
+    return ids, table
+
+
+def _gloo_rank(rank, world, port, n, vocab, dim, q):
+    import torch
+    import torch.distributed as dist
+    import tb_b200 as T
+    from oracle import oracle as O
+    try:
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=world)
+        ids, table = problem(n, vocab, dim, 1234)
+        vlo, vhi = T.partition(vocab, world, rank)
+        tlo, thi = T.partition(n, world, rank)
+        shard = table[vlo:vhi]
+        sc, rc, send, recv, ld, ls = T.shard_plan(ids, vocab, world, rank)
+        out = np.full((thi - tlo, dim), np.nan, np.float32)
+        out[ld] = shard[ls]
+        sendbuf = torch.from_numpy(np.ascontiguousarray(shard[send]))
+        recvbuf = torch.empty((int(rc.sum()), dim), dtype=torch.float32)
+        reqs, so, ro = [], 0, 0
+        for p in range(world):
+            if p == rank:
+                continue
+            if sc[p]:
+                reqs.append(dist.isend(sendbuf[so:so + sc[p]].contiguous(), p))
+            if rc[p]:
+                reqs.append(dist.irecv(recvbuf[ro:ro + rc[p]], p))
+            so += int(sc[p])
+            ro += int(rc[p])
+        for r in reqs:
+            r.wait()
+        out[recv] = recvbuf.numpy()
+        ok = np.array_equal(out, O.embedding(ids[tlo:thi], table))
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, ok, ""))
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, False, repr(e)))
+
+
+def run_ranks(target, world, *args, timeout=180):
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=target, args=(r, world, port) + args + (q,)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = []
+    try:
+        for _ in range(world):
+            results.append(q.get(timeout=timeout))
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    return sorted(results)
+
+
+@pytest.mark.parametrize("world,n,vocab,dim", [(2, 1000, 32000, 16), (3, 257, 1000, 8)])
+def test_sharded_embedding_exchange_gloo(world, n, vocab, dim):
+    res = run_ranks(_gloo_rank, world, n, vocab, dim)
+    assert len(res) == world
+    for rank, ok, err in res:
+        assert ok, f"rank {rank}: {err or 'token part differs from the full-table gather'}"
+
+
+def _nccl_rank(rank, world, port, n, vocab, dim, q):
+    import torch
+    import torch.distributed as dist
+    import tb_b200 as T
+    from oracle import oracle as O
+    try:
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=world)
+        uid = [T.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        T.comm_init(world, rank, uid[0], rank)
+        ids, table = problem(n, vocab, dim, 99)
+        vlo, vhi = T.partition(vocab, world, rank)
+        tlo, thi = T.partition(n, world, rank)
+        oks = []
+        for host in (table, O.f32_to_bf16(table)):  # f32, then bf16 bits
+            ref = O.embedding(ids[tlo:thi], host)
+            shard = torch.from_numpy(np.ascontiguousarray(host[vlo:vhi]))
+            if host.dtype == np.uint16:
+                shard = shard.view(torch.int16).view(torch.bfloat16)
+            y = T.embedding_sharded(ids, shard.cuda(), vocab)
+            torch.cuda.synchronize()
+            got = y.cpu()
+            if host.dtype == np.uint16:
+                got = got.view(torch.int16)
+            oks.append(np.array_equal(got.numpy().view(host.dtype), ref))
+        T.comm_destroy()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, all(oks), ""))
+    except Exception as e:
+        q.put((rank, False, repr(e)))
+
+
+@pytest.mark.gpu
+def test_sharded_embedding_nccl_two_gpus():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    res = run_ranks(_nccl_rank, 2, 4096, 32000, 4096)
+    assert len(res) == 2
+    for rank, ok, err in res:
+        assert ok, f"rank {rank}: {err or 'sharded gather differs from the full-table gather'}"
