@@ -48,6 +48,17 @@ WORKLOAD = "llama7b-prefill-4096 row ops (embedding, residual+RMSNorm, RoPE, Swi
            "softmax, argmax)"
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per row of each
+# kernel, from one ncu capture each (profiles/*.md), for roofline.traffic.
+# Writes still dirty in L2 when a kernel ends are not in the write count.
+TRAFFIC_PER_ROW = {
+    "embedding": (32137856 / 4096, "profiles/k_embed_llama7b-prefill-4096.md"),
+    "layer_chain": (485573888 / 4096, "profiles/k_chain_llama7b-prefill-4096.md"),
+    "softmax": ((135831040 + 74903040) / 1024, "profiles/k_softmax_staged_logits-1024x32000.md"),
+    "argmax": (530358016 / 4096, "profiles/k_argmax_llama7b-prefill-4096.md"),
+}
+
+
 def step_bytes(rows, act_s):
     c = CFG
     parts = {
@@ -380,7 +391,11 @@ def run_gpu(args, rank, world, local):
         "per_op": per_op,
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1),
                      "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
-                     "frac": round(achieved / peak, 3), "traffic": None},
+                     "frac": round(achieved / peak, 3),
+                     "traffic": (round(TRAFFIC_PER_ROW[dom][0] * R)
+                                 if TRAFFIC_PER_ROW[dom][0] else None),
+                     "algorithmic_bytes": parts[dom],
+                     "traffic_source": TRAFFIC_PER_ROW[dom][1] + " (ncu, scaled to the launch's rows)"},
         "e2e": {"value": round(total_bytes / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": bi,
                 "d2h_bytes_per_step": bo, "api": "tb_b200_* C ABI, pinned host buffers"},

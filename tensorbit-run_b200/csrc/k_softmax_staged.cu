@@ -13,10 +13,10 @@
 //
 // CTA = 16 warps, persistent over rows blockIdx.x, +gridDim.x, ... (one CTA
 // per SM at V = 32000: the row buffer is 125 KB of shared memory):
-//   warps 0-2   scanners: the ordered sum of every third row, from the tile
+//   warps 0,4,8 scanners: the ordered sum of every third row, from the tile
 //               summaries below (three summary buffers); each scan overlaps
-//               the workers' next three rows.
-//   warps 3-15  workers, per row:
+//               the workers' next row.  They share one warp scheduler.
+//   the others  workers, per row:
 //     load   bulk asynchronous copies of the row in four chunks, one
 //            mbarrier each -- the copy engine keeps the row in flight, HBM
 //            is read once.  A chunk of the next row is issued as soon as
@@ -61,6 +61,7 @@ constexpr int kMaxCols = 32768;
 constexpr int kMaxTiles = kMaxCols / kTileN;
 constexpr int kChunks = 4;
 constexpr int kMaxSlots = 10;
+constexpr uint64_t kStaggerNs = 7000;  // start offset of odd CTAs
 constexpr uint32_t kSat = 1u << 30;
 constexpr uint32_t kLimit = 1u << 24;
 constexpr uint32_t kExact = 1u << 16;  // meta flag: sum the tile term by term
@@ -81,7 +82,8 @@ struct RowSummary {
     uint2 D[kMaxTiles];        // (D0, D1) per tile
     uint32_t meta[kMaxTiles];  // predicted binade (int8) | kExact | slot << 24
     float m;                   // the row max
-    float pad[3];
+    float s0;                  // in-order sum of tile 0's terms
+    float pad[2];
 };
 
 // e = 2^((x - m) * log2(e)) on the MUFU pipe (subnormal results flush to 0).
@@ -269,36 +271,7 @@ __device__ float scan_row(const RowSummary& R, const Slot* slots, int nslot, con
     const int lane = threadIdx.x & 31;
     const int ntiles = (cols + kTileN - 1) / kTileN;
     tbk::RunSum st;
-    {  // tile 0: one lane's in-order additions (the sum crosses many binades here)
-        const uint32_t s0 = R.meta[0] >> 24;
-        const int n0 = min(cols, kTileN);
-        float acc = 0.0f;
-        if (lane == 0) {
-            if (s0 < (uint32_t)nslot && n0 == kTileN) {
-                const float* e0 = slots[s0].e;
-#pragma unroll 16
-                for (int i = 0; i < kTileN; i += 4) {
-                    const float4 v = *reinterpret_cast<const float4*>(e0 + i);
-                    acc = __fadd_rn(acc, v.x);
-                    acc = __fadd_rn(acc, v.y);
-                    acc = __fadd_rn(acc, v.z);
-                    acc = __fadd_rn(acc, v.w);
-                }
-            } else if (s0 < (uint32_t)nslot) {
-                const float* e0 = slots[s0].e;
-                for (int i = 0; i < n0; i += 4) {
-                    const float4 v = *reinterpret_cast<const float4*>(e0 + i);
-                    acc = __fadd_rn(acc, v.x);
-                    acc = __fadd_rn(acc, v.y);
-                    acc = __fadd_rn(acc, v.z);
-                    acc = __fadd_rn(acc, v.w);
-                }
-            } else {
-                for (int i = 0; i < n0; ++i) acc = __fadd_rn(acc, expo(xr[i], m));
-            }
-        }
-        st.set(__shfl_sync(tbk::kFull, acc, 0));
-    }
+    st.set(R.s0);  // tile 0: summed in order by a worker
     for (int t0 = 0; t0 < ntiles && !st.nan; t0 += 32) {
         const int cnt = min(32, ntiles - t0);
         uint2 dl = make_uint2(0u, 0u);
@@ -398,27 +371,40 @@ k_softmax_staged(const float* x, float* y, int rows, int cols, int nslot, unsign
                                tbk::policy_evict_last());
     };
 
-    if (warp < kScanWarps) {
-        // ---------------- scanners: warp s takes rows s, s + kBufs, ...
-        for (int i = warp; i < nloc; i += kScanWarps) {
-            wait_bar(&bar_ready[warp], (uint32_t)(i / kBufs) & 1u, status, abort_v);
+    // Scanners are warps 0, 4, 8: one warp scheduler (warp id mod 4) runs
+    // them beside a single worker warp, so their latency-bound chains are
+    // not starved of issue slots by the throughput-bound workers.
+    const bool scanner = (warp & 3) == 0 && (warp >> 2) < kScanWarps;
+    if (scanner) {
+        // ---------------- scanner sc takes rows sc, sc + kBufs, ...
+        const int sc = warp >> 2;
+        for (int i = sc; i < nloc; i += kScanWarps) {
+            wait_bar(&bar_ready[sc], (uint32_t)(i / kBufs) & 1u, status, abort_v);
             const int row = (int)blockIdx.x + i * (int)gridDim.x;
-            const RowSummary& R = sh.sum[warp];
+            const RowSummary& R = sh.sum[sc];
             const float sum =
-                scan_row(R, sh.slots + warp * nslot, nslot, x + (int64_t)row * cols, R.m, cols);
+                scan_row(R, sh.slots + sc * nslot, nslot, x + (int64_t)row * cols, R.m, cols);
             if (lane == 0) row_sum[i & 3] = sum;
             __syncwarp();
             if (lane == 0) {
                 __threadfence_block();
-                tbk::mbar_arrive(&bar_done[warp]);
+                tbk::mbar_arrive(&bar_done[sc]);
             }
         }
         return;
     }
 
     // ---------------- workers
-    const int wt = threadIdx.x - kScanWarps * 32;
-    const int ww = wt >> 5;
+    // Odd CTAs start half a row period later: the CTAs alternate between
+    // their memory-bound and compute-bound phases instead of all hitting
+    // HBM at once.
+    if (blockIdx.x & 1) {
+        const uint64_t t0 = tbk::global_ns();
+        while (tbk::global_ns() - t0 < kStaggerNs) {
+        }
+    }
+    const int ww = warp - min(kScanWarps, (warp + 3) >> 2);  // worker index 0..kWorkWarps-1
+    const int wt = ww * 32 + lane;
     if (wt == 0 && nloc > 0)
         for (int c = 0; c < kChunks; ++c) issue_chunk(0, c);
     float m_prev = 0.0f;  // row max of row i-1
@@ -437,11 +423,11 @@ k_softmax_staged(const float* x, float* y, int rows, int cols, int nslot, unsign
                 for (; waited < c; ++waited) wait_bar(&bar_x[waited + 1], par, status, abort_v);
                 const float* xt = sh.xbuf + t * kTileN;
                 const int n = min(kTileN, cols - t * kTileN);
-                if (4 * lane < n) {
+                if (n == kTileN || 4 * lane < n) {
                     const float4 a = *reinterpret_cast<const float4*>(xt + 4 * lane);
                     mx = fmaxf(mx, fmaxf(fmaxf(a.x, a.y), fmaxf(a.z, a.w)));
                 }
-                if (128 + 4 * lane < n) {
+                if (n == kTileN || 128 + 4 * lane < n) {
                     const float4 b = *reinterpret_cast<const float4*>(xt + 128 + 4 * lane);
                     mx = fmaxf(mx, fmaxf(fmaxf(b.x, b.y), fmaxf(b.z, b.w)));
                 }
@@ -455,40 +441,62 @@ k_softmax_staged(const float* x, float* y, int rows, int cols, int nslot, unsign
 #pragma unroll
             for (int w = 1; w < kWorkWarps; ++w) m = fmaxf(m, red[w]);
             m_row = m;
-            // ---- exp in place + tile sums, two tiles per iteration
-            for (int t0 = ww; t0 < ntiles; t0 += 2 * kWorkWarps) {
-                const int tq[2] = {t0, t0 + kWorkWarps};
-                float s[2];
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    s[h] = 0.0f;
-                    if (tq[h] >= ntiles) continue;
-                    float* xt = sh.xbuf + tq[h] * kTileN;
-                    const int n = min(kTileN, cols - tq[h] * kTileN);
+            // ---- exp in place + tile sums (full tiles unconditional; the
+            //      last tile may be partial)
+            const int nfull = cols / kTileN;
+            for (int t = ww; t < ntiles; t += kWorkWarps) {
+                float* xt = sh.xbuf + t * kTileN;
+                float s = 0.0f;
+                if (t < nfull) {
+                    float4 a = *reinterpret_cast<float4*>(xt + 4 * lane);
+                    float4 b = *reinterpret_cast<float4*>(xt + 128 + 4 * lane);
+                    a.x = expo(a.x, m); a.y = expo(a.y, m); a.z = expo(a.z, m); a.w = expo(a.w, m);
+                    b.x = expo(b.x, m); b.y = expo(b.y, m); b.z = expo(b.z, m); b.w = expo(b.w, m);
+                    *reinterpret_cast<float4*>(xt + 4 * lane) = a;
+                    *reinterpret_cast<float4*>(xt + 128 + 4 * lane) = b;
+                    s = ((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w));
+                } else {
+                    const int n = cols - t * kTileN;
                     if (4 * lane < n) {
                         float4 a = *reinterpret_cast<float4*>(xt + 4 * lane);
                         a.x = expo(a.x, m); a.y = expo(a.y, m); a.z = expo(a.z, m); a.w = expo(a.w, m);
                         *reinterpret_cast<float4*>(xt + 4 * lane) = a;
-                        s[h] = (a.x + a.y) + (a.z + a.w);
+                        s = (a.x + a.y) + (a.z + a.w);
                     }
                     if (128 + 4 * lane < n) {
                         float4 b = *reinterpret_cast<float4*>(xt + 128 + 4 * lane);
                         b.x = expo(b.x, m); b.y = expo(b.y, m); b.z = expo(b.z, m); b.w = expo(b.w, m);
                         *reinterpret_cast<float4*>(xt + 128 + 4 * lane) = b;
-                        s[h] += (b.x + b.y) + (b.z + b.w);
+                        s += (b.x + b.y) + (b.z + b.w);
                     }
                 }
-                s[0] = warp_sum_est(s[0]);
-                s[1] = warp_sum_est(s[1]);
-                if (lane == 0) {
-                    sh.tsum[tq[0]] = s[0];
-                    if (tq[1] < ntiles) sh.tsum[tq[1]] = s[1];
-                }
+                s = warp_sum_est(s);
+                if (lane == 0) sh.tsum[t] = s;
             }
             // buffer k last held row i - kBufs: its scan must be over
             if (i >= kBufs)
                 wait_bar(&bar_done[k], (uint32_t)((i - kBufs) / kBufs) & 1u, status, abort_v);
             work_sync();
+            // ---- tile 0's in-order sum, by the last worker warp, beside the
+            //      estimate below (the row buffer still holds e)
+            if (ww == kWorkWarps - 1 && lane == 0) {
+                const int n0 = min(cols, kTileN);
+                const float* e0 = sh.xbuf;
+                float acc = 0.0f;
+                if (n0 == kTileN) {
+#pragma unroll 16
+                    for (int q = 0; q < kTileN; q += 4) {
+                        const float4 v = *reinterpret_cast<const float4*>(e0 + q);
+                        acc = __fadd_rn(acc, v.x);
+                        acc = __fadd_rn(acc, v.y);
+                        acc = __fadd_rn(acc, v.z);
+                        acc = __fadd_rn(acc, v.w);
+                    }
+                } else {
+                    for (int q = 0; q < n0; ++q) acc = __fadd_rn(acc, e0[q]);
+                }
+                R.s0 = acc;
+            }
             // ---- estimate -> predicted binades, slots (first worker warp)
             if (ww == 0) {
                 float v[4];
@@ -538,86 +546,65 @@ k_softmax_staged(const float* x, float* y, int rows, int cols, int nslot, unsign
                 if (lane == 0) R.m = m;
             }
             work_sync();
-            // ---- units: (D0, D1) per tile, two tiles per iteration; a slotted
-            //      tile's terms go to its slot; finished chunks are released
-            for (int t0 = ww; t0 < ntiles; t0 += 2 * kWorkWarps) {
-                const int tq[2] = {t0, t0 + kWorkWarps};
-                float e[2][8];
-                uint32_t meta[2];
-                float acc[2], dm[2];
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int t = tq[h];
-                    const bool live = t < ntiles;
-                    const int n = live ? min(kTileN, cols - t * kTileN) : 0;
-                    const float* xt = sh.xbuf + (live ? t : 0) * kTileN;
-                    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), c = a;
+            // ---- units: (D0, D1) per tile; a slotted tile's terms go to its slot
+            for (int t = ww; t < ntiles; t += kWorkWarps) {
+                const float* xt = sh.xbuf + t * kTileN;
+                const uint32_t meta = R.meta[t];
+                const int b = (int)(int8_t)(meta & 0xffu);
+                const uint32_t slot = meta >> 24;
+                float4 a, c;
+                if (t < nfull) {
+                    a = *reinterpret_cast<const float4*>(xt + 4 * lane);
+                    c = *reinterpret_cast<const float4*>(xt + 128 + 4 * lane);
+                } else {
+                    const int n = cols - t * kTileN;
+                    a = make_float4(0.f, 0.f, 0.f, 0.f);
+                    c = a;
                     if (4 * lane < n) a = *reinterpret_cast<const float4*>(xt + 4 * lane);
                     if (128 + 4 * lane < n) c = *reinterpret_cast<const float4*>(xt + 128 + 4 * lane);
-                    e[h][0] = a.x; e[h][1] = a.y; e[h][2] = a.z; e[h][3] = a.w;
-                    e[h][4] = c.x; e[h][5] = c.y; e[h][6] = c.z; e[h][7] = c.w;
-                    meta[h] = live ? R.meta[t] : (uint32_t)(uint8_t)tbk::kNoBinade | (kNoSlot << 24);
-                    const uint32_t slot = meta[h] >> 24;
-                    if (slot < (uint32_t)nslot) {
-                        Slot& S = SL[slot];
-                        if (4 * lane < n) *reinterpret_cast<float4*>(S.e + 4 * lane) = a;
-                        if (128 + 4 * lane < n) *reinterpret_cast<float4*>(S.e + 128 + 4 * lane) = c;
-                    }
                 }
+                if (slot < (uint32_t)nslot) {  // warp-uniform; terms past cols are 0
+                    Slot& S = SL[slot];
+                    *reinterpret_cast<float4*>(S.e + 4 * lane) = a;
+                    *reinterpret_cast<float4*>(S.e + 128 + 4 * lane) = c;
+                }
+                const float e[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+                const float iu = tbk::inv_grid(b == tbk::kNoBinade ? 0 : b);
+                float acc = 0.0f, dm = 0.0f;
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int b = (int)(int8_t)(meta[h] & 0xffu);
-                    const float iu = tbk::inv_grid(b == tbk::kNoBinade ? 0 : b);
-                    acc[h] = 0.0f;
-                    dm[h] = 0.0f;
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        const float tt = __fmul_rn(e[h][q], iu);
-                        const float r = __fsub_rn(__fadd_rn(tt, kMagic), kMagic);
-                        acc[h] = __fadd_rn(acc[h], r);
-                        dm[h] = fmaxf(dm[h], fabsf(__fsub_rn(tt, r)));
-                    }
+                for (int q = 0; q < 8; ++q) {
+                    const float tt = __fmul_rn(e[q], iu);
+                    const float r = __fsub_rn(__fadd_rn(tt, kMagic), kMagic);
+                    acc = __fadd_rn(acc, r);
+                    dm = fmaxf(dm, fabsf(__fsub_rn(tt, r)));
                 }
                 // acc < 2^22 - 1 implies every t < 2^22 - 1/2: the magic
                 // rounding was exact; NaN fails the test too.
-                const unsigned big = (__ballot_sync(tbk::kFull, !(acc[0] < 4194303.0f)) ? 1u : 0u) |
-                                     (__ballot_sync(tbk::kFull, !(acc[1] < 4194303.0f)) ? 2u : 0u);
-                const unsigned tie = (__ballot_sync(tbk::kFull, dm[0] == 0.5f) ? 1u : 0u) |
-                                     (__ballot_sync(tbk::kFull, dm[1] == 0.5f) ? 2u : 0u);
-                // exact integer tile sums (each lane's acc < 2^22 unless big)
-                const uint32_t sa = __reduce_add_sync(tbk::kFull, magic_int(__fadd_rn(fminf(acc[0], 4194303.0f), kMagic)));
-                const uint32_t sb = __reduce_add_sync(tbk::kFull, magic_int(__fadd_rn(fminf(acc[1], 4194303.0f), kMagic)));
+                const bool big = __any_sync(tbk::kFull, !(acc < 4194303.0f));
+                const bool tie = __any_sync(tbk::kFull, dm == 0.5f);
+                const uint32_t sum_u =
+                    __reduce_add_sync(tbk::kFull, magic_int(__fadd_rn(fminf(acc, 4194303.0f), kMagic)));
+                uint2 D = make_uint2(sum_u, sum_u);
+                uint32_t flags = 0;
+                if (b == tbk::kNoBinade) {
+                    D = make_uint2(0u, 0u);
+                    flags = kExact;
+                } else if (big) {
+                    D = make_uint2(kSat, kSat);
+                } else if (tie) {
+                    Fn fa{0u, 0u}, fb{0u, 0u};
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int t = tq[h];
-                    if (t >= ntiles) continue;
-                    const int b = (int)(int8_t)(meta[h] & 0xffu);
-                    uint2 D;
-                    uint32_t flags = 0;
-                    if (b == tbk::kNoBinade) {
-                        D = make_uint2(0u, 0u);
-                        flags = kExact;
-                    } else if ((big >> h) & 1u) {
-                        D = make_uint2(kSat, kSat);
-                    } else if ((tie >> h) & 1u) {
-                        const float iu = tbk::inv_grid(b);
-                        Fn fa{0u, 0u}, fb{0u, 0u};
+                    for (int q = 0; q < 4; ++q) fa = compose(fa, term_fn(e[q], iu));
 #pragma unroll
-                        for (int q = 0; q < 4; ++q) fa = compose(fa, term_fn(e[h][q], iu));
-#pragma unroll
-                        for (int q = 4; q < 8; ++q) fb = compose(fb, term_fn(e[h][q], iu));
-                        fa = warp_compose(fa);
-                        fb = warp_compose(fb);
-                        const Fn ft = compose(fa, fb);
-                        D = make_uint2(ft.a0, ft.a1);
-                    } else {
-                        const uint32_t s = h == 0 ? sa : sb;
-                        D = make_uint2(s, s);
-                    }
-                    if (lane == 0) {
-                        R.D[t] = D;
-                        if (flags) R.meta[t] = meta[h] | flags;
-                    }
+                    for (int q = 4; q < 8; ++q) fb = compose(fb, term_fn(e[q], iu));
+                    fa = warp_compose(fa);
+                    fb = warp_compose(fb);
+                    const Fn ft = compose(fa, fb);
+                    D = make_uint2(ft.a0, ft.a1);
+                }
+                if (lane == 0) {
+                    R.D[t] = D;
+                    if (flags) R.meta[t] = meta | flags;
                 }
             }
             work_sync();

@@ -306,6 +306,20 @@ def test_softmax_in_place_and_nan_in_wide_rows(dev):
     assert_f32(gy[keep], y_ref[keep], "softmax in place")
 
 
+def test_staged_softmax_sum_is_the_sequential_sum(dev):
+    """The shared-memory-staged path (f32, 32000 columns, many rows per CTA)
+    must also return the in-order sum: row error < 2e-6, where a tree sum of
+    the same terms misses by ~7e-5; std-12 rows cross many binades."""
+    rng = np.random.default_rng(78)
+    for std in (3.0, 12.0):
+        x = rng.standard_normal((600, 32000), dtype=np.float32) * np.float32(std)
+        y_ref = O.softmax(x, threads=8)
+        gy = to_np(T.softmax(gpu(x, dev)))
+        sync()
+        worst, _ = assert_f32(gy, y_ref, f"staged softmax std {std}")
+        assert worst < 2e-6, f"staged softmax std {std}: row error {worst:.2e}"
+
+
 def test_softmax_with_mask_and_special_rows(dev):
     nan, inf = np.float32("nan"), np.float32("inf")
     x = np.array([[1, 2, 3, 4], [0, nan, 1, 2], [-inf, -inf, -inf, -inf], [inf, 1, 2, 3],
