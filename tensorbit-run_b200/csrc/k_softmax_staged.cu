@@ -11,35 +11,34 @@
 // the in-order f32 sum of those terms, bit for bit (see ordered_sum.cuh for
 // the integer-grid argument).
 //
-// CTA = 16 warps, persistent over rows blockIdx.x, +gridDim.x, ... (one CTA
+// CTA = 24 warps, persistent over rows blockIdx.x, +gridDim.x, ... (one CTA
 // per SM at V = 32000: the row buffer is 125 KB of shared memory):
 //   warps 0,4,8 scanners: the ordered sum of every third row, from the tile
-//               summaries below (three summary buffers); each scan overlaps
-//               the workers' next row.  They share one warp scheduler.
-//   the others  workers, per row:
+//               summaries below (three summary buffers), while the workers
+//               go on.  They share one warp scheduler.
+//   6 warps     finalizers: y = e * (1/sum) of each scanned row, e recomputed
+//               from x (still in L2), streaming stores.
+//   15 warps    workers, per row:
 //     load   bulk asynchronous copies of the row in four chunks, one
 //            mbarrier each -- the copy engine keeps the row in flight, HBM
-//            is read once.  A chunk of the next row is issued as soon as
-//            the units pass below has finished with that chunk.
+//            is read once; the next row's copy is issued as soon as the
+//            units pass below is done with the buffer.
 //     max    row max over the staged row.
-//     exp    e = __expf(x - m) in place, and a float sum per 256-term tile.
+//     exp    e = ex2(...) in place, and a sum estimate per 256-term tile.
 //     est    running-sum estimate at each tile start -> predicted binade b_t;
 //            tiles likely to cross a binade (or near a power of two) get a
-//            slot: their terms and prefix arrays of grid units on grids b_t
-//            and b_t + 1, with per-term tie bits.
+//            slot: a copy of their terms for the scanner.
 //     units  per tile, the integer sum of rne(e / u_b) as a function of the
 //            running sum's parity at the tile start: (D0, D1).  Only exact
 //            ties (e/u = k + 1/2) make them differ; round-to-even then
 //            depends on the parity of the partial sum.
 //     handoff the summaries go to the row's scanner.
-//     final  y = e * (1/sum) of the row three back, e recomputed from x
-//            (still in L2), streaming stores.
 //   The scanner walks 32 tiles per step: an ordered composition scan of the
 //   (D0, D1) functions gives every tile's exact start offset; the first tile
 //   that is not in the current binade, is flagged, or crosses 2^24 units is
-//   resolved -- in a slotted tile by a ballot over the prefix array (the
-//   crossing term is one real f32 addition, the rest of the tile O(1) on the
-//   next grid), otherwise term by term (ordered_sum_tile).
+//   resolved -- in a slotted tile by prefix sums of its grid units and a
+//   ballot (the crossing term is one real f32 addition, the rest of the tile
+//   O(1) on the next grid), otherwise term by term (ordered_sum_tile).
 // Every wait is bounded (tma.cuh); a timeout raises TB_B200_FLAG_WAIT_TIMEOUT,
 // after which the CTA skips its remaining waits and copies and ends.
 #include <math.h>
@@ -51,16 +50,18 @@
 
 namespace {
 
-constexpr int kNT = 512;
+constexpr int kNT = 768;
 constexpr int kScanWarps = 3;
 constexpr int kBufs = kScanWarps;  // summary/slot buffers: row i uses i % kBufs
-constexpr int kWorkWarps = kNT / 32 - kScanWarps;
+constexpr int kFinWarps = 6;  // finalizers: the normalising pass, beside the workers
+constexpr int kFin = kFinWarps * 32;
+constexpr int kWorkWarps = kNT / 32 - kScanWarps - kFinWarps;
 constexpr int kWork = kWorkWarps * 32;
 constexpr int kTileN = 256;
 constexpr int kMaxCols = 32768;
 constexpr int kMaxTiles = kMaxCols / kTileN;
-constexpr int kChunks = 4;
-constexpr int kMaxSlots = 10;
+constexpr int kChunks = 4;  // the row arrives in four bulk copies, one mbarrier each
+constexpr int kMaxSlots = 16;
 constexpr uint64_t kStaggerNs = 7000;  // start offset of odd CTAs
 constexpr uint32_t kSat = 1u << 30;
 constexpr uint32_t kLimit = 1u << 24;
@@ -68,13 +69,10 @@ constexpr uint32_t kExact = 1u << 16;  // meta flag: sum the tile term by term
 constexpr uint32_t kNoSlot = 0xffu;
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
 
-// A slotted tile: its terms and, per grid g (binade b_t + g), the inclusive
-// prefix sums of the terms' grid units (floor for a tie) and the tie bits
-// (byte q: terms 4q .. 4q+3).
+// A slotted tile: its terms, kept for the scanner (the row buffer is
+// reused before the row is scanned).
 struct Slot {
     float e[kTileN];
-    uint32_t P[2][kTileN];
-    uint8_t tie[2][kTileN / 4];
 };
 
 // Hand-off from the workers to a row's scanner (double-buffered).
@@ -213,6 +211,55 @@ __device__ __forceinline__ void tile_terms(const Slot* s, const float* xr, float
     }
 }
 
+// Inclusive prefix sums of a slotted tile's grid units on one grid, in
+// registers: lane l holds those of terms 4l..4l+3 (pa) and 128+4l..128+4l+3
+// (pb), with their tie bits (bits 0-3, 4-7).  Terms past the row are 0.
+struct TilePrefix {
+    uint32_t pa[4], pb[4];
+    uint32_t tie;
+};
+__device__ __forceinline__ TilePrefix tile_prefix(const Slot* s, float inv_u) {
+    const int lane = threadIdx.x & 31;
+    const float4 a = *reinterpret_cast<const float4*>(s->e + 4 * lane);
+    const float4 c = *reinterpret_cast<const float4*>(s->e + 128 + 4 * lane);
+    const float e[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+    uint32_t u[8];
+    TilePrefix P;
+    P.tie = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        bool tq;
+        u[q] = units_exact(e[q], inv_u, &tq);
+        P.tie |= (uint32_t)tq << q;
+    }
+    const uint32_t ha = min(min(u[0] + u[1], kSat) + min(u[2] + u[3], kSat), kSat);
+    const uint32_t hb = min(min(u[4] + u[5], kSat) + min(u[6] + u[7], kSat), kSat);
+    const uint32_t ia = warp_incl(ha);
+    const uint32_t ib = warp_incl(hb);
+    const uint32_t tot_a = __shfl_sync(tbk::kFull, ia, 31);
+    uint32_t pa = ia - ha, pb = min(tot_a + (ib - hb), kSat);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        pa = min(pa + u[q], kSat);
+        P.pa[q] = pa;
+        pb = min(pb + u[4 + q], kSat);
+        P.pb[q] = pb;
+    }
+    return P;
+}
+// The prefix at term q (warp-uniform q in [0, 256)).
+__device__ __forceinline__ uint32_t prefix_at(const TilePrefix& P, int q) {
+    const int r = q & 3;
+    const uint32_t* v = q >= 128 ? P.pb : P.pa;
+    const uint32_t x = r == 0 ? v[0] : r == 1 ? v[1] : r == 2 ? v[2] : v[3];
+    return __shfl_sync(tbk::kFull, x, (q & 127) >> 2);
+}
+
+// Consume `tile` into the running sum, exactly.  A slotted tile on the
+// current grid: the prefix arrays of grid b (then b+1 after a crossing) find
+// each event -- the first term that is a tie or takes the sum to 2^24 units
+// -- which is one real f32 addition; the terms between events add in O(1).
+// Anything else: term by term.
 __device__ void resolve_tile(tbk::RunSum& st, const Slot* slots, int nslot, const float* xr,
                              float m, int tile, uint32_t meta, int cols) {
     const int lane = threadIdx.x & 31;
@@ -222,28 +269,30 @@ __device__ void resolve_tile(tbk::RunSum& st, const Slot* slots, int nslot, cons
     const int n = min(kTileN, cols - tile * kTileN);
     int pos = 0;
     if (s && !(meta & kExact) && st.fast && st.b == tb) {
+        int gcur = -1;
+        TilePrefix P;
         while (pos < n && !st.nan) {
             const int g = st.fast ? st.b - tb : -1;
             if (g != 0 && g != 1) break;
-            const uint32_t* P = s->P[g];
-            const uint32_t P0 = pos ? P[pos - 1] : 0u;
-            const uint4 pa = *reinterpret_cast<const uint4*>(P + 4 * lane);
-            const uint4 pb = *reinterpret_cast<const uint4*>(P + 128 + 4 * lane);
-            const uint32_t ta = s->tie[g][lane], tbt = s->tie[g][32 + lane];
-            const uint32_t va[4] = {pa.x, pa.y, pa.z, pa.w}, vb[4] = {pb.x, pb.y, pb.z, pb.w};
+            if (g != gcur) {
+                P = tile_prefix(s, tbk::inv_grid(tb + g));
+                gcur = g;
+            }
+            const uint32_t P0 = pos ? prefix_at(P, pos - 1) : 0u;
             uint32_t ea = 0, eb = 0;
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 const int ja = 4 * lane + k, jb = 128 + 4 * lane + k;
-                if (ja >= pos && ja < n && (((ta >> k) & 1u) || st.S + (va[k] - P0) >= kLimit))
+                if (ja >= pos && ja < n && (((P.tie >> k) & 1u) || st.S + (P.pa[k] - P0) >= kLimit))
                     ea |= 1u << k;
-                if (jb >= pos && jb < n && (((tbt >> k) & 1u) || st.S + (vb[k] - P0) >= kLimit))
+                if (jb >= pos && jb < n &&
+                    (((P.tie >> (4 + k)) & 1u) || st.S + (P.pb[k] - P0) >= kLimit))
                     eb |= 1u << k;
             }
             const unsigned ba = __ballot_sync(tbk::kFull, ea != 0);
             const unsigned bb = __ballot_sync(tbk::kFull, eb != 0);
             if (!ba && !bb) {
-                st.S += P[n - 1] - P0;
+                st.S += prefix_at(P, n - 1) - P0;
                 st.s = __fmul_rn((float)st.S, st.u);
                 return;
             }
@@ -255,7 +304,7 @@ __device__ void resolve_tile(tbk::RunSum& st, const Slot* slots, int nslot, cons
                 const int f = __ffs(bb) - 1;
                 j = 128 + 4 * f + __ffs(__shfl_sync(tbk::kFull, eb, f)) - 1;
             }
-            const uint32_t before = st.S + (j ? P[j - 1] - P0 : 0u);
+            const uint32_t before = st.S + (j ? prefix_at(P, j - 1) - P0 : 0u);
             st.set(__fadd_rn(__fmul_rn((float)before, st.u), s->e[j]));
             pos = j + 1;
         }
@@ -327,16 +376,15 @@ k_softmax_staged(const float* x, float* y, int rows, int cols, int nslot, unsign
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t bar_x[kChunks], bar_ready[kBufs], bar_done[kBufs];
     __shared__ float red[kWorkWarps];
-    __shared__ float row_sum[4];           // ordered sum of row i at i & 3 (scanner -> final)
-    __shared__ uint8_t slot_tile[kMaxSlots];   // the current row's slotted tiles, slot order
-    __shared__ int n_slotted;
+    __shared__ float row_sum[4];           // ordered sum of row i at i & 3 (scanner -> finalizers)
+    __shared__ float row_m[4];             // row max of row i at i & 3 (workers -> finalizers)
+    __shared__ __align__(8) uint64_t bar_fin[4];  // finalizers have read row_sum/row_m of row i
     __shared__ int abort_flag;
 
     const int ntiles = (cols + kTileN - 1) / kTileN;
-    const int xbytes = ((cols * 4 + 1023) / 1024) * 1024;
     Shared sh;
-    sh.xbuf = reinterpret_cast<float*>(smem);
-    sh.sum = reinterpret_cast<RowSummary*>(smem + xbytes);
+    sh.xbuf = reinterpret_cast<float*>(smem);  // the row buffer
+    sh.sum = reinterpret_cast<RowSummary*>(smem + (size_t)ntiles * kTileN * 4);
     sh.tsum = reinterpret_cast<float*>(sh.sum + kBufs);
     sh.slots = reinterpret_cast<Slot*>(sh.tsum + kMaxTiles);
 
@@ -349,26 +397,25 @@ k_softmax_staged(const float* x, float* y, int rows, int cols, int nslot, unsign
     volatile int* abort_v = &abort_flag;
 
     if (threadIdx.x == 0) {
-        for (int c = 0; c < kChunks; ++c) {
-            tbk::mbar_init(&bar_x[c], 1);
-        }
+        for (int c = 0; c < kChunks; ++c) tbk::mbar_init(&bar_x[c], 1);
         for (int k = 0; k < kBufs; ++k) {
             tbk::mbar_init(&bar_ready[k], 1);
             tbk::mbar_init(&bar_done[k], 1);
         }
+        for (int k = 0; k < 4; ++k) tbk::mbar_init(&bar_fin[k], kFin);
         abort_flag = 0;
         tbk::fence_mbar_init();
     }
     __syncthreads();
 
-    auto issue_chunk = [&](int i, int c) {  // one thread: chunk c of local row i into xbuf
+    auto issue_chunk = [&](int i, int c, uint64_t pol) {  // one thread: chunk c of local row i
         const float* src = x + (int64_t)((int)blockIdx.x + i * (int)gridDim.x) * cols;
         const uint32_t lo = min(rowbytes, c * cb), hi = min(rowbytes, (c + 1) * cb);
         tbk::mbar_expect_tx(&bar_x[c], hi - lo);
-        if (hi > lo)  // x stays in L2 until the final pass reads it again
+        if (hi > lo)  // x stays in L2 until the finalizers read it again
             tbk::bulk_g2s_hint(reinterpret_cast<unsigned char*>(sh.xbuf) + lo,
                                reinterpret_cast<const unsigned char*>(src) + lo, hi - lo, &bar_x[c],
-                               tbk::policy_evict_last());
+                               pol);
     };
 
     // Scanners are warps 0, 4, 8: one warp scheduler (warp id mod 4) runs
@@ -394,6 +441,56 @@ k_softmax_staged(const float* x, float* y, int rows, int cols, int nslot, unsign
         return;
     }
 
+    const int nw = warp - min(kScanWarps, (warp + 3) >> 2);  // index among the other warps
+    if (nw < kFinWarps) {
+        // ---------------- finalizers: y = e * (1/sum) of each row once it is
+        //                  scanned, x re-read from L2, while the workers
+        //                  process the following rows
+        const int ft = nw * 32 + lane;
+        const uint64_t pol = tbk::policy_evict_first();  // last use of x
+        for (int i = 0; i < nloc; ++i) {
+            wait_bar(&bar_done[i % kBufs], (uint32_t)(i / kBufs) & 1u, status, abort_v);
+            const float sum = row_sum[i & 3];
+            const float mp = row_m[i & 3];
+            tbk::mbar_arrive(&bar_fin[i & 3]);  // this thread is done with slot i & 3
+            const bool norm = sum > 0.0f;
+            const float inv = __fdiv_rn(1.0f, sum);
+            const int64_t row = (int64_t)blockIdx.x + (int64_t)i * gridDim.x;
+            const float4* xr = reinterpret_cast<const float4*>(x + row * cols);
+            float4* yr = reinterpret_cast<float4*>(y + row * cols);
+            const int nv = cols / 4;
+            constexpr int kU = 12;
+            int v = ft;
+            for (; v + (kU - 1) * kFin < nv; v += kU * kFin) {
+                float4 q[kU];
+#pragma unroll
+                for (int u = 0; u < kU; ++u) q[u] = tbk::ld_f4_hint(xr + v + u * kFin, pol);
+#pragma unroll
+                for (int u = 0; u < kU; ++u) {
+                    float4 o;
+                    o.x = expo(q[u].x, mp); o.y = expo(q[u].y, mp);
+                    o.z = expo(q[u].z, mp); o.w = expo(q[u].w, mp);
+                    if (norm) {
+                        o.x = __fmul_rn(o.x, inv); o.y = __fmul_rn(o.y, inv);
+                        o.z = __fmul_rn(o.z, inv); o.w = __fmul_rn(o.w, inv);
+                    }
+                    __stcs(yr + v + u * kFin, o);
+                }
+            }
+            for (; v < nv; v += kFin) {
+                const float4 q = tbk::ld_f4_hint(xr + v, pol);
+                float4 o;
+                o.x = expo(q.x, mp); o.y = expo(q.y, mp); o.z = expo(q.z, mp); o.w = expo(q.w, mp);
+                if (norm) {
+                    o.x = __fmul_rn(o.x, inv); o.y = __fmul_rn(o.y, inv);
+                    o.z = __fmul_rn(o.z, inv); o.w = __fmul_rn(o.w, inv);
+                }
+                __stcs(yr + v, o);
+            }
+        }
+        return;
+    }
+
     // ---------------- workers
     // Odd CTAs start half a row period later: the CTAs alternate between
     // their memory-bound and compute-bound phases instead of all hitting
@@ -403,25 +500,25 @@ k_softmax_staged(const float* x, float* y, int rows, int cols, int nslot, unsign
         while (tbk::global_ns() - t0 < kStaggerNs) {
         }
     }
-    const int ww = warp - min(kScanWarps, (warp + 3) >> 2);  // worker index 0..kWorkWarps-1
+    const int ww = nw - kFinWarps;  // worker index 0..kWorkWarps-1
     const int wt = ww * 32 + lane;
+    const uint64_t pol_last = tbk::policy_evict_last();
     if (wt == 0 && nloc > 0)
-        for (int c = 0; c < kChunks; ++c) issue_chunk(0, c);
-    float m_prev = 0.0f;  // row max of row i-1
-    for (int i = 0; i < nloc + 1; ++i) {
-        float m_row = 0.0f;
-        if (i < nloc) {
+        for (int c = 0; c < kChunks; ++c) issue_chunk(0, c, pol_last);
+    for (int i = 0; i < nloc; ++i) {
+        auto tp = [&](int t) -> float* { return sh.xbuf + (size_t)t * kTileN; };
+        {
             const int k = i % kBufs;
             RowSummary& R = sh.sum[k];
             Slot* SL = sh.slots + k * nslot;
             const uint32_t par = (uint32_t)i & 1u;
-            // ---- max
+            // ---- max (each warp waits for the chunks of its own tiles)
             float mx = -INFINITY;
             int waited = -1;
             for (int t = ww; t < ntiles; t += kWorkWarps) {
                 const int c = t / tpc;
                 for (; waited < c; ++waited) wait_bar(&bar_x[waited + 1], par, status, abort_v);
-                const float* xt = sh.xbuf + t * kTileN;
+                const float* xt = tp(t);
                 const int n = min(kTileN, cols - t * kTileN);
                 if (n == kTileN || 4 * lane < n) {
                     const float4 a = *reinterpret_cast<const float4*>(xt + 4 * lane);
@@ -440,12 +537,11 @@ k_softmax_staged(const float* x, float* y, int rows, int cols, int nslot, unsign
             float m = red[0];
 #pragma unroll
             for (int w = 1; w < kWorkWarps; ++w) m = fmaxf(m, red[w]);
-            m_row = m;
             // ---- exp in place + tile sums (full tiles unconditional; the
             //      last tile may be partial)
             const int nfull = cols / kTileN;
             for (int t = ww; t < ntiles; t += kWorkWarps) {
-                float* xt = sh.xbuf + t * kTileN;
+                float* xt = tp(t);
                 float s = 0.0f;
                 if (t < nfull) {
                     float4 a = *reinterpret_cast<float4*>(xt + 4 * lane);
@@ -473,15 +569,21 @@ k_softmax_staged(const float* x, float* y, int rows, int cols, int nslot, unsign
                 s = warp_sum_est(s);
                 if (lane == 0) sh.tsum[t] = s;
             }
-            // buffer k last held row i - kBufs: its scan must be over
+            // Buffer k last held row i - kBufs: its scan must be over.  The
+            // finalizers must have taken row i-3's sum and max: then ring slot
+            // i & 3 (row i-4) is free, and no scanner completes a phase of its
+            // done barrier (row i's, once handed off) before the finalizers have
+            // waited on the one before -- each barrier stays at most one phase
+            // ahead of its waiters.
             if (i >= kBufs)
                 wait_bar(&bar_done[k], (uint32_t)((i - kBufs) / kBufs) & 1u, status, abort_v);
+            if (i >= 3) wait_bar(&bar_fin[(i - 3) & 3], (uint32_t)((i - 3) >> 2) & 1u, status, abort_v);
             work_sync();
             // ---- tile 0's in-order sum, by the last worker warp, beside the
             //      estimate below (the row buffer still holds e)
             if (ww == kWorkWarps - 1 && lane == 0) {
                 const int n0 = min(cols, kTileN);
-                const float* e0 = sh.xbuf;
+                const float* e0 = tp(0);
                 float acc = 0.0f;
                 if (n0 == kTileN) {
 #pragma unroll 16
@@ -540,15 +642,16 @@ k_softmax_staged(const float* x, float* y, int rows, int cols, int nslot, unsign
                         ++sl;
                     }
                     R.meta[t] = ((uint32_t)bq[q] & 0xffu) | (slot << 24);
-                    if (slot != kNoSlot) slot_tile[slot] = (uint8_t)t;
                 }
-                if (lane == 31) n_slotted = (int)min(sl, (uint32_t)nslot);
-                if (lane == 0) R.m = m;
+                if (lane == 0) {
+                    R.m = m;
+                    row_m[i & 3] = m;
+                }
             }
             work_sync();
             // ---- units: (D0, D1) per tile; a slotted tile's terms go to its slot
             for (int t = ww; t < ntiles; t += kWorkWarps) {
-                const float* xt = sh.xbuf + t * kTileN;
+                const float* xt = tp(t);
                 const uint32_t meta = R.meta[t];
                 const int b = (int)(int8_t)(meta & 0xffu);
                 const uint32_t slot = meta >> 24;
@@ -608,104 +711,15 @@ k_softmax_staged(const float* x, float* y, int rows, int cols, int nslot, unsign
                 }
             }
             work_sync();
-            // the row buffer is free: the next row's copy starts now
-            if (wt == 0 && i + 1 < nloc && !*abort_v) {
-                tbk::fence_proxy_async_shared();
-                for (int c = 0; c < kChunks; ++c) issue_chunk(i + 1, c);
-            }
-            // ---- slot prefix arrays, one slotted tile per warp
-            for (int sidx = ww; sidx < n_slotted; sidx += kWorkWarps) {
-                const int t = slot_tile[sidx];
-                const uint32_t meta = R.meta[t];
-                const uint32_t slot = meta >> 24;
-                const int b = (int)(int8_t)(meta & 0xffu);
-                if (b == tbk::kNoBinade) continue;
-                Slot& S = SL[slot];
-                const int n = min(kTileN, cols - t * kTileN);
-                const bool va = 4 * lane < n, vb = 128 + 4 * lane < n;
-                float4 a = make_float4(0.f, 0.f, 0.f, 0.f), c = a;
-                if (va) a = *reinterpret_cast<const float4*>(S.e + 4 * lane);
-                if (vb) c = *reinterpret_cast<const float4*>(S.e + 128 + 4 * lane);
-                const float e[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
-#pragma unroll
-                for (int g = 0; g < 2; ++g) {
-                    const float iug = tbk::inv_grid(b + g);
-                    uint32_t u[8], tie = 0;
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        bool tq = false;
-                        u[q] = (q < 4 ? va : vb) ? units_exact(e[q], iug, &tq) : 0u;
-                        tie |= (uint32_t)tq << q;
-                    }
-                    const uint32_t ha = min(min(u[0] + u[1], kSat) + min(u[2] + u[3], kSat), kSat);
-                    const uint32_t hb = min(min(u[4] + u[5], kSat) + min(u[6] + u[7], kSat), kSat);
-                    const uint32_t ia = warp_incl(ha);
-                    const uint32_t tot_a = __shfl_sync(tbk::kFull, ia, 31);
-                    const uint32_t ib = warp_incl(hb);
-                    uint32_t pa = ia - ha, pb = min(tot_a + (ib - hb), kSat);
-                    uint4 wa, wb;
-                    pa = min(pa + u[0], kSat); wa.x = pa;
-                    pa = min(pa + u[1], kSat); wa.y = pa;
-                    pa = min(pa + u[2], kSat); wa.z = pa;
-                    pa = min(pa + u[3], kSat); wa.w = pa;
-                    pb = min(pb + u[4], kSat); wb.x = pb;
-                    pb = min(pb + u[5], kSat); wb.y = pb;
-                    pb = min(pb + u[6], kSat); wb.z = pb;
-                    pb = min(pb + u[7], kSat); wb.w = pb;
-                    *reinterpret_cast<uint4*>(S.P[g] + 4 * lane) = wa;
-                    *reinterpret_cast<uint4*>(S.P[g] + 128 + 4 * lane) = wb;
-                    S.tie[g][lane] = (uint8_t)(tie & 0xfu);
-                    S.tie[g][32 + lane] = (uint8_t)(tie >> 4);
-                }
-            }
-            work_sync();
+            // The row buffer is free: the next row's copy starts now.  The
+            // summaries are complete: hand the row to its scanner.
             if (wt == 0) {
+                if (i + 1 < nloc && !*abort_v) {
+                    tbk::fence_proxy_async_shared();
+                    for (int c = 0; c < kChunks; ++c) issue_chunk(i + 1, c, pol_last);
+                }
                 __threadfence_block();
                 tbk::mbar_arrive(&bar_ready[k]);
-            }
-        }
-        // ---- final pass of row i-1 (scanned while this row was processed;
-        //      its x is still in L2)
-        const float mp = m_prev;
-        m_prev = m_row;
-        if (i >= 1) {
-            const int ip = i - 1;
-            wait_bar(&bar_done[ip % kBufs], (uint32_t)(ip / kBufs) & 1u, status, abort_v);
-            const float sum = row_sum[ip & 3];
-            const bool norm = sum > 0.0f;
-            const float inv = __fdiv_rn(1.0f, sum);
-            const int64_t row = (int64_t)blockIdx.x + (int64_t)ip * gridDim.x;
-            const float4* xr = reinterpret_cast<const float4*>(x + row * cols);
-            float4* yr = reinterpret_cast<float4*>(y + row * cols);
-            const int nv = cols / 4;
-            constexpr int kU8 = 8;
-            const uint64_t pol = tbk::policy_evict_first();  // last use of x
-            int v = wt;
-            for (; v + (kU8 - 1) * kWork < nv; v += kU8 * kWork) {
-                float4 q[kU8];
-#pragma unroll
-                for (int u = 0; u < kU8; ++u) q[u] = tbk::ld_f4_hint(xr + v + u * kWork, pol);
-#pragma unroll
-                for (int u = 0; u < kU8; ++u) {
-                    float4 o;
-                    o.x = expo(q[u].x, mp); o.y = expo(q[u].y, mp);
-                    o.z = expo(q[u].z, mp); o.w = expo(q[u].w, mp);
-                    if (norm) {
-                        o.x = __fmul_rn(o.x, inv); o.y = __fmul_rn(o.y, inv);
-                        o.z = __fmul_rn(o.z, inv); o.w = __fmul_rn(o.w, inv);
-                    }
-                    __stcs(yr + v + u * kWork, o);
-                }
-            }
-            for (; v < nv; v += kWork) {
-                const float4 q = tbk::ld_f4_hint(xr + v, pol);
-                float4 o;
-                o.x = expo(q.x, mp); o.y = expo(q.y, mp); o.z = expo(q.z, mp); o.w = expo(q.w, mp);
-                if (norm) {
-                    o.x = __fmul_rn(o.x, inv); o.y = __fmul_rn(o.y, inv);
-                    o.z = __fmul_rn(o.z, inv); o.w = __fmul_rn(o.w, inv);
-                }
-                __stcs(yr + v, o);
             }
         }
     }
@@ -716,9 +730,9 @@ k_softmax_staged(const float* x, float* y, int rows, int cols, int nslot, unsign
             tbk::mbar_wait(&bar_x[c], (uint32_t)(nloc - 1) & 1u, status, 200000000ull);
 }
 
-size_t staged_smem(int cols, int nslot) {
-    const size_t xbytes = ((size_t)cols * 4 + 1023) / 1024 * 1024;
-    return xbytes + kBufs * sizeof(RowSummary) + kMaxTiles * sizeof(float) +
+// Shared memory besides the row buffer: summaries, tile sums, slots.
+size_t staged_fixed(int nslot) {
+    return kBufs * sizeof(RowSummary) + kMaxTiles * sizeof(float) +
            kBufs * (size_t)nslot * sizeof(Slot);
 }
 
@@ -735,11 +749,12 @@ int softmax_staged_f32(int64_t rows, int64_t cols, const float* x, float* y, cud
     DeviceState* ds = current_device_state();
     if (!ds) return TB_ERR_DEVICE;
     const int ntiles = (int)((cols + kTileN - 1) / kTileN);
+    const size_t xbytes = (size_t)ntiles * kTileN * 4;
     const size_t budget = ds->smem_optin > 1024 ? ds->smem_optin - 1024 : 0;  // static shared
     int nslot = ntiles < kMaxSlots ? ntiles : kMaxSlots;
-    while (nslot > 0 && staged_smem((int)cols, nslot) > budget) --nslot;
-    if (nslot < 2) return 1;
-    const size_t smem = staged_smem((int)cols, nslot);
+    while (nslot > 2 && xbytes + staged_fixed(nslot) > budget) --nslot;
+    if (nslot < 2 || xbytes + staged_fixed(nslot) > budget) return 1;
+    const size_t smem = xbytes + staged_fixed(nslot);
     static thread_local size_t attr_set[64];
     if (ds->device >= 0 && ds->device < 64 && attr_set[ds->device] < smem) {
         TB_CUDA_TRY(cudaFuncSetAttribute(k_softmax_staged,

@@ -109,6 +109,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return done != 0;
 }
 
+// A counter in shared memory published by one thread and polled by another.
+__device__ __forceinline__ void st_release_shared(int* p, int v) {
+    asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_addr(p)), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_shared(const int* p) {
+    int v;
+    asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_addr(p)) : "memory");
+    return v;
+}
+
 // Wait for phase `parity` of `bar` to complete, at most `limit_ns`.  On
 // timeout raise kFlagTimeout in *status and return false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* status,
