@@ -22,7 +22,8 @@
 //     load   bulk asynchronous copies of the row in four chunks, one
 //            mbarrier each -- the copy engine keeps the row in flight, HBM
 //            is read once; the next row's copy is issued as soon as the
-//            units pass below is done with the buffer.
+//            units pass below is done with the buffer, and that row is
+//            prefetched to L2 at the start of this one.
 //     max    row max over the staged row.
 //     exp    e = ex2(...) in place, and a sum estimate per 256-term tile.
 //     est    running-sum estimate at each tile start -> predicted binade b_t;
@@ -506,6 +507,11 @@ k_softmax_staged(const float* x, float* y, int rows, int cols, int nslot, unsign
     if (wt == 0 && nloc > 0)
         for (int c = 0; c < kChunks; ++c) issue_chunk(0, c, pol_last);
     for (int i = 0; i < nloc; ++i) {
+        // The next row heads for L2 while this one is worked on: its bulk
+        // copy, issued after this row's units pass, then reads L2.
+        if (wt == 0 && i + 1 < nloc && !*abort_v)
+            tbk::prefetch_l2_hint(x + ((int64_t)blockIdx.x + (int64_t)(i + 1) * gridDim.x) * cols,
+                                  rowbytes, pol_last);
         auto tp = [&](int t) -> float* { return sh.xbuf + (size_t)t * kTileN; };
         {
             const int k = i % kBufs;

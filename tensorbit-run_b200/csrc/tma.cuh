@@ -75,6 +75,16 @@ __device__ __forceinline__ void bulk_g2s_hint(void* dst_smem, const void* src_gm
         : "memory");
 }
 
+// Ask L2 to fetch `bytes` (multiple of 16; 16-byte aligned) of global
+// memory ahead of use, with an L2 cache policy.  No completion is tracked:
+// a later load or copy of the same bytes simply hits L2 if it has landed.
+__device__ __forceinline__ void prefetch_l2_hint(const void* src_gmem, uint32_t bytes,
+                                                 uint64_t policy) {
+    asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(src_gmem),
+                 "r"(bytes), "l"(policy)
+                 : "memory");
+}
+
 // 16-byte global load, not allocated in L1, with an L2 cache policy.
 __device__ __forceinline__ float4 ld_f4_hint(const float4* p, uint64_t policy) {
     float4 v;
