@@ -43,6 +43,8 @@ for _p in (ROOT, PKG):
 import workloads as W  # noqa: E402
 
 CFG = W.CONFIGS["7b"]
+E2E_BLOCKS = 8    # row blocks of the end-to-end step
+E2E_STREAMS = 3   # streams they are spread over
 METRIC = "fused layer-op HBM GB/s"
 WORKLOAD = "llama7b-prefill-4096 row ops (embedding, residual+RMSNorm, RoPE, SwiGLU, " \
            "softmax, argmax)"
@@ -54,7 +56,7 @@ WORKLOAD = "llama7b-prefill-4096 row ops (embedding, residual+RMSNorm, RoPE, Swi
 TRAFFIC_PER_ROW = {
     "embedding": (32137856 / 4096, "profiles/k_embed_llama7b-prefill-4096.md"),
     "layer_chain": (485573888 / 4096, "profiles/k_chain_llama7b-prefill-4096.md"),
-    "softmax": ((135831040 + 74903040) / 1024, "profiles/k_softmax_staged_logits-1024x32000.md"),
+    "softmax": ((192851456 + 74482944) / 1024, "profiles/k_softmax_staged_logits-1024x32000.md"),
     "argmax": (530358016 / 4096, "profiles/k_argmax_llama7b-prefill-4096.md"),
 }
 
@@ -340,7 +342,13 @@ def run_gpu(args, rank, world, local):
                   "frac": round(parts[n] / per_op_ms[n] / 1e6 / peak, 3),
                   "bytes": parts[n]} for n in names}
 
-    # end to end through the C ABI: pinned host inputs in, outputs back out
+    # End to end through the C ABI: pinned host inputs in, outputs back out,
+    # every step.  The rows are independent, so the step runs as E2E_BLOCKS
+    # row blocks spread over E2E_STREAMS streams, each block copying its own
+    # inputs in, running the four ops on its rows and copying its outputs
+    # out: one block's host-to-device copy overlaps the others' kernels and
+    # device-to-host copies (separate copy engines).  Weights (embedding
+    # table, RMSNorm gamma, RoPE table) stay resident.
     ins = ["ids", "x", "res", "q", "k", "gate", "up", "logits_s", "logits_a"]
     outs = ["emb", "h", "y", "q", "k", "act", "probs", "tok"]
     host_in = {n: torch.empty_like(t[n], device="cpu").pin_memory() for n in ins}
@@ -350,17 +358,46 @@ def run_gpu(args, rank, world, local):
                 for n in outs}
     bi = sum(host_in[n].numel() * host_in[n].element_size() for n in ins)
     bo = sum(host_out[n].numel() * host_out[n].element_size() for n in outs)
+    nb = E2E_BLOCKS if R % E2E_BLOCKS == 0 else 1
+    rb = R // nb
+    streams = [torch.cuda.Stream(device=dev) for _ in range(E2E_STREAMS)]
+
+    def dev_of(n):
+        return o[n] if n in o else t[n]
+
+    blocks = []
+    for j in range(nb):
+        lo, hi = j * rb, (j + 1) * rb
+        sl = {n: dev_of(n)[lo:hi] for n in set(ins) | set(outs)}
+        sl["pos"] = t["pos"][lo:hi]
+        ch = T.make_chain(sl["x"], sl["res"], t["gamma"], sl["h"], sl["y"], CFG.eps, sl["q"],
+                          sl["k"], sl["pos"], CFG.theta, table, sl["gate"], sl["up"], sl["act"])
+        blocks.append((lo, hi, sl, ch))
 
     def e2e_step():
-        for n in ins:
-            T.check(L.tb_b200_memcpy_h2d(T.ptr(t[n]), C.c_void_p(host_in[n].data_ptr()),
-                                         host_in[n].numel() * host_in[n].element_size(), sp), "h2d")
-        step()
-        for n in outs:
-            src = o[n] if n in o else t[n]
-            T.check(L.tb_b200_memcpy_d2h(C.c_void_p(host_out[n].data_ptr()), T.ptr(src),
-                                         host_out[n].numel() * host_out[n].element_size(), sp),
-                    "d2h")
+        main = torch.cuda.current_stream()
+        for st in streams:
+            st.wait_stream(main)
+        for j, (lo, hi, sl, ch) in enumerate(blocks):
+            st = streams[j % len(streams)]
+            ss = C.c_void_p(st.cuda_stream)
+            for n in ins:
+                hb = host_in[n][lo:hi]
+                T.check(L.tb_b200_memcpy_h2d(T.ptr(sl[n]), C.c_void_p(hb.data_ptr()),
+                                             hb.numel() * hb.element_size(), ss), "h2d")
+            T.check(L.tb_b200_embedding(T.BF16, hi - lo, c.hidden, c.vocab, T.ptr(sl["ids"]),
+                                        T.ptr(t["table"]), T.ptr(sl["emb"]), ss), "embedding")
+            T.check(L.tb_b200_layer_chain(C.byref(ch), ss), "layer_chain")
+            T.check(L.tb_b200_softmax(T.F32, hi - lo, c.vocab, T.ptr(sl["logits_s"]), None,
+                                      T.ptr(sl["probs"]), ss), "softmax")
+            T.check(L.tb_b200_argmax(T.F32, hi - lo, c.vocab, T.ptr(sl["logits_a"]),
+                                     T.ptr(sl["tok"]), ss), "argmax")
+            for n in outs:
+                hb = host_out[n][lo:hi]
+                T.check(L.tb_b200_memcpy_d2h(C.c_void_p(hb.data_ptr()), T.ptr(sl[n]),
+                                             hb.numel() * hb.element_size(), ss), "d2h")
+        for st in streams:
+            main.wait_stream(st)
 
     e2e_steps = max(3, min(args.steps, 10))
     e2e_step()
@@ -398,7 +435,9 @@ def run_gpu(args, rank, world, local):
                      "traffic_source": TRAFFIC_PER_ROW[dom][1] + " (ncu, scaled to the launch's rows)"},
         "e2e": {"value": round(total_bytes / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": bi,
-                "d2h_bytes_per_step": bo, "api": "tb_b200_* C ABI, pinned host buffers"},
+                "d2h_bytes_per_step": bo,
+                "api": f"tb_b200_* C ABI, pinned host buffers, {nb} row blocks on "
+                       f"{len(streams)} streams (copies in and out overlap the kernels)"},
         "gpu_launches": int(launches),
         "clocks": clocks.summary(),
     }
