@@ -42,12 +42,24 @@ for _p in (ROOT, PKG):
 
 import workloads as W  # noqa: E402
 
-CFG = W.CONFIGS["7b"]
+# --config: the default is the Llama-7B prefill (the headline); 70b runs
+# the Llama-70B prefill's layer ops on 16384 tokens and the bandwidth
+# sweep's widest softmax/argmax point (4096 rows of 128256 logits).
+CONFIGS = {
+    "7b": (W.CONFIGS["7b"], None, "llama7b-prefill-4096 row ops (embedding, residual+RMSNorm, "
+                                  "RoPE, SwiGLU, softmax, argmax)"),
+    "70b": (W.CONFIGS["70b"], 4096, "llama70b-prefill-16384 layer ops (embedding, residual+RMSNorm, "
+                                    "RoPE, SwiGLU) + softmax/argmax over 4096 x 128256 logits"),
+}
+CFG, LOGIT_ROWS, WORKLOAD = CONFIGS["7b"]
 E2E_BLOCKS = 8    # row blocks of the end-to-end step
 E2E_STREAMS = 3   # streams they are spread over
 METRIC = "fused layer-op HBM GB/s"
-WORKLOAD = "llama7b-prefill-4096 row ops (embedding, residual+RMSNorm, RoPE, SwiGLU, " \
-           "softmax, argmax)"
+
+
+def logit_rows(rows):
+    """Rows of the softmax/argmax logits for `rows` layer-op rows."""
+    return rows if LOGIT_ROWS is None else min(rows, LOGIT_ROWS)
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per row of each
@@ -63,13 +75,14 @@ TRAFFIC_PER_ROW = {
 
 def step_bytes(rows, act_s):
     c = CFG
+    lr = logit_rows(rows)
     parts = {
         "embedding": W.bytes_embedding(rows, c.hidden, act_s),
         "layer_chain": (W.bytes_res_rms(rows, c.hidden, act_s)
                         + W.bytes_rope(rows, c.n_q_heads, c.n_kv_heads, c.head_dim, act_s)
                         + W.bytes_swiglu(rows, c.intermediate, act_s)),
-        "softmax": W.bytes_softmax(rows, c.vocab, 4),
-        "argmax": W.bytes_argmax(rows, c.vocab, 4),
+        "softmax": W.bytes_softmax(lr, c.vocab, 4),
+        "argmax": W.bytes_argmax(lr, c.vocab, 4),
     }
     return parts
 
@@ -160,8 +173,9 @@ def cpu_sample(rows=256):
     q, k = bf(li["q"]), bf(li["k"])
     gate, up = bf(li["gate"]), bf(li["up"])
     rng = np.random.default_rng(c.seed + 7)
-    table = bf(rng.standard_normal((c.vocab, c.hidden), dtype=np.float32) * np.float32(0.02))
-    ids = rng.integers(0, c.vocab, rows).astype(np.int32)
+    vt = min(c.vocab, 32768)  # table rows of the host sample (the gather's cost is per row)
+    table = bf(rng.standard_normal((vt, c.hidden), dtype=np.float32) * np.float32(0.02))
+    ids = rng.integers(0, vt, rows).astype(np.int32)
     lg_s = W.logits(c, rows=rows)
     lg_a = W.normal(c, 10, (rows, c.vocab), std=c.logit_std)
 
@@ -231,6 +245,7 @@ def build_inputs(torch, dev, seed, rows=None):
         return (torch.randn(shape, generator=g, device=dev) * std + mean).to(dtype)
 
     R = c.rows if rows is None else rows
+    LR = logit_rows(R)
     t = {
         "table": randn((c.vocab, c.hidden), 0.02, k=7),
         "ids": torch.randint(0, c.vocab, (R,), generator=g, device=dev, dtype=torch.int32),
@@ -239,15 +254,15 @@ def build_inputs(torch, dev, seed, rows=None):
         "q": randn((R, c.n_q_heads, c.head_dim), k=3), "k": randn((R, c.n_kv_heads, c.head_dim), k=4),
         "gate": randn((R, c.intermediate), k=5), "up": randn((R, c.intermediate), k=6),
         "pos": torch.arange(R, dtype=torch.int32, device=dev),
-        "logits_s": randn((R, c.vocab), c.logit_std, dtype=torch.float32, k=9),
-        "logits_a": randn((R, c.vocab), c.logit_std, dtype=torch.float32, k=10),
+        "logits_s": randn((LR, c.vocab), c.logit_std, dtype=torch.float32, k=9),
+        "logits_a": randn((LR, c.vocab), c.logit_std, dtype=torch.float32, k=10),
     }
     o = {
         "emb": torch.empty((R, c.hidden), dtype=torch.bfloat16, device=dev),
         "h": torch.empty_like(t["x"]), "y": torch.empty_like(t["x"]),
         "act": torch.empty_like(t["gate"]),
         "probs": torch.empty_like(t["logits_s"]),
-        "tok": torch.empty(R, dtype=torch.int32, device=dev),
+        "tok": torch.empty(LR, dtype=torch.int32, device=dev),
     }
     return t, o
 
@@ -261,6 +276,7 @@ def run_gpu(args, rank, world, local):
     torch.cuda.set_device(dev)
     L = T.lib()
     R, c = args.rows, CFG
+    LR = logit_rows(R)
     t, o = build_inputs(torch, dev, 12345 + 1000 * rank, R)
     table = T.rope_table(CFG.theta, CFG.head_dim, R)
     stream = torch.cuda.current_stream()
@@ -273,9 +289,9 @@ def run_gpu(args, rank, world, local):
                                                          T.ptr(t["table"]), T.ptr(o["emb"]), sp),
                                      "embedding"),
         "layer_chain": lambda: T.check(L.tb_b200_layer_chain(C.byref(chain), sp), "layer_chain"),
-        "softmax": lambda: T.check(L.tb_b200_softmax(T.F32, R, c.vocab, T.ptr(t["logits_s"]), None,
+        "softmax": lambda: T.check(L.tb_b200_softmax(T.F32, LR, c.vocab, T.ptr(t["logits_s"]), None,
                                                      T.ptr(o["probs"]), sp), "softmax"),
-        "argmax": lambda: T.check(L.tb_b200_argmax(T.F32, R, c.vocab, T.ptr(t["logits_a"]),
+        "argmax": lambda: T.check(L.tb_b200_argmax(T.F32, LR, c.vocab, T.ptr(t["logits_a"]),
                                                    T.ptr(o["tok"]), sp), "argmax"),
     }
 
@@ -358,8 +374,9 @@ def run_gpu(args, rank, world, local):
                 for n in outs}
     bi = sum(host_in[n].numel() * host_in[n].element_size() for n in ins)
     bo = sum(host_out[n].numel() * host_out[n].element_size() for n in outs)
-    nb = E2E_BLOCKS if R % E2E_BLOCKS == 0 else 1
-    rb = R // nb
+    nb = E2E_BLOCKS if R % E2E_BLOCKS == 0 and LR % E2E_BLOCKS == 0 else 1
+    rb, lrb = R // nb, LR // nb
+    logit_names = {"logits_s", "logits_a", "probs", "tok"}  # LR rows, the rest R
     streams = [torch.cuda.Stream(device=dev) for _ in range(E2E_STREAMS)]
 
     def dev_of(n):
@@ -367,33 +384,34 @@ def run_gpu(args, rank, world, local):
 
     blocks = []
     for j in range(nb):
-        lo, hi = j * rb, (j + 1) * rb
-        sl = {n: dev_of(n)[lo:hi] for n in set(ins) | set(outs)}
-        sl["pos"] = t["pos"][lo:hi]
+        span = {n: ((j * lrb, (j + 1) * lrb) if n in logit_names else (j * rb, (j + 1) * rb))
+                for n in set(ins) | set(outs)}
+        sl = {n: dev_of(n)[a:b] for n, (a, b) in span.items()}
+        sl["pos"] = t["pos"][j * rb:(j + 1) * rb]
         ch = T.make_chain(sl["x"], sl["res"], t["gamma"], sl["h"], sl["y"], CFG.eps, sl["q"],
                           sl["k"], sl["pos"], CFG.theta, table, sl["gate"], sl["up"], sl["act"])
-        blocks.append((lo, hi, sl, ch))
+        blocks.append((span, sl, ch))
 
     def e2e_step():
         main = torch.cuda.current_stream()
         for st in streams:
             st.wait_stream(main)
-        for j, (lo, hi, sl, ch) in enumerate(blocks):
+        for j, (span, sl, ch) in enumerate(blocks):
             st = streams[j % len(streams)]
             ss = C.c_void_p(st.cuda_stream)
             for n in ins:
-                hb = host_in[n][lo:hi]
+                hb = host_in[n][span[n][0]:span[n][1]]
                 T.check(L.tb_b200_memcpy_h2d(T.ptr(sl[n]), C.c_void_p(hb.data_ptr()),
                                              hb.numel() * hb.element_size(), ss), "h2d")
-            T.check(L.tb_b200_embedding(T.BF16, hi - lo, c.hidden, c.vocab, T.ptr(sl["ids"]),
+            T.check(L.tb_b200_embedding(T.BF16, rb, c.hidden, c.vocab, T.ptr(sl["ids"]),
                                         T.ptr(t["table"]), T.ptr(sl["emb"]), ss), "embedding")
             T.check(L.tb_b200_layer_chain(C.byref(ch), ss), "layer_chain")
-            T.check(L.tb_b200_softmax(T.F32, hi - lo, c.vocab, T.ptr(sl["logits_s"]), None,
+            T.check(L.tb_b200_softmax(T.F32, lrb, c.vocab, T.ptr(sl["logits_s"]), None,
                                       T.ptr(sl["probs"]), ss), "softmax")
-            T.check(L.tb_b200_argmax(T.F32, hi - lo, c.vocab, T.ptr(sl["logits_a"]),
+            T.check(L.tb_b200_argmax(T.F32, lrb, c.vocab, T.ptr(sl["logits_a"]),
                                      T.ptr(sl["tok"]), ss), "argmax")
             for n in outs:
-                hb = host_out[n][lo:hi]
+                hb = host_out[n][span[n][0]:span[n][1]]
                 T.check(L.tb_b200_memcpy_d2h(C.c_void_p(hb.data_ptr()), T.ptr(sl[n]),
                                              hb.numel() * hb.element_size(), ss), "d2h")
         for st in streams:
@@ -421,18 +439,20 @@ def run_gpu(args, rank, world, local):
                    "heads": [c.n_q_heads, c.n_kv_heads, c.head_dim],
                    "intermediate": c.intermediate, "vocab": c.vocab,
                    "activations": "bf16 (f32 arithmetic)", "logits": "f32",
-                   "bytes_per_step_per_gpu": step_b,
-                   "l2": "inputs larger than L2: ~2.2 GB of distinct buffers per step",
+                   "logit_rows_per_gpu": LR, "bytes_per_step_per_gpu": step_b,
+                   "l2": f"inputs larger than L2: {step_b / 1e9:.1f} GB of distinct buffers per step",
                    "parallelism": f"row-sharded x{world}, no data-path collective"},
         "rows_per_s": round(R * world / (ms / 1e3), 1),
         "per_op": per_op,
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1),
                      "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
                      "frac": round(achieved / peak, 3),
-                     "traffic": (round(TRAFFIC_PER_ROW[dom][0] * R)
-                                 if TRAFFIC_PER_ROW[dom][0] else None),
+                     "traffic": (round(TRAFFIC_PER_ROW[dom][0] * (LR if dom in ("softmax", "argmax") else R))
+                                 if CFG is CONFIGS["7b"][0] else None),
                      "algorithmic_bytes": parts[dom],
-                     "traffic_source": TRAFFIC_PER_ROW[dom][1] + " (ncu, scaled to the launch's rows)"},
+                     "traffic_source": (TRAFFIC_PER_ROW[dom][1] + " (ncu, scaled to the launch's rows)"
+                                        if CFG is CONFIGS["7b"][0] else
+                                        "no ncu capture of this configuration")},
         "e2e": {"value": round(total_bytes / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": bi,
                 "d2h_bytes_per_step": bo,
@@ -454,8 +474,15 @@ def main():
     ap.add_argument("--profile-op", choices=["embedding", "layer_chain", "softmax", "argmax"],
                     help="only launch this op (warmup + steps times) on --rows rows: a small "
                          "case for ncu captures")
-    ap.add_argument("--rows", type=int, default=CFG.rows)
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="7b",
+                    help="7b (default): the Llama-7B prefill step; 70b: the Llama-70B prefill's "
+                         "layer ops and the sweep's 4096 x 128256 softmax/argmax")
+    ap.add_argument("--rows", type=int, default=None, help="layer-op rows per GPU (config's)")
     args = ap.parse_args()
+    global CFG, LOGIT_ROWS, WORKLOAD
+    CFG, LOGIT_ROWS, WORKLOAD = CONFIGS[args.config]
+    if args.rows is None:
+        args.rows = CFG.rows
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
