@@ -50,7 +50,11 @@ CONFIGS = {
                                   "RoPE, SwiGLU, softmax, argmax)"),
     "70b": (W.CONFIGS["70b"], 4096, "llama70b-prefill-16384 layer ops (embedding, residual+RMSNorm, "
                                     "RoPE, SwiGLU) + softmax/argmax over 4096 x 128256 logits"),
+    "decode": (W.CONFIGS["decode"], None, "decode 256 sequences x 1 token at the llama7b shape: the "
+                                          "fused layer chain (residual+RMSNorm, RoPE, SwiGLU) over "
+                                          "32 layers, one CUDA graph"),
 }
+DECODE_LAYERS = 32
 CFG, LOGIT_ROWS, WORKLOAD = CONFIGS["7b"]
 E2E_BLOCKS = 8    # row blocks of the end-to-end step
 E2E_STREAMS = 3   # streams they are spread over
@@ -190,9 +194,9 @@ def cpu_sample(rows=256):
     return run, sum(step_bytes(rows, 2).values()), kind, cores
 
 
-def cpu_baseline(seconds=12.0, rows=256):
+def cpu_baseline(seconds=12.0, rows=256, sample=None):
     """Reported CPU baseline: repeat the sample for about `seconds`."""
-    run, nbytes, kind, cores = cpu_sample(rows)
+    run, nbytes, kind, cores = (sample or cpu_sample)(rows)
     run()  # warm-up: page faults, thread start-up
     reps, t0 = 0, time.perf_counter()
     while True:
@@ -212,7 +216,8 @@ def run_reference(args, world):
     """--impl reference: the reference's CPU kernels on this host's cores.
     Each step is one pass of the step's ops over a 256-row sample."""
     rows = 256
-    run, nbytes, kind, cores = cpu_sample(rows)
+    run, nbytes, kind, cores = (cpu_sample_decode(rows) if CFG is CONFIGS["decode"][0]
+                                else cpu_sample(rows))
     for _ in range(args.warmup):
         run()
     times = []
@@ -233,6 +238,209 @@ def run_reference(args, world):
                                        f"median of {args.steps} steps on {cores} threads"},
             "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
+
+
+# ------------------------------------------------------------ decode config
+def decode_layer_bytes(rows, act_s):
+    c = CFG
+    return (W.bytes_res_rms(rows, c.hidden, act_s)
+            + W.bytes_rope(rows, c.n_q_heads, c.n_kv_heads, c.head_dim, act_s)
+            + W.bytes_swiglu(rows, c.intermediate, act_s))
+
+
+def cpu_sample_decode(rows=256):
+    """The decode step on the host cores through the reference's kernels:
+    the chain's ops over the batch for DECODE_LAYERS layers, each with its
+    own copy of the inputs.  Returns (run, bytes, kind, cores)."""
+    import numpy as np
+    from oracle import oracle as O
+    O.lib()
+    impl, kind = (O.REF, "reference") if O.ref_available() else (O.PORT, "port")
+    cores = os.cpu_count() or 1
+    c = CFG
+    li = W.layer_inputs(c, rows=rows)
+    bf = O.f32_to_bf16
+    one = {k: bf(li[k]) for k in ("x", "res", "gamma", "q", "k", "gate", "up")}
+    layers = [{k: np.copy(v) for k, v in one.items()} for _ in range(DECODE_LAYERS)]
+    pos = li["pos"]
+
+    def run():
+        for d in layers:
+            O.residual_rms_norm(d["x"], d["res"], d["gamma"], c.eps, impl, cores)
+            O.rope(d["q"], d["k"], pos, c.theta, impl, cores)
+            O.swiglu(d["gate"], d["up"], impl, cores)
+
+    return run, DECODE_LAYERS * decode_layer_bytes(rows, 2), kind, cores
+
+
+def run_decode(args, rank, world, local):
+    """One decode step = the fused layer chain over DECODE_LAYERS layers of
+    the batch, each layer with its own buffers (1.08 GB per step, so nothing
+    is served from L2), captured once in a CUDA graph and replayed."""
+    import torch
+    import torch.distributed as dist
+    import tb_b200 as T
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    L = T.lib()
+    R, c, NL = args.rows, CFG, DECODE_LAYERS
+    g = torch.Generator(device=dev)
+
+    def randn(shape, seed, std=1.0, mean=0.0):
+        g.manual_seed(seed)
+        return (torch.randn(shape, generator=g, device=dev) * std + mean).to(torch.bfloat16)
+
+    base = 54321 + 1000 * rank
+    g.manual_seed(base)
+    pos = torch.randint(0, 4096, (R,), generator=g, device=dev, dtype=torch.int32)
+    table = T.rope_table(c.theta, c.head_dim, 4096)
+    layers = []
+    for l in range(NL):
+        sd = base + 16 * l
+        d = {"x": randn((R, c.hidden), sd), "res": randn((R, c.hidden), sd + 1),
+             "gamma": randn((c.hidden,), sd + 2, 0.1, 1.0),
+             "q": randn((R, c.n_q_heads, c.head_dim), sd + 3),
+             "k": randn((R, c.n_kv_heads, c.head_dim), sd + 4),
+             "gate": randn((R, c.intermediate), sd + 5), "up": randn((R, c.intermediate), sd + 6)}
+        d["h"], d["y"], d["act"] = (torch.empty_like(d["x"]), torch.empty_like(d["x"]),
+                                    torch.empty_like(d["gate"]))
+        d["chain"] = T.make_chain(d["x"], d["res"], d["gamma"], d["h"], d["y"], c.eps, d["q"],
+                                  d["k"], pos, c.theta, table, d["gate"], d["up"], d["act"])
+        layers.append(d)
+    s = torch.cuda.Stream(device=dev)
+    sp = C.c_void_p(s.cuda_stream)
+
+    def eager(stream_ptr=sp):
+        for d in layers:
+            T.check(L.tb_b200_layer_chain(C.byref(d["chain"]), stream_ptr), "layer_chain")
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        x = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(x, op=dist.ReduceOp.MAX)
+        return float(x.item())
+
+    s.wait_stream(torch.cuda.current_stream())
+    eager()
+    s.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        eager()
+    with torch.cuda.stream(s):
+        for _ in range(args.warmup):
+            graph.replay()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    uuid = getattr(torch.cuda.get_device_properties(dev), "uuid", None)
+    uuid = f"GPU-{uuid}" if uuid is not None else None
+    with ClockSampler(local, uuid) as clocks:
+        with torch.cuda.stream(s):
+            e0.record(s)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(s)
+        e1.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+
+    # the same 32 launches without the graph, for the launch overhead
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ke = max(3, min(args.steps, 20))
+    a.record(s)
+    for _ in range(ke):
+        eager()
+    b.record(s)
+    b.synchronize()
+    eager_ms = max_over_ranks(a.elapsed_time(b)) / ke
+
+    # end to end: every layer's inputs copied in and outputs copied out each
+    # step, the layers spread over streams so copies overlap the kernels
+    ins, outs = ["x", "res", "q", "k", "gate", "up"], ["h", "y", "q", "k", "act"]
+    host = [{n: torch.empty_like(d[n], device="cpu").pin_memory() for n in set(ins) | set(outs)}
+            for d in layers]
+    for d, hd in zip(layers, host):
+        for n in ins:
+            hd[n].copy_(d[n])
+    bi = sum(host[0][n].numel() * host[0][n].element_size() for n in ins) * NL
+    bo = sum(host[0][n].numel() * host[0][n].element_size() for n in outs) * NL
+    streams = [torch.cuda.Stream(device=dev) for _ in range(E2E_STREAMS)]
+
+    def e2e_step():
+        main = torch.cuda.current_stream()
+        for st in streams:
+            st.wait_stream(main)
+        for l, (d, hd) in enumerate(zip(layers, host)):
+            ss = C.c_void_p(streams[l % len(streams)].cuda_stream)
+            for n in ins:
+                T.check(L.tb_b200_memcpy_h2d(T.ptr(d[n]), C.c_void_p(hd[n].data_ptr()),
+                                             hd[n].numel() * hd[n].element_size(), ss), "h2d")
+            T.check(L.tb_b200_layer_chain(C.byref(d["chain"]), ss), "layer_chain")
+            for n in outs:
+                T.check(L.tb_b200_memcpy_d2h(C.c_void_p(hd[n].data_ptr()), T.ptr(d[n]),
+                                             hd[n].numel() * hd[n].element_size(), ss), "d2h")
+        for st in streams:
+            main.wait_stream(st)
+
+    stream = torch.cuda.current_stream()
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n2 = max(3, min(args.steps, 10))
+    a.record(stream)
+    for _ in range(n2):
+        e2e_step()
+    b.record(stream)
+    b.synchronize()
+    e2e_ms = max_over_ranks(a.elapsed_time(b)) / n2
+
+    lb = decode_layer_bytes(R, 2)
+    step_b = NL * lb
+    peak, peak_kind = peaks()
+    per_launch = ms / NL
+    achieved = lb / (per_launch / 1e3) / 1e9
+    total = step_b * world
+    return {
+        "metric": METRIC, "value": round(total / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded, reference config distributions)",
+        "config": {"workload": WORKLOAD, "rows_per_gpu": R, "layers": NL, "hidden": c.hidden,
+                   "heads": [c.n_q_heads, c.n_kv_heads, c.head_dim],
+                   "intermediate": c.intermediate, "positions": "uniform [0, 4096)",
+                   "activations": "bf16 (f32 arithmetic)", "bytes_per_step_per_gpu": step_b,
+                   "l2": f"inputs larger than L2: {step_b / 1e9:.2f} GB of distinct per-layer "
+                         "buffers per step",
+                   "parallelism": f"row-sharded x{world}, no data-path collective"},
+        "rows_per_s": round(R * world / (ms / 1e3), 1),
+        "per_op": {"layer_chain": {"ms": round(per_launch, 5),
+                                   "GB/s": round(lb / per_launch / 1e6, 1),
+                                   "frac": round(lb / per_launch / 1e6 / peak, 3), "bytes": lb}},
+        "eager_ms_per_step": round(eager_ms, 4),
+        "roofline": {"bound": "hbm", "kernel": "layer_chain", "achieved": round(achieved, 1),
+                     "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
+                     "frac": round(achieved / peak, 3),
+                     "traffic": round(TRAFFIC_PER_ROW["layer_chain"][0] * R),
+                     "algorithmic_bytes": lb,
+                     "traffic_source": TRAFFIC_PER_ROW["layer_chain"][1]
+                                       + " (ncu, same row shape, scaled to the launch's rows)",
+                     "duration": "graph step time / layers (launch gaps included)"},
+        "e2e": {"value": round(total / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": bi,
+                "d2h_bytes_per_step": bo,
+                "api": f"tb_b200_* C ABI, pinned host buffers, layers on {len(streams)} streams"},
+        "gpu_launches": NL * args.steps,
+        "clocks": clocks.summary(),
+    }
 
 
 # ------------------------------------------------------------------ GPU arm
@@ -476,7 +684,8 @@ def main():
                          "case for ncu captures")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="7b",
                     help="7b (default): the Llama-7B prefill step; 70b: the Llama-70B prefill's "
-                         "layer ops and the sweep's 4096 x 128256 softmax/argmax")
+                         "layer ops and the sweep's 4096 x 128256 softmax/argmax; decode: the "
+                         "32-layer chain over a 256-sequence decode batch")
     ap.add_argument("--rows", type=int, default=None, help="layer-op rows per GPU (config's)")
     args = ap.parse_args()
     global CFG, LOGIT_ROWS, WORKLOAD
@@ -500,11 +709,12 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     try:
-        line = run_gpu(args, rank, world, local)
+        decode = args.config == "decode"
+        line = (run_decode if decode else run_gpu)(args, rank, world, local)
         if line is None:
             return
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline()
+            line["cpu_baseline"] = cpu_baseline(sample=cpu_sample_decode if decode else cpu_sample)
         if rank == 0:
             print(json.dumps(line))
     finally:
