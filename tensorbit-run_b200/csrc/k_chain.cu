@@ -14,6 +14,15 @@
 //
 // The fused path needs 16-byte-aligned rows; other shapes run the three
 // standalone kernels back to back (same results).
+//
+// Launches use programmatic dependent launch: a chain kernel may be
+// scheduled while the kernel before it in the stream drains its last wave.
+// Each CTA first waits (griddepcontrol.wait) until that kernel has
+// completed and its memory is visible, so nothing is read or written early;
+// it then lets the next kernel's launch begin (launch_dependents), which
+// happens once every CTA of this grid has started.  Over the 32 layers of a
+// decode step the launch latency of layer l + 1 overlaps the tail of
+// layer l.
 #include <string.h>
 
 #include "bodies.cuh"
@@ -59,6 +68,8 @@ template <typename T, int ITEMS>
 __global__ void __launch_bounds__(kThreads) k_chain(const __grid_constant__ ChainArgs<T> a) {
     constexpr int V = Elt<T>::kVec;
     __shared__ float red[32];
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     int64_t b = blockIdx.x;
     if (b < a.norm_blocks) {
         tbk::res_rms_body<T, V, ITEMS>(a.x, a.res, a.w, a.h, a.y, a.rows, a.hidden, a.eps, a.G, b,
@@ -117,10 +128,26 @@ int launch_fused(const TbB200LayerChain* c, const tbh::DeviceState* ds, cudaStre
     }
     const int64_t grid = a.norm_blocks + a.rope_blocks + a.ew_blocks;
     if (grid == 0) return TB_OK;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e;
     switch (items) {
-        case 1: k_chain<T, 1><<<(unsigned)grid, kThreads, 0, s>>>(a); break;
-        case 2: k_chain<T, 2><<<(unsigned)grid, kThreads, 0, s>>>(a); break;
-        default: k_chain<T, 4><<<(unsigned)grid, kThreads, 0, s>>>(a); break;
+        case 1: e = cudaLaunchKernelEx(&cfg, k_chain<T, 1>, a); break;
+        case 2: e = cudaLaunchKernelEx(&cfg, k_chain<T, 2>, a); break;
+        default: e = cudaLaunchKernelEx(&cfg, k_chain<T, 4>, a); break;
+    }
+    if (e != cudaSuccess) {
+        tbh::count_launch();
+        tbh::set_error("layer chain kernel", e);
+        return TB_ERR_DEVICE;
     }
     TB_LAUNCH_CHECK("layer chain kernel");
     return TB_OK;
