@@ -152,6 +152,19 @@ int tb_b200_softmax(int dtype, int64_t rows, int64_t cols, const void* x, const 
 int tb_b200_argmax(int dtype, int64_t rows, int64_t cols, const void* x, int32_t* out,
                    void* stream);
 
+/* Temperature sampling of each row of f32 logits [rows, cols]: the index
+ * sample_temperature (src/main.cpp:91-111) draws when its generator step
+ * yields uniforms[r] (device doubles in [0, 1), one per row -- the value
+ * std::generate_canonical<double, 53> makes of the std::mt19937 output that
+ * std::discrete_distribution consumes).  temperature <= 0 is tb_b200_argmax
+ * (uniforms unused); one column draws 0.  Rows whose weights hold a NaN draw
+ * 0, as libstdc++'s lower_bound does over such a table.  The draw is the
+ * reference's for the same u unless u lies within ~1e-15 of a cumulative
+ * boundary where CUDA's and the C library's double exp differ by an ulp. */
+int tb_b200_sample_temperature(int64_t rows, int64_t cols, const float* logits,
+                               float temperature, const double* uniforms, int32_t* out,
+                               void* stream);
+
 /* y[t] = table[ids[t]] for t < n_tokens; table [vocab, dim]; ids device
  * int32 (tb_cpu_embedding_f32, src/ops/embedding.c:4-14).  Bit-exact copy.
  * An id outside [0, vocab) zero-fills its row and raises

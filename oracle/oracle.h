@@ -83,6 +83,26 @@ int orc_rows_argmax(int impl, int dtype, int64_t rows, int64_t cols, const void*
 int orc_rows_embedding(int impl, int dtype, int64_t n_tokens, int64_t dim, const int32_t* ids,
                        const void* table, void* y, int nthreads);
 
+/* ---- temperature sampling (sampling.c) --------------------------------
+ * The reference's sample_temperature (src/main.cpp:91-111) with the draw of
+ * libstdc++'s discrete_distribution restated for a given uniform u (the
+ * generate_canonical<double, 53> value of its mt19937 step).              */
+typedef struct {
+    uint32_t s[624];
+    int i;
+} orc_mt;
+void orc_mt_seed(orc_mt* st, uint32_t seed);
+uint32_t orc_mt_next(orc_mt* st);
+double orc_canonical53(orc_mt* st);
+/* count successive canonical doubles of mt19937(seed), two outputs each. */
+void orc_uniforms(uint32_t seed, int64_t count, double* out);
+/* scratch: n doubles.  Returns the drawn index (-1 without scratch). */
+int orc_sample_temperature_u(const float* logits, int n, float temperature, double u,
+                             double* scratch);
+/* Row driver: logits f32 [rows, cols], u [rows] -> out [rows]. */
+int orc_rows_sample_temperature(int64_t rows, int64_t cols, const float* logits,
+                                float temperature, const double* u, int32_t* out, int nthreads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -20,6 +20,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 PORT_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libtbref.so")
+PIN_SAMPLING_SO = os.path.join(HERE, "_ref", "libpinsampling.so")
 
 PORT, REF = 0, 1
 F32, BF16 = 0, 2  # TbDtype codes (include/tensorbit/run/common.h:89-99)
@@ -68,6 +69,8 @@ def _declare(L: C.CDLL) -> None:
     L.orc_rms_norm_f32.argtypes = [C.c_size_t, vp, vp, vp, f32]
     L.orc_softmax_f32.argtypes = [C.c_size_t, vp, vp, vp]
     L.orc_argmax_f32.argtypes = [vp, i32]
+    L.orc_uniforms.argtypes = [C.c_uint32, i64, vp]
+    L.orc_rows_sample_temperature.argtypes = [i64, i64, vp, f32, vp, vp, i32]
 
 
 # ---------------------------------------------------------------- helpers
@@ -213,3 +216,53 @@ def softmax_vec(x, mask=None):
     y = np.empty_like(x)
     _check(lib().orc_softmax_f32(x.size, _p(x), _p(m), _p(y)), "softmax_f32")
     return y
+
+
+# ------------------------------------------------------- temperature sampling
+def uniforms(seed: int, count: int) -> np.ndarray:
+    """The first `count` generate_canonical<double, 53> values of
+    std::mt19937(seed), as the reference's discrete_distribution draws them."""
+    out = np.empty(count, dtype=np.float64)
+    lib().orc_uniforms(seed & 0xFFFFFFFF, count, _p(out))
+    return out
+
+
+def sample_temperature(logits, temperature, u, threads=1):
+    """sample_temperature (src/main.cpp:91-111) per row of f32 logits, the
+    discrete_distribution draw taken at the given uniform u[row]."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    rows, cols = logits.shape
+    u = np.ascontiguousarray(u, dtype=np.float64)
+    out = np.empty(rows, dtype=np.int32)
+    _check(lib().orc_rows_sample_temperature(rows, cols, _p(logits), temperature, _p(u), _p(out),
+                                             threads), "sample_temperature")
+    return out
+
+
+def pin_available() -> bool:
+    return os.path.exists(PIN_SAMPLING_SO)
+
+
+def _pin():
+    L = C.CDLL(PIN_SAMPLING_SO)
+    L.pin_sample_temperature_rows.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_float,
+                                              C.c_uint32, C.c_void_p]
+    L.pin_uniforms.argtypes = [C.c_uint32, C.c_int64, C.c_void_p]
+    return L
+
+
+def pin_sample_temperature(logits, temperature, seed):
+    """The same draws through libstdc++'s own mt19937 / discrete_distribution
+    (oracle/_ref/libpinsampling.so), one per row in row order."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    rows, cols = logits.shape
+    out = np.empty(rows, dtype=np.int32)
+    _pin().pin_sample_temperature_rows(_p(logits), rows, cols, temperature, seed & 0xFFFFFFFF,
+                                       _p(out))
+    return out
+
+
+def pin_uniforms(seed: int, count: int) -> np.ndarray:
+    out = np.empty(count, dtype=np.float64)
+    _pin().pin_uniforms(seed & 0xFFFFFFFF, count, _p(out))
+    return out

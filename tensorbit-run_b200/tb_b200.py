@@ -106,6 +106,7 @@ SIGNATURES = {
     "tb_b200_rope_rows": (i32, [i32, i64, i32, i32, i32, vp, vp, vp, f32, vp, i32, vp]),
     "tb_b200_rope": (i32, [i32, i32, i32, i32, vp, vp, i32, f32, vp]),
     "tb_b200_softmax": (i32, [i32, i64, i64, vp, vp, vp, vp]),
+    "tb_b200_sample_temperature": (i32, [i64, i64, vp, f32, vp, vp, vp]),
     "tb_b200_argmax": (i32, [i32, i64, i64, vp, vp, vp]),
     "tb_b200_embedding": (i32, [i32, i64, i64, i64, vp, vp, vp, vp]),
     "tb_b200_embedding_host_ids": (i32, [i32, i64, i64, i64, vp, vp, vp, vp]),
@@ -313,6 +314,19 @@ def argmax(x, out=None, stream=None):
     _dev(x, out)
     check(lib().tb_b200_argmax(dtype_code(x), rows, cols, ptr(x), ptr(out),
                                stream or cur_stream()), "argmax")
+    return out
+
+
+def sample_temperature(logits, temperature, uniforms, out=None, stream=None):
+    """Index drawn per row of f32 logits at the given uniform (float64 device
+    tensor, one per row), as the reference's sample_temperature draws it."""
+    torch = _torch()
+    rows, cols = logits.numel() // logits.shape[-1], logits.shape[-1]
+    out = torch.empty(rows, dtype=torch.int32, device=logits.device) if out is None else out
+    _dev(logits, out)
+    u = None if uniforms is None else ptr(uniforms)
+    check(lib().tb_b200_sample_temperature(rows, cols, ptr(logits), temperature, u, ptr(out),
+                                           stream or cur_stream()), "sample_temperature")
     return out
 
 

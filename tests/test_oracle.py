@@ -185,3 +185,69 @@ def test_bf16_round_to_nearest_even():
     assert back[1] == 1.0 and back[2] == np.float32(1.015625)
     assert back[0] == 1.0 and back[4] == -2.5
     assert np.isnan(O.bf16_to_f32(O.f32_to_bf16(np.array([np.nan], np.float32))))[0]
+
+
+# ------------------------------------------------------ temperature sampling
+def test_mt19937_known_answer():
+    """The C++ standard's check for mt19937: the 10000th output of a
+    default-seeded (5489) engine is 4123659995."""
+    import ctypes as C
+    L = O.lib()
+    L.orc_mt_seed.argtypes = [C.c_void_p, C.c_uint32]
+    L.orc_mt_next.argtypes = [C.c_void_p]
+    L.orc_mt_next.restype = C.c_uint32
+    st = (C.c_uint8 * (624 * 4 + 8))()
+    L.orc_mt_seed(st, 5489)
+    for _ in range(9999):
+        L.orc_mt_next(st)
+    assert L.orc_mt_next(st) == 4123659995
+
+
+def _sampling_rows():
+    rng = np.random.default_rng(5)
+    x = (rng.standard_normal((64, 1000)) * 3).astype(np.float32)
+    x[1, 0] = np.nan                 # the reference's max stays NaN
+    x[2, 500] = np.nan               # a NaN weight
+    x[3, 7] = np.inf                 # max = +inf: inf - inf
+    x[4, :] = -np.inf                # every weight NaN
+    x[5, 100:] = -np.inf             # zero weights
+    x[6, :] = 2.5                    # equal weights: cp = (i + 1) / n
+    x[7, :] = np.float32(1e30)       # one huge logit and the rest
+    x[7, 3] = np.float32(-1e30)
+    return x
+
+
+@pytest.mark.skipif(not O.pin_available(), reason="libstdc++ pin not built (no reference tree)")
+@pytest.mark.parametrize("temperature", [0.7, 1.0, 2.5, 1e-4, 1e4, 0.0, -1.0])
+def test_sampling_restatement_matches_libstdcxx(temperature):
+    """Oracle draws (restated discrete_distribution at the canonical u of its
+    own mt19937) equal libstdc++'s own mt19937 + discrete_distribution."""
+    x = _sampling_rows()
+    u = O.uniforms(99, x.shape[0])
+    assert np.array_equal(O.sample_temperature(x, temperature, u, threads=4),
+                          O.pin_sample_temperature(x, temperature, 99))
+    rng = np.random.default_rng(6)
+    big = (rng.standard_normal((32, 32000)) * 3).astype(np.float32)
+    assert np.array_equal(O.sample_temperature(big, temperature, O.uniforms(3, 32), threads=4),
+                          O.pin_sample_temperature(big, temperature, 3))
+
+
+@pytest.mark.skipif(not O.pin_available(), reason="libstdc++ pin not built (no reference tree)")
+def test_canonical_draws_match_libstdcxx():
+    for seed in (0, 1, 5489, 2**32 - 1):
+        a, b = O.uniforms(seed, 5000), O.pin_uniforms(seed, 5000)
+        assert np.array_equal(a.view(np.uint64), b.view(np.uint64))
+        assert (a >= 0).all() and (a < 1).all()
+
+
+def test_sampling_special_rows():
+    """Rows whose weights hold a NaN draw index 0 (lower_bound over a NaN
+    table); one logit draws 0 without a table; equal weights follow u."""
+    x = _sampling_rows()
+    u = np.full(x.shape[0], 0.5)
+    got = O.sample_temperature(x, 1.0, u)
+    assert got[1] == 0 and got[2] == 0 and got[3] == 0 and got[4] == 0
+    assert 0 <= got[5] < 100
+    assert got[6] == 499  # cp[i] = (i + 1) / 1000: first cp >= 0.5
+    one = O.sample_temperature(np.array([[3.0]], np.float32), 1.0, np.array([0.9]))
+    assert one[0] == 0
