@@ -165,6 +165,19 @@ int tb_b200_sample_temperature(int64_t rows, int64_t cols, const float* logits,
                                float temperature, const double* uniforms, int32_t* out,
                                void* stream);
 
+/* INT4 / INT8 weights to f32 or bf16 on the device, bit-exact with the
+ * engine's dequantisation of a .tbm layer (Model::get_weight_fp32,
+ * include/tensorbit/run/model.hpp:181-225): n weights, INT4 packed two per
+ * byte (element i in the low nibble of byte i / 2 when i is even, the high
+ * one when odd, two's complement) or INT8 one signed byte; element i scaled
+ * by scales[i / gs] (1 past n_scales), gs = group_size or n when it is 0;
+ * out = (float)q * scale, rounded to nearest even for bf16.
+ * src_dtype TB_DTYPE_INT4 / TB_DTYPE_INT8; out_dtype TB_DTYPE_F32 /
+ * TB_DTYPE_BF16; src, scales, dst device memory. */
+int tb_b200_dequant(int src_dtype, int64_t n, const void* src, const float* scales,
+                    int64_t n_scales, uint32_t group_size, int out_dtype, void* dst,
+                    void* stream);
+
 /* y[t] = table[ids[t]] for t < n_tokens; table [vocab, dim]; ids device
  * int32 (tb_cpu_embedding_f32, src/ops/embedding.c:4-14).  Bit-exact copy.
  * An id outside [0, vocab) zero-fills its row and raises

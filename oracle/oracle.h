@@ -103,6 +103,12 @@ int orc_sample_temperature_u(const float* logits, int n, float temperature, doub
 int orc_rows_sample_temperature(int64_t rows, int64_t cols, const float* logits,
                                 float temperature, const double* u, int32_t* out, int nthreads);
 
+/* ---- INT4 / INT8 weight dequantisation (dequant.c) --------------------
+ * Model::get_weight_fp32 (include/tensorbit/run/model.hpp:181-225):
+ * dtype 7 = INT8, 8 = INT4 (TbDtype).                                     */
+int orc_dequant_f32(int dtype, size_t n, const void* src, const float* scales, size_t n_scales,
+                    uint32_t group_size, float* dst);
+
 #ifdef __cplusplus
 }
 #endif

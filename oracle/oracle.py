@@ -21,6 +21,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 PORT_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libtbref.so")
 PIN_SAMPLING_SO = os.path.join(HERE, "_ref", "libpinsampling.so")
+PIN_DEQUANT_SO = os.path.join(HERE, "_ref", "libpindequant.so")
 
 PORT, REF = 0, 1
 F32, BF16 = 0, 2  # TbDtype codes (include/tensorbit/run/common.h:89-99)
@@ -71,6 +72,7 @@ def _declare(L: C.CDLL) -> None:
     L.orc_argmax_f32.argtypes = [vp, i32]
     L.orc_uniforms.argtypes = [C.c_uint32, i64, vp]
     L.orc_rows_sample_temperature.argtypes = [i64, i64, vp, f32, vp, vp, i32]
+    L.orc_dequant_f32.argtypes = [i32, C.c_size_t, vp, vp, C.c_size_t, C.c_uint32, vp]
 
 
 # ---------------------------------------------------------------- helpers
@@ -265,4 +267,37 @@ def pin_sample_temperature(logits, temperature, seed):
 def pin_uniforms(seed: int, count: int) -> np.ndarray:
     out = np.empty(count, dtype=np.float64)
     _pin().pin_uniforms(seed & 0xFFFFFFFF, count, _p(out))
+    return out
+
+
+# ----------------------------------------------------------- INT4/INT8 weights
+INT8, INT4 = 7, 8  # TbDtype codes
+
+
+def dequant(dtype: int, q, scales, group_size: int, n: int) -> np.ndarray:
+    """Model::get_weight_fp32 (include/tensorbit/run/model.hpp:181-225) on n
+    quantized weights `q` (uint8 bytes: INT4 packed two per byte, INT8 one)."""
+    q = np.ascontiguousarray(q, dtype=np.uint8)
+    scales = np.ascontiguousarray(scales, dtype=np.float32)
+    out = np.empty(n, dtype=np.float32)
+    _check(lib().orc_dequant_f32(dtype, n, _p(q), _p(scales), scales.size, group_size, _p(out)),
+           "dequant")
+    return out
+
+
+def pin_dequant_available() -> bool:
+    return os.path.exists(PIN_DEQUANT_SO)
+
+
+def pin_dequant(dtype: int, q, scales, group_size: int, rows: int, cols: int) -> np.ndarray:
+    """The reference's own Model::get_weight_fp32 on the same bytes
+    (oracle/_ref/libpindequant.so)."""
+    L = C.CDLL(PIN_DEQUANT_SO)
+    L.pin_dequant_f32.argtypes = [C.c_int, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p,
+                                  C.c_int64, C.c_uint32, C.c_void_p]
+    q = np.ascontiguousarray(q, dtype=np.uint8)
+    scales = np.ascontiguousarray(scales, dtype=np.float32)
+    out = np.empty(rows * cols, dtype=np.float32)
+    _check(L.pin_dequant_f32(dtype, rows, cols, _p(q), _p(scales), scales.size, group_size,
+                             _p(out)), "pin_dequant")
     return out

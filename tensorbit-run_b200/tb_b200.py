@@ -107,6 +107,7 @@ SIGNATURES = {
     "tb_b200_rope": (i32, [i32, i32, i32, i32, vp, vp, i32, f32, vp]),
     "tb_b200_softmax": (i32, [i32, i64, i64, vp, vp, vp, vp]),
     "tb_b200_sample_temperature": (i32, [i64, i64, vp, f32, vp, vp, vp]),
+    "tb_b200_dequant": (i32, [i32, i64, vp, vp, i64, C.c_uint32, i32, vp, vp]),
     "tb_b200_argmax": (i32, [i32, i64, i64, vp, vp, vp]),
     "tb_b200_embedding": (i32, [i32, i64, i64, i64, vp, vp, vp, vp]),
     "tb_b200_embedding_host_ids": (i32, [i32, i64, i64, i64, vp, vp, vp, vp]),
@@ -327,6 +328,20 @@ def sample_temperature(logits, temperature, uniforms, out=None, stream=None):
     u = None if uniforms is None else ptr(uniforms)
     check(lib().tb_b200_sample_temperature(rows, cols, ptr(logits), temperature, u, ptr(out),
                                            stream or cur_stream()), "sample_temperature")
+    return out
+
+
+def dequant(src_dtype, n, q, scales, group_size, out_dtype=F32, out=None, stream=None):
+    """n INT4 (src_dtype 8) / INT8 (7) weights in the uint8 device tensor q
+    to f32 or bf16 with per-group f32 scales (Model::get_weight_fp32)."""
+    torch = _torch()
+    if out is None:
+        dt = torch.float32 if out_dtype == F32 else torch.bfloat16
+        out = torch.empty(n, dtype=dt, device=q.device)
+    _dev(q, out)
+    check(lib().tb_b200_dequant(src_dtype, n, ptr(q), ptr(scales) if scales is not None else None,
+                                0 if scales is None else scales.numel(), group_size, out_dtype,
+                                ptr(out), stream or cur_stream()), "dequant")
     return out
 
 

@@ -251,3 +251,32 @@ def test_sampling_special_rows():
     assert got[6] == 499  # cp[i] = (i + 1) / 1000: first cp >= 0.5
     one = O.sample_temperature(np.array([[3.0]], np.float32), 1.0, np.array([0.9]))
     assert one[0] == 0
+
+
+# ------------------------------------------------------ INT4 / INT8 weights
+def _quant_case(dtype, rows, cols, group_size, seed):
+    rng = np.random.default_rng(seed)
+    n = rows * cols
+    nbytes = (n + 1) // 2 if dtype == O.INT4 else n
+    q = rng.integers(0, 256, nbytes, dtype=np.uint8)
+    gs = group_size if group_size > 0 else n
+    ngroups = (n + gs - 1) // gs
+    scales = (rng.standard_normal(ngroups) * 0.01).astype(np.float32)
+    return q, scales
+
+
+@pytest.mark.skipif(not O.pin_dequant_available(), reason="reference build absent")
+@pytest.mark.parametrize("dtype", [7, 8])
+@pytest.mark.parametrize("rows,cols,group_size,drop", [(64, 256, 64, 0), (33, 101, 32, 0),
+                                                       (7, 9, 0, 0), (16, 128, 128, 5),
+                                                       (3, 5, 7, 0)])
+def test_dequant_restatement_matches_reference(dtype, rows, cols, group_size, drop):
+    """Bit-exact against the reference's own Model::get_weight_fp32; `drop`
+    scales fewer than groups exercise the 1.0 default of missing scales."""
+    q, scales = _quant_case(dtype, rows, cols, group_size, rows * cols + dtype)
+    if drop:
+        scales = scales[:-drop]
+    n = rows * cols
+    want = O.pin_dequant(dtype, q, scales, group_size, rows, cols)
+    got = O.dequant(dtype, q, scales, group_size, n)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
