@@ -178,6 +178,19 @@ int tb_b200_dequant(int src_dtype, int64_t n, const void* src, const float* scal
                     int64_t n_scales, uint32_t group_size, int out_dtype, void* dst,
                     void* stream);
 
+/* y[out] = W[out, in] x[in] (+ bias), f32, one input vector: the engine's
+ * linear layers (tb_cpu_sparse_linear_f32 / tb_cpu_dense_linear_f32,
+ * src/ops/linear.c:4-53).  Sparse: one mask byte per M-group of a row
+ * ([out, in / M] bytes), bit k keeps weight g*M + k; columns past
+ * (in / M) * M are not used; nm_m >= 2 and nm_n < nm_m, else
+ * TB_ERR_INVALID_ARG.  bias may be NULL.  Summed in a different order from
+ * the reference's left-to-right chain: equal within f32 rounding. */
+int tb_b200_sparse_linear(int64_t out_features, int64_t in_features, const float* x,
+                          const float* w, const uint8_t* mask, const float* bias, float* y,
+                          int nm_n, int nm_m, void* stream);
+int tb_b200_dense_linear(int64_t out_features, int64_t in_features, const float* x,
+                         const float* w, const float* bias, float* y, void* stream);
+
 /* y[t] = table[ids[t]] for t < n_tokens; table [vocab, dim]; ids device
  * int32 (tb_cpu_embedding_f32, src/ops/embedding.c:4-14).  Bit-exact copy.
  * An id outside [0, vocab) zero-fills its row and raises

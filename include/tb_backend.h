@@ -66,6 +66,13 @@ typedef struct {
     float eps;
 } TbNormParams;
 
+/* N:M of a sparse linear layer (include/tensorbit/run/ops.h:23-26 in the
+ * engine; the CPU adapter reads it from the op's params). */
+typedef struct {
+    int nm_n;
+    int nm_m;
+} TbLinearParams;
+
 typedef struct {
     float scale;
     bool causal;

@@ -46,6 +46,10 @@ int orc_embedding_f32(const int* token_ids, int n_tokens, int embedding_dim, con
                       float* y);
 int orc_argmax_f32(const float* logits, int n);
 int orc_swiglu_f32(size_t n, const float* gate, const float* up, float* out);
+int orc_sparse_linear_f32(size_t out_features, size_t in_features, const float* x, const float* w,
+                          const uint8_t* mask, const float* bias, float* y, int nm_n, int nm_m);
+int orc_dense_linear_f32(size_t out_features, size_t in_features, const float* x, const float* w,
+                         const float* bias, float* y);
 
 /* bf16 <-> f32 (round to nearest even; NaN stays a quiet NaN). */
 uint16_t orc_f32_to_bf16(float f);

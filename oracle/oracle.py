@@ -301,3 +301,30 @@ def pin_dequant(dtype: int, q, scales, group_size: int, rows: int, cols: int) ->
     _check(L.pin_dequant_f32(dtype, rows, cols, _p(q), _p(scales), scales.size, group_size,
                              _p(out)), "pin_dequant")
     return out
+
+
+# ------------------------------------------------------------- linear (GEMV)
+def linear(x, w, mask=None, bias=None, nm_n=2, nm_m=4, impl=PORT):
+    """y = W x (+ bias): tb_cpu_sparse_linear_f32 when `mask` is given, else
+    tb_cpu_dense_linear_f32 (src/ops/linear.c:4-53); impl REF calls the
+    reference's own functions in oracle/_ref/libtbref.so."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    out_f, in_f = w.shape
+    y = np.empty(out_f, dtype=np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    if impl == REF:
+        L = C.CDLL(REF_SO)
+        sp, dn = L.tb_cpu_sparse_linear_f32, L.tb_cpu_dense_linear_f32
+    else:
+        L = lib()
+        sp, dn = L.orc_sparse_linear_f32, L.orc_dense_linear_f32
+    if mask is not None:
+        m = np.ascontiguousarray(mask, dtype=np.uint8)
+        sp.argtypes = [C.c_size_t, C.c_size_t, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                       C.c_void_p, C.c_int, C.c_int]
+        _check(sp(out_f, in_f, _p(x), _p(w), _p(m), _p(b), _p(y), nm_n, nm_m), "sparse_linear")
+    else:
+        dn.argtypes = [C.c_size_t, C.c_size_t, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
+        _check(dn(out_f, in_f, _p(x), _p(w), _p(b), _p(y)), "dense_linear")
+    return y

@@ -213,3 +213,42 @@ uint16_t orc_f32_to_bf16(float f) {
     u += 0x7fffu + lsb;
     return (uint16_t)(u >> 16);
 }
+
+/*
+ * N:M-masked and dense f32 linear (GEMV), src/ops/linear.c:4-53:
+ *   y[j] = bias[j] (or 0) + sum over kept i of x[i] * w[j][i], accumulated
+ *   left to right in f32 (gcc contracts each step into an FMA with the
+ *   reference's flags).  Sparse: in / M groups per row, one mask byte per
+ *   group, bit k (k < M) keeps weight g*M + k (linear.c:16-27); a bit past 7
+ *   never matches the byte, and columns past (in / M) * M are not used.
+ */
+int orc_sparse_linear_f32(size_t out_features, size_t in_features, const float* x, const float* w,
+                          const uint8_t* mask, const float* bias, float* y, int nm_n, int nm_m) {
+    if (!x || !w || !mask || !y) return ORC_ERR_INVALID_ARG;
+    if (nm_m < 2 || nm_n >= nm_m) return ORC_ERR_INVALID_ARG;
+    const size_t groups = in_features / (size_t)nm_m;
+    for (size_t j = 0; j < out_features; j++) {
+        float acc = bias ? bias[j] : 0.0f;
+        const float* wr = w + j * in_features;
+        const uint8_t* mr = mask + j * groups;
+        for (size_t g = 0; g < groups; g++) {
+            const uint8_t mb = mr[g];
+            for (int k = 0; k < nm_m; k++)
+                if (mb & (uint8_t)(1u << k)) acc += x[g * nm_m + k] * wr[g * nm_m + k];
+        }
+        y[j] = acc;
+    }
+    return ORC_OK;
+}
+
+int orc_dense_linear_f32(size_t out_features, size_t in_features, const float* x, const float* w,
+                         const float* bias, float* y) {
+    if (!x || !w || !y) return ORC_ERR_INVALID_ARG;
+    for (size_t j = 0; j < out_features; j++) {
+        float acc = bias ? bias[j] : 0.0f;
+        const float* wr = w + j * in_features;
+        for (size_t i = 0; i < in_features; i++) acc += x[i] * wr[i];
+        y[j] = acc;
+    }
+    return ORC_OK;
+}

@@ -66,6 +66,60 @@ static int check(int n, const TbTensor* const* ts) {
 
 /* --------------------------------------------------------------- ops */
 
+/* SPARSE_LINEAR: inputs {x, w, mask, bias}, params N:M (defaults 2:4 as in
+ * src/backend/cpu/linear.c:16-24); out = w.shape[0], in = w.shape[1].  f32
+ * vectors and weights, a U8 device mask. */
+static int b200_sparse_linear(void* output, const void** inputs, int n_inputs,
+                              const void* params) {
+    TbTensor* y = (TbTensor*)output;
+    const TbTensor* x = IN(0);
+    const TbTensor* w = IN(1);
+    const TbTensor* mask = IN(2);
+    const TbTensor* bias = IN(3);
+    if (!x || !w || !mask || !y || w->rank < 2) return TB_ERR_INVALID_ARG;
+    const TbTensor* ts[] = {y, x, w, bias};
+    int rc = check(4, ts);
+    if (rc) return rc;
+    if (x->dtype != TB_DTYPE_F32) return TB_ERR_UNSUPPORTED_DTYPE;
+    if (!is_dev(mask)) return TB_ERR_INVALID_ARG;
+    if (mask->dtype != TB_DTYPE_U8) return TB_ERR_UNSUPPORTED_DTYPE;
+    int nm_n = 2, nm_m = 4;
+    if (params) {
+        const TbLinearParams* lp = (const TbLinearParams*)params;
+        nm_n = lp->nm_n > 0 ? lp->nm_n : 2;
+        nm_m = lp->nm_m > 0 ? lp->nm_m : 4;
+    }
+    const int64_t out_f = (int64_t)w->shape[0], in_f = (int64_t)w->shape[1];
+    if (nelem(x) < in_f || nelem(y) < out_f || (bias && nelem(bias) < out_f) ||
+        (nm_m >= 2 && nelem(mask) < out_f * (in_f / nm_m)))
+        return TB_ERR_INVALID_SHAPE;
+    return tb_b200_sparse_linear(out_f, in_f, (const float*)x->data, (const float*)w->data,
+                                 (const uint8_t*)mask->data,
+                                 bias ? (const float*)bias->data : NULL, (float*)y->data, nm_n,
+                                 nm_m, NULL);
+}
+
+/* DENSE_LINEAR: inputs {x, w, bias}; out = nelem(y) (the CPU adapter's rule
+ * for tied embeddings, src/backend/cpu/linear.c:38-44), in = w.shape[1]. */
+static int b200_dense_linear(void* output, const void** inputs, int n_inputs,
+                             const void* params) {
+    (void)params;
+    TbTensor* y = (TbTensor*)output;
+    const TbTensor* x = IN(0);
+    const TbTensor* w = IN(1);
+    const TbTensor* bias = IN(2);
+    if (!x || !w || !y || w->rank < 2) return TB_ERR_INVALID_ARG;
+    const TbTensor* ts[] = {y, x, w, bias};
+    int rc = check(4, ts);
+    if (rc) return rc;
+    if (x->dtype != TB_DTYPE_F32) return TB_ERR_UNSUPPORTED_DTYPE;
+    const int64_t out_f = nelem(y), in_f = (int64_t)w->shape[1];
+    if (nelem(x) < in_f || out_f > (int64_t)w->shape[0] || (bias && nelem(bias) < out_f))
+        return TB_ERR_INVALID_SHAPE;
+    return tb_b200_dense_linear(out_f, in_f, (const float*)x->data, (const float*)w->data,
+                                bias ? (const float*)bias->data : NULL, (float*)y->data, NULL);
+}
+
 /* RMS_NORM: inputs {x, weight}, params TbNormParams (eps defaults to 1e-6f
  * as in src/backend/cpu/norm.c:6). */
 static int b200_rms_norm(void* output, const void** inputs, int n_inputs, const void* params) {
@@ -429,6 +483,8 @@ int tb_backend_b200_init(void) {
     memset(&be, 0, sizeof be);
     be.name = "b200";
     be.priority = 200;
+    be.ops[TB_OP_SPARSE_LINEAR] = b200_sparse_linear;
+    be.ops[TB_OP_DENSE_LINEAR] = b200_dense_linear;
     be.ops[TB_OP_RMS_NORM] = b200_rms_norm;
     be.ops[TB_OP_RESIDUAL_ADD] = b200_residual_add;
     be.ops[TB_OP_GELU] = b200_gelu;

@@ -108,6 +108,8 @@ SIGNATURES = {
     "tb_b200_softmax": (i32, [i32, i64, i64, vp, vp, vp, vp]),
     "tb_b200_sample_temperature": (i32, [i64, i64, vp, f32, vp, vp, vp]),
     "tb_b200_dequant": (i32, [i32, i64, vp, vp, i64, C.c_uint32, i32, vp, vp]),
+    "tb_b200_sparse_linear": (i32, [i64, i64, vp, vp, vp, vp, vp, i32, i32, vp]),
+    "tb_b200_dense_linear": (i32, [i64, i64, vp, vp, vp, vp, vp]),
     "tb_b200_argmax": (i32, [i32, i64, i64, vp, vp, vp]),
     "tb_b200_embedding": (i32, [i32, i64, i64, i64, vp, vp, vp, vp]),
     "tb_b200_embedding_host_ids": (i32, [i32, i64, i64, i64, vp, vp, vp, vp]),
@@ -343,6 +345,24 @@ def dequant(src_dtype, n, q, scales, group_size, out_dtype=F32, out=None, stream
                                 0 if scales is None else scales.numel(), group_size, out_dtype,
                                 ptr(out), stream or cur_stream()), "dequant")
     return out
+
+
+def linear(x, w, mask=None, bias=None, nm_n=2, nm_m=4, y=None, stream=None):
+    """y = W x (+ bias) for an f32 vector x: N:M-masked when `mask` (uint8,
+    one byte per M-group of a row) is given, else dense."""
+    torch = _torch()
+    out_f, in_f = w.shape
+    y = torch.empty(out_f, dtype=torch.float32, device=w.device) if y is None else y
+    _dev(x, w, y)
+    b = ptr(bias) if bias is not None else None
+    if mask is not None:
+        rc = lib().tb_b200_sparse_linear(out_f, in_f, ptr(x), ptr(w), ptr(mask), b, ptr(y), nm_n,
+                                         nm_m, stream or cur_stream())
+    else:
+        rc = lib().tb_b200_dense_linear(out_f, in_f, ptr(x), ptr(w), b, ptr(y),
+                                        stream or cur_stream())
+    check(rc, "linear")
+    return y
 
 
 def embedding(ids, table, y=None, stream=None):

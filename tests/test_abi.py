@@ -217,7 +217,8 @@ def test_b200_backend_registers_for_cuda_and_rejects_host_tensors(registry):
     assert be.name == b"b200" and be.priority == 200
     filled = {op for op, v in T.OP.items() if op != "COUNT" and be.ops[v]}
     assert filled == {"RMS_NORM", "RESIDUAL_ADD", "GELU", "SILU", "SOFTMAX", "ROPE", "EMBEDDING",
-                      "RESIDUAL_RMS_NORM", "SWIGLU", "ARGMAX", "ROPE_ROWS", "LAYER_CHAIN"}
+                      "RESIDUAL_RMS_NORM", "SWIGLU", "ARGMAX", "ROPE_ROWS", "LAYER_CHAIN",
+                      "SPARSE_LINEAR", "DENSE_LINEAR"}
     a = np.zeros(16, np.float32)
     host = T.TbTensor(data=a.ctypes.data, rank=1, dtype=T.F32, device=T.DEVICE_CPU)
     host.shape[0] = 16

@@ -280,3 +280,29 @@ def test_dequant_restatement_matches_reference(dtype, rows, cols, group_size, dr
     want = O.pin_dequant(dtype, q, scales, group_size, rows, cols)
     got = O.dequant(dtype, q, scales, group_size, n)
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+# ------------------------------------------------------------- linear (GEMV)
+def nm_mask(rng, out_f, in_f, n, m):
+    """One byte per M-group with exactly n of the low m bits set."""
+    groups = in_f // m
+    bits = np.zeros((out_f, groups), np.uint8)
+    for k in range(n):
+        pick = rng.integers(0, m, (out_f, groups))
+        bits |= (1 << pick).astype(np.uint8)
+    return bits
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="reference build absent")
+@pytest.mark.parametrize("out_f,in_f,n,m,with_bias", [(256, 1024, 2, 4, True), (100, 37, 2, 4, False),
+                                                      (64, 4096, 1, 8, True), (33, 64, 3, 4, False)])
+def test_linear_restatement_matches_reference(out_f, in_f, n, m, with_bias):
+    rng = np.random.default_rng(out_f + in_f)
+    x = rng.standard_normal(in_f).astype(np.float32)
+    w = rng.standard_normal((out_f, in_f)).astype(np.float32)
+    b = rng.standard_normal(out_f).astype(np.float32) if with_bias else None
+    mask = nm_mask(rng, out_f, in_f, n, m)
+    for msk in (mask, None):
+        got = O.linear(x, w, msk, b, n, m, O.PORT)
+        want = O.linear(x, w, msk, b, n, m, O.REF)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
