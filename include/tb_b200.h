@@ -83,6 +83,7 @@ int tb_b200_is_device_ptr(const void* p, int* is_device);
 int tb_b200_check_status(void* stream, unsigned int* flags_out);
 #define TB_B200_FLAG_TOKEN_RANGE 0x1u   /* embedding: id < 0 or id >= vocab */
 #define TB_B200_FLAG_WAIT_TIMEOUT 0x2u  /* a kernel's bounded wait gave up (its output is invalid) */
+#define TB_B200_FLAG_POSITION_RANGE 0x4u /* decode attention: position outside [0, max_seq) */
 
 /* ======================================================================
  * Row kernels
@@ -259,6 +260,104 @@ typedef struct {
 } TbB200LayerChain;
 
 int tb_b200_layer_chain(const TbB200LayerChain* chain, void* stream);
+
+/* ======================================================================
+ * Decoder forward on the device (TransformerRunner)
+ * ====================================================================== */
+
+/* Attention row layouts of tb_b200_decode_attention / the runner. */
+#define TB_B200_ATTN_REFERENCE 0 /* the rows the reference's runner passes on */
+#define TB_B200_ATTN_STANDARD 1  /* query row `position` of every head */
+
+/* Single-token attention over one layer's KV cache (the attention step of
+ * TransformerRunner::forward, include/tensorbit/run/ops.hpp:162-204, over
+ * tb_cpu_scaled_dot_product_f32, src/ops/attention.c:5-69), f32.
+ *   position  device int32: the token's position p, in [0, max_seq);
+ *   q [n_heads * head_dim], k/v [n_kv_heads * head_dim]: the token's
+ *             projections after RoPE; k and v are also written to cache row p;
+ *   k_cache/v_cache [max_seq, n_kv_heads * head_dim]: rows 0 .. p-1 hold the
+ *             earlier tokens';
+ *   out [n_heads * head_dim].
+ * Scale 1/sqrtf(head_dim).  TB_B200_ATTN_REFERENCE: out holds the first
+ * n_heads * head_dim floats of the reference's [n_heads, p+1, head_dim]
+ * causal attention over q repeated p+1 times -- row r is head r / (p+1)
+ * attending keys 0 .. r % (p+1).  TB_B200_ATTN_STANDARD: row h is head h
+ * attending keys 0 .. p.  Query head h reads k/v head h / (n_heads /
+ * n_kv_heads).  head_dim <= 256; a position outside [0, max_seq) writes
+ * nothing and raises TB_B200_FLAG_POSITION_RANGE. */
+int tb_b200_decode_attention(int mode, int n_heads, int n_kv_heads, int head_dim, int max_seq,
+                             const int32_t* position, const float* q, const float* k,
+                             const float* v, float* k_cache, float* v_cache, float* out,
+                             void* stream);
+
+/* One weight tensor of a model, as the reference's Model hands it out
+ * (Model::get_weights / get_mask / get_scales, include/tensorbit/run/
+ * model.hpp:154-177).  data: [rows, cols] in host or device memory (the
+ * runner copies host data to the device); NULL means the tensor is absent.
+ * dtype TB_DTYPE_F32, TB_DTYPE_INT8 or TB_DTYPE_INT4 (dequantised once to
+ * f32 on the device, as Model::get_weight_fp32 does per use, model.hpp:
+ * 181-225).  mask: rows * (cols / 4) bytes of 2:4 groups, NULL for a dense
+ * projection. */
+typedef struct {
+    const void* data;
+    int dtype;
+    int64_t rows;
+    int64_t cols;
+    const uint8_t* mask;
+    const float* scales;
+    int64_t n_scales;
+    uint32_t group_size;
+} TbB200Weight;
+
+/* One decoder layer: the tensors ops.hpp:97-105 looks up.  A layer without
+ * q, k or v is skipped (ops.hpp:109); without o, no attention output
+ * projection; without gate or up, no MLP; without down, no MLP residual.
+ * Norm weights: [hidden] f32, NULL for none. */
+typedef struct {
+    TbB200Weight q, k, v, o, gate, up, down;
+    const float* input_norm;
+    const float* post_norm;
+} TbB200RunnerLayer;
+
+/* A model for the device runner: TransformerRunner's normalised config
+ * (ops.hpp:291-323, every field given) and its tensors. */
+typedef struct {
+    int hidden, n_heads, n_kv_heads, head_dim, intermediate, vocab, max_seq, layers;
+    float norm_eps;
+    float rope_theta;
+    int attention;                  /* TB_B200_ATTN_REFERENCE or _STANDARD */
+    int use_graph;                  /* nonzero: replay each token as one CUDA graph */
+    TbB200Weight embed;             /* [vocab, hidden] */
+    const float* final_norm;        /* [hidden] or NULL */
+    TbB200Weight lm_head;           /* [vocab, hidden]; data NULL: the embedding table */
+    const TbB200RunnerLayer* layer; /* [layers] */
+} TbB200RunnerDesc;
+
+/* TransformerRunner on the device (include/tensorbit/run/ops.hpp:33-288):
+ * weights, activations and the KV cache live in HBM; each forward runs the
+ * token's whole decoder step on the runner's own stream.  The norms cover
+ * `hidden` floats (the reference normalises its max(hidden, vocab) state
+ * vector, reading past the hidden-sized norm weights when vocab > hidden).
+ * create: uploads / dequantises what is not already f32 on the device
+ * (borrowed device tensors must outlive the runner), allocates the cache,
+ * builds the RoPE table with the host C library. */
+int tb_b200_runner_create(const TbB200RunnerDesc* desc, void** runner);
+/* Run one token at the next position; *logits_dev (optional) receives the
+ * runner's device logits [vocab], valid until the next forward.  A token
+ * outside [0, vocab) returns TB_ERR_INVALID_ARG and a full cache (max_seq
+ * positions used) TB_ERR_INVALID_SHAPE, both with nothing queued.
+ * Asynchronous: the runner's stream orders later calls. */
+int tb_b200_runner_forward(void* runner, int32_t token, const float** logits_dev);
+/* Copy the last logits to host memory (synchronises the runner's stream). */
+int tb_b200_runner_logits(void* runner, float* logits_host);
+/* Start a new sequence at position 0 (TransformerRunner::reset, ops.hpp:52). */
+int tb_b200_runner_reset(void* runner);
+int tb_b200_runner_position(void* runner, int* position);
+/* The runner's stream (cudaStream_t), for callers that order work after it. */
+int tb_b200_runner_stream(void* runner, void** stream);
+/* Kernels one forward launches (the graph's nodes when use_graph is set). */
+int tb_b200_runner_launches_per_token(void* runner, int* launches);
+int tb_b200_runner_destroy(void* runner);
 
 /* ======================================================================
  * Multi-GPU (one process per GPU)

@@ -113,6 +113,37 @@ int orc_rows_sample_temperature(int64_t rows, int64_t cols, const float* logits,
 int orc_dequant_f32(int dtype, size_t n, const void* src, const float* scales, size_t n_scales,
                     uint32_t group_size, float* dst);
 
+/* ---- single-token decoder forward (runner.c) ---------------------------
+ * TransformerRunner::forward (include/tensorbit/run/ops.hpp:79-288) over f32
+ * weights.  A projection with a mask runs as 2:4 groups, without one dense.
+ * Norm weights may be NULL (no scaling); lm_head NULL uses the embedding
+ * table (tied weights).  logits: [n_tokens, vocab], the logits after each
+ * token, positions 0 .. n_tokens-1 from a fresh state.                    */
+enum { ORC_ATTN_REFERENCE = 0, ORC_ATTN_STANDARD = 1 };
+typedef struct {
+    const float* w;      /* [rows, cols] f32, NULL: absent */
+    const uint8_t* mask; /* rows * (cols / 4) bytes, NULL: dense */
+    int64_t rows, cols;
+} orc_lin;
+typedef struct {
+    orc_lin q, k, v, o, gate, up, down;
+    const float* in_norm;
+    const float* post_norm;
+} orc_layer;
+typedef struct {
+    const float* embed;      /* [vocab, hidden] */
+    const float* final_norm; /* [hidden] or NULL */
+    const float* lm_head;    /* [vocab, hidden] or NULL */
+    const orc_layer* layers; /* [layers] */
+} orc_model;
+typedef struct {
+    int hidden, n_heads, n_kv_heads, head_dim, intermediate, vocab, max_seq, layers;
+    float norm_eps, rope_theta;
+    int attention; /* ORC_ATTN_REFERENCE / ORC_ATTN_STANDARD */
+} orc_runner_cfg;
+int orc_runner_run(const orc_runner_cfg* cfg, const orc_model* model, int n_tokens,
+                   const int32_t* tokens, float* logits);
+
 #ifdef __cplusplus
 }
 #endif

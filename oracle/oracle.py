@@ -328,3 +328,83 @@ def linear(x, w, mask=None, bias=None, nm_n=2, nm_m=4, impl=PORT):
         dn.argtypes = [C.c_size_t, C.c_size_t, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
         _check(dn(out_f, in_f, _p(x), _p(w), _p(b), _p(y)), "dense_linear")
     return y
+
+
+# ------------------------------------------------- decoder forward (runner)
+PIN_RUNNER_SO = os.path.join(HERE, "_ref", "libpinrunner.so")
+ATTN_REFERENCE, ATTN_STANDARD = 0, 1
+PROJECTIONS = ("q", "k", "v", "o", "gate", "up", "down")
+CFG_FIELDS = ("hidden", "n_heads", "n_kv_heads", "head_dim", "intermediate", "vocab", "max_seq",
+              "layers")
+
+
+class _Lin(C.Structure):
+    _fields_ = [("w", C.c_void_p), ("mask", C.c_void_p), ("rows", C.c_int64),
+                ("cols", C.c_int64)]
+
+
+class _Layer(C.Structure):
+    _fields_ = [(n, _Lin) for n in PROJECTIONS] + [("in_norm", C.c_void_p),
+                                                   ("post_norm", C.c_void_p)]
+
+
+class _Model(C.Structure):
+    _fields_ = [("embed", C.c_void_p), ("final_norm", C.c_void_p), ("lm_head", C.c_void_p),
+                ("layers", C.POINTER(_Layer))]
+
+
+class _Cfg(C.Structure):
+    _fields_ = [(n, C.c_int) for n in CFG_FIELDS] + [("norm_eps", C.c_float),
+                                                     ("rope_theta", C.c_float),
+                                                     ("attention", C.c_int)]
+
+
+def _runner_args(cfg: dict, model: dict):
+    """ctypes views of a model dict: {"embed", "final_norm", "lm_head",
+    "layers": [{"q": (w, mask or None), ..., "in_norm", "post_norm"}]} with
+    f32 numpy weights; keeps the arrays alive in the returned tuple."""
+    keep = []
+
+    def arr(a, dt=np.float32):
+        if a is None:
+            return None
+        a = np.ascontiguousarray(a, dtype=dt)
+        keep.append(a)
+        return a.ctypes.data
+
+    layers = (_Layer * max(1, len(model["layers"])))()
+    for i, ly in enumerate(model["layers"]):
+        for n in PROJECTIONS:
+            w, m = ly.get(n, (None, None))
+            if w is not None:
+                setattr(layers[i], n, _Lin(arr(w), arr(m, np.uint8), w.shape[0], w.shape[1]))
+        layers[i].in_norm = arr(ly.get("in_norm"))
+        layers[i].post_norm = arr(ly.get("post_norm"))
+    m = _Model(arr(model["embed"]), arr(model.get("final_norm")), arr(model.get("lm_head")),
+               layers)
+    c = _Cfg(*[int(cfg[n]) for n in CFG_FIELDS], float(cfg.get("norm_eps", 1e-5)),
+             float(cfg.get("rope_theta", 10000.0)), int(cfg.get("attention", ATTN_REFERENCE)))
+    return c, m, (keep, layers)
+
+
+def runner_run(cfg: dict, model: dict, tokens, impl=PORT) -> np.ndarray:
+    """Logits [len(tokens), vocab] after each token of a fresh decoder
+    (TransformerRunner::forward, include/tensorbit/run/ops.hpp:79-288):
+    impl PORT is oracle/runner.c, REF the reference's own runner
+    (oracle/_ref/libpinrunner.so)."""
+    c, m, keep = _runner_args(cfg, model)
+    toks = np.ascontiguousarray(tokens, dtype=np.int32)
+    out = np.empty((toks.size, int(cfg["vocab"])), dtype=np.float32)
+    if impl == REF:
+        L = C.CDLL(PIN_RUNNER_SO)
+        fn = L.pin_runner_run
+    else:
+        fn = lib().orc_runner_run
+    fn.argtypes = [C.POINTER(_Cfg), C.POINTER(_Model), C.c_int, C.c_void_p, C.c_void_p]
+    _check(fn(C.byref(c), C.byref(m), toks.size, _p(toks), _p(out)), "runner")
+    del keep
+    return out
+
+
+def pin_runner_available() -> bool:
+    return os.path.exists(PIN_RUNNER_SO)

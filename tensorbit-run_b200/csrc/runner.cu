@@ -1,0 +1,401 @@
+// runner.cu -- the engine's single-token decoder forward on the device
+// (tensorbit::run::TransformerRunner, include/tensorbit/run/ops.hpp:33-288).
+//
+// Per token, on the runner's own stream (ops.hpp line numbers):
+//   embedding gather of the token from the device copy of its id      :92
+//   per layer whose q/k/v exist (:109):
+//     x = rms_norm(x) * input_norm, in place                           :119
+//     q, k, v = W x (2:4 sparse GEMV over the mask, or dense)          :140-149
+//     RoPE of q and k at the device position (host-built table)        :159
+//     decode attention: append k/v to the cache, attend (one launch)   :162-204
+//     x = x + Wo attn (the GEMV's epilogue adds the residual)          :207-218
+//     x_mlp = rms_norm(x) * post_norm                                  :221-223
+//     g = silu(Wg x_mlp) * (Wu x_mlp); x = x + Wd g                    :226-256
+//   x = rms_norm(x) * final_norm; logits = Wlm x                       :260-281
+//   position += 1 on the device                                        :284
+// The position and the token id live in device memory, so the whole step
+// is captured once as a CUDA graph and replayed for every token
+// (use_graph); eager launches otherwise.  Weights stay resident: f32 device
+// tensors are borrowed, host tensors copied once, INT4/INT8 tensors
+// dequantised once with tb_b200_dequant (the reference dequantises on every
+// use, to the same values).
+#include <cmath>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "tb_internal.h"
+
+namespace tbh {
+int decode_attention_setup(int head_dim, int max_seq);
+}
+
+namespace {
+
+__global__ void k_advance(int32_t* pos) { *pos += 1; }
+
+struct Proj {
+    const float* w = nullptr;
+    const uint8_t* mask = nullptr;
+    int64_t rows = 0, cols = 0;
+};
+
+struct Layer {
+    Proj q, k, v, o, gate, up, down;
+    const float* in_norm = nullptr;
+    const float* post_norm = nullptr;
+};
+
+struct Runner {
+    TbB200RunnerDesc cfg{};
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::vector<void*> owned;  // device allocations
+    const float* embed = nullptr;
+    const float* final_norm = nullptr;
+    const float* lm_head = nullptr;
+    std::vector<Layer> layers;
+    float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr;
+    float *xm = nullptr, *g = nullptr, *u = nullptr, *logits = nullptr;
+    float *kc = nullptr, *vc = nullptr, *rope = nullptr;
+    int32_t* dstate = nullptr;  // [0] position, [1] token
+    int pos = 0;
+    int launches = 0;
+    cudaGraphExec_t exec = nullptr;
+    cudaGraph_t graph = nullptr;
+};
+
+int dev_alloc(Runner* r, size_t bytes, void** p) {
+    TB_CUDA_TRY(cudaMalloc(p, bytes ? bytes : 16));
+    r->owned.push_back(*p);
+    return TB_OK;
+}
+
+// An f32 device copy of a weight tensor (borrowed when it already is one).
+int materialize(Runner* r, const TbB200Weight& w, const float** out) {
+    *out = nullptr;
+    if (!w.data) return TB_OK;
+    if (w.rows <= 0 || w.cols < 0) return TB_ERR_INVALID_SHAPE;
+    const int64_t n = w.cols ? w.rows * w.cols : w.rows;
+    int on_dev = 0;
+    tb_b200_is_device_ptr(w.data, &on_dev);
+    if (w.dtype == TB_DTYPE_F32) {
+        if (on_dev) {
+            *out = static_cast<const float*>(w.data);
+            return TB_OK;
+        }
+        void* d = nullptr;
+        int rc = dev_alloc(r, (size_t)n * 4, &d);
+        if (rc) return rc;
+        TB_CUDA_TRY(cudaMemcpyAsync(d, w.data, (size_t)n * 4, cudaMemcpyHostToDevice, r->stream));
+        *out = static_cast<const float*>(d);
+        return TB_OK;
+    }
+    if (w.dtype != TB_DTYPE_INT4 && w.dtype != TB_DTYPE_INT8) return TB_ERR_UNSUPPORTED_DTYPE;
+    const size_t qbytes = w.dtype == TB_DTYPE_INT4 ? (size_t)(n + 1) / 2 : (size_t)n;
+    const void* src = w.data;
+    const float* sc = w.scales;
+    if (!on_dev) {
+        void* d = nullptr;
+        int rc = dev_alloc(r, qbytes, &d);
+        if (rc) return rc;
+        TB_CUDA_TRY(cudaMemcpyAsync(d, w.data, qbytes, cudaMemcpyHostToDevice, r->stream));
+        src = d;
+    }
+    int sc_dev = 0;
+    tb_b200_is_device_ptr(w.scales, &sc_dev);
+    if (w.n_scales > 0 && w.scales && !sc_dev) {
+        void* d = nullptr;
+        int rc = dev_alloc(r, (size_t)w.n_scales * 4, &d);
+        if (rc) return rc;
+        TB_CUDA_TRY(cudaMemcpyAsync(d, w.scales, (size_t)w.n_scales * 4, cudaMemcpyHostToDevice,
+                                    r->stream));
+        sc = static_cast<const float*>(d);
+    }
+    void* d = nullptr;
+    int rc = dev_alloc(r, (size_t)n * 4, &d);
+    if (rc) return rc;
+    rc = tb_b200_dequant(w.dtype, n, src, sc, w.n_scales, w.group_size, TB_DTYPE_F32, d, r->stream);
+    if (rc) return rc;
+    *out = static_cast<const float*>(d);
+    return TB_OK;
+}
+
+int materialize_vec(Runner* r, const float* p, int64_t n, const float** out) {
+    TbB200Weight w{};
+    w.data = p;
+    w.dtype = TB_DTYPE_F32;
+    w.rows = n;
+    w.cols = 0;
+    return materialize(r, w, out);
+}
+
+int materialize_mask(Runner* r, const TbB200Weight& w, const uint8_t** out) {
+    *out = nullptr;
+    if (!w.data || !w.mask) return TB_OK;
+    int on_dev = 0;
+    tb_b200_is_device_ptr(w.mask, &on_dev);
+    if (on_dev) {
+        *out = w.mask;
+        return TB_OK;
+    }
+    const size_t bytes = (size_t)w.rows * (size_t)(w.cols / 4);
+    void* d = nullptr;
+    int rc = dev_alloc(r, bytes, &d);
+    if (rc) return rc;
+    TB_CUDA_TRY(cudaMemcpyAsync(d, w.mask, bytes, cudaMemcpyHostToDevice, r->stream));
+    *out = static_cast<const uint8_t*>(d);
+    return TB_OK;
+}
+
+int make_proj(Runner* r, const TbB200Weight& w, int64_t rows, int64_t cols, Proj* p) {
+    *p = Proj{};
+    if (!w.data) return TB_OK;
+    if (w.rows != rows || w.cols != cols) return TB_ERR_INVALID_SHAPE;
+    int rc = materialize(r, w, &p->w);
+    if (rc) return rc;
+    rc = materialize_mask(r, w, &p->mask);
+    if (rc) return rc;
+    p->rows = rows;
+    p->cols = cols;
+    return TB_OK;
+}
+
+// y = W x, plus `res` (which may be y itself) when given.
+int project(Runner* r, const Proj& p, const float* x, const float* res, float* y) {
+    r->launches++;
+    if (p.mask)  // the runner's projections run as 2:4 groups (registry.c:93)
+        return tb_b200_sparse_linear(p.rows, p.cols, x, p.w, p.mask, res, y, 2, 4, r->stream);
+    return tb_b200_dense_linear(p.rows, p.cols, x, p.w, res, y, r->stream);
+}
+
+// The token's decoder step, queued on the runner's stream.
+int enqueue(Runner* r) {
+    const TbB200RunnerDesc& c = r->cfg;
+    const int H = c.hidden;
+    void* s = r->stream;
+    int rc;
+    r->launches = 0;
+#define TRY(call)                    \
+    do {                             \
+        if ((rc = (call)) != TB_OK) return rc; \
+    } while (0)
+    TRY(tb_b200_embedding(TB_DTYPE_F32, 1, H, c.vocab, r->dstate + 1, r->embed, r->x, s));
+    r->launches++;
+    for (const Layer& L : r->layers) {
+        if (!L.q.w || !L.k.w || !L.v.w) continue;  // ops.hpp:109
+        TRY(tb_b200_rms_norm(TB_DTYPE_F32, 1, H, r->x, L.in_norm, r->x, c.norm_eps, s));
+        r->launches++;
+        TRY(project(r, L.q, r->x, nullptr, r->q));
+        TRY(project(r, L.k, r->x, nullptr, r->k));
+        TRY(project(r, L.v, r->x, nullptr, r->v));
+        TRY(tb_b200_rope_rows(TB_DTYPE_F32, 1, c.n_heads, c.n_kv_heads, c.head_dim, r->q, r->k,
+                              r->dstate, c.rope_theta, r->rope, c.max_seq, s));
+        r->launches++;
+        const size_t layer_off = (size_t)(&L - r->layers.data()) * (size_t)c.max_seq *
+                                 (size_t)c.n_kv_heads * (size_t)c.head_dim;
+        TRY(tb_b200_decode_attention(c.attention, c.n_heads, c.n_kv_heads, c.head_dim, c.max_seq,
+                                     r->dstate, r->q, r->k, r->v, r->kc + layer_off,
+                                     r->vc + layer_off, r->attn, s));
+        r->launches++;
+        if (L.o.w) TRY(project(r, L.o, r->attn, r->x, r->x));  // ops.hpp:207-218
+        TRY(tb_b200_rms_norm(TB_DTYPE_F32, 1, H, r->x, L.post_norm, r->xm, c.norm_eps, s));
+        r->launches++;
+        if (L.gate.w && L.up.w && c.intermediate > 0) {  // ops.hpp:226-256
+            TRY(project(r, L.gate, r->xm, nullptr, r->g));
+            TRY(project(r, L.up, r->xm, nullptr, r->u));
+            TRY(tb_b200_swiglu(TB_DTYPE_F32, c.intermediate, r->g, r->u, r->g, s));
+            r->launches++;
+            if (L.down.w) TRY(project(r, L.down, r->g, r->x, r->x));
+        }
+    }
+    TRY(tb_b200_rms_norm(TB_DTYPE_F32, 1, H, r->x, r->final_norm, r->x, c.norm_eps, s));
+    r->launches++;
+    TRY(tb_b200_dense_linear(c.vocab, H, r->x, r->lm_head, nullptr, r->logits, s));
+    r->launches++;
+    k_advance<<<1, 1, 0, r->stream>>>(r->dstate);
+    TB_LAUNCH_CHECK("runner position kernel");
+    r->launches++;
+#undef TRY
+    return TB_OK;
+}
+
+void release(Runner* r) {
+    if (!r) return;
+    if (r->exec) cudaGraphExecDestroy(r->exec);
+    if (r->graph) cudaGraphDestroy(r->graph);
+    if (r->stream) cudaStreamSynchronize(r->stream);
+    for (void* p : r->owned) cudaFree(p);
+    if (r->stream) cudaStreamDestroy(r->stream);
+    delete r;
+}
+
+int create(const TbB200RunnerDesc* d, Runner* r) {
+    const TbB200RunnerDesc& c = *d;
+    if (c.hidden <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.head_dim <= 0 ||
+        c.n_heads % c.n_kv_heads || c.vocab <= 0 || c.max_seq <= 0 || c.layers < 0 ||
+        c.intermediate < 0 || c.head_dim % 2)
+        return TB_ERR_INVALID_SHAPE;
+    if (c.attention != TB_B200_ATTN_REFERENCE && c.attention != TB_B200_ATTN_STANDARD)
+        return TB_ERR_INVALID_ARG;
+    if (!c.embed.data || (c.layers > 0 && !c.layer)) return TB_ERR_INVALID_ARG;
+    r->cfg = c;
+    r->cfg.layer = nullptr;
+    TB_CUDA_TRY(cudaGetDevice(&r->device));
+    TB_CUDA_TRY(cudaStreamCreateWithFlags(&r->stream, cudaStreamNonBlocking));
+    int rc = tbh::decode_attention_setup(c.head_dim, c.max_seq);
+    if (rc) return rc;
+    const int64_t H = c.hidden, I = c.intermediate, V = c.vocab;
+    const int64_t qd = (int64_t)c.n_heads * c.head_dim, kvd = (int64_t)c.n_kv_heads * c.head_dim;
+    if (c.embed.rows != V || c.embed.cols != H) return TB_ERR_INVALID_SHAPE;
+    if ((rc = materialize(r, c.embed, &r->embed))) return rc;
+    if ((rc = materialize_vec(r, c.final_norm, H, &r->final_norm))) return rc;
+    if (c.lm_head.data) {
+        if (c.lm_head.rows != V || c.lm_head.cols != H) return TB_ERR_INVALID_SHAPE;
+        if ((rc = materialize(r, c.lm_head, &r->lm_head))) return rc;
+    } else {
+        r->lm_head = r->embed;  // ops.hpp:269-273
+    }
+    r->layers.resize((size_t)c.layers);
+    for (int l = 0; l < c.layers; l++) {
+        const TbB200RunnerLayer& s = c.layer[l];
+        Layer& L = r->layers[(size_t)l];
+        if ((rc = make_proj(r, s.q, qd, H, &L.q)) || (rc = make_proj(r, s.k, kvd, H, &L.k)) ||
+            (rc = make_proj(r, s.v, kvd, H, &L.v)) || (rc = make_proj(r, s.o, H, qd, &L.o)) ||
+            (rc = make_proj(r, s.gate, I, H, &L.gate)) || (rc = make_proj(r, s.up, I, H, &L.up)) ||
+            (rc = make_proj(r, s.down, H, I, &L.down)) ||
+            (rc = materialize_vec(r, s.input_norm, H, &L.in_norm)) ||
+            (rc = materialize_vec(r, s.post_norm, H, &L.post_norm)))
+            return rc;
+    }
+    void* p;
+    const size_t f = sizeof(float);
+    if ((rc = dev_alloc(r, (size_t)H * f, &p))) return rc;
+    r->x = (float*)p;
+    if ((rc = dev_alloc(r, (size_t)qd * f, &p))) return rc;
+    r->q = (float*)p;
+    if ((rc = dev_alloc(r, (size_t)kvd * f, &p))) return rc;
+    r->k = (float*)p;
+    if ((rc = dev_alloc(r, (size_t)kvd * f, &p))) return rc;
+    r->v = (float*)p;
+    if ((rc = dev_alloc(r, (size_t)qd * f, &p))) return rc;
+    r->attn = (float*)p;
+    if ((rc = dev_alloc(r, (size_t)H * f, &p))) return rc;
+    r->xm = (float*)p;
+    if ((rc = dev_alloc(r, (size_t)(I > 0 ? I : 1) * f, &p))) return rc;
+    r->g = (float*)p;
+    if ((rc = dev_alloc(r, (size_t)(I > 0 ? I : 1) * f, &p))) return rc;
+    r->u = (float*)p;
+    if ((rc = dev_alloc(r, (size_t)V * f, &p))) return rc;
+    r->logits = (float*)p;
+    const size_t cache = (size_t)(c.layers > 0 ? c.layers : 1) * (size_t)c.max_seq * (size_t)kvd * f;
+    if ((rc = dev_alloc(r, cache, &p))) return rc;
+    r->kc = (float*)p;
+    if ((rc = dev_alloc(r, cache, &p))) return rc;
+    r->vc = (float*)p;
+    if ((rc = dev_alloc(r, (size_t)c.max_seq * c.head_dim * f, &p))) return rc;
+    r->rope = (float*)p;
+    if ((rc = tb_b200_rope_table(c.rope_theta, c.head_dim, c.max_seq, r->rope, r->stream)))
+        return rc;
+    if ((rc = dev_alloc(r, 2 * sizeof(int32_t), &p))) return rc;
+    r->dstate = (int32_t*)p;
+    TB_CUDA_TRY(cudaMemsetAsync(r->dstate, 0, 2 * sizeof(int32_t), r->stream));
+    TB_CUDA_TRY(cudaMemsetAsync(r->x, 0, (size_t)H * f, r->stream));
+    TB_CUDA_TRY(cudaStreamSynchronize(r->stream));
+    if (c.use_graph) {
+        TB_CUDA_TRY(cudaStreamBeginCapture(r->stream, cudaStreamCaptureModeThreadLocal));
+        rc = enqueue(r);
+        cudaGraph_t graph = nullptr;
+        const cudaError_t e = cudaStreamEndCapture(r->stream, &graph);
+        if (rc) {
+            if (graph) cudaGraphDestroy(graph);
+            return rc;
+        }
+        if (e != cudaSuccess) {
+            tbh::set_error("runner graph capture", e);
+            return TB_ERR_DEVICE;
+        }
+        r->graph = graph;
+        TB_CUDA_TRY(cudaGraphInstantiate(&r->exec, graph, 0));
+    }
+    return TB_OK;
+}
+
+}  // namespace
+
+extern "C" int tb_b200_runner_create(const TbB200RunnerDesc* desc, void** runner) {
+    if (!desc || !runner) return TB_ERR_INVALID_ARG;
+    *runner = nullptr;
+    Runner* r = new (std::nothrow) Runner();
+    if (!r) return TB_ERR_OOM;
+    const int rc = create(desc, r);
+    if (rc != TB_OK) {
+        release(r);
+        return rc;
+    }
+    *runner = r;
+    return TB_OK;
+}
+
+extern "C" int tb_b200_runner_forward(void* runner, int32_t token, const float** logits_dev) {
+    Runner* r = static_cast<Runner*>(runner);
+    if (!r) return TB_ERR_INVALID_ARG;
+    if (token < 0 || token >= r->cfg.vocab) return TB_ERR_INVALID_ARG;
+    if (r->pos >= r->cfg.max_seq) return TB_ERR_INVALID_SHAPE;
+    // from pageable memory: the copy takes the value before it returns
+    const int32_t tok = token;
+    TB_CUDA_TRY(cudaMemcpyAsync(r->dstate + 1, &tok, sizeof(int32_t), cudaMemcpyHostToDevice,
+                                r->stream));
+    if (r->exec) {
+        TB_CUDA_TRY(cudaGraphLaunch(r->exec, r->stream));
+    } else {
+        const int rc = enqueue(r);
+        if (rc) return rc;
+    }
+    r->pos++;
+    if (logits_dev) *logits_dev = r->logits;
+    return TB_OK;
+}
+
+extern "C" int tb_b200_runner_logits(void* runner, float* logits_host) {
+    Runner* r = static_cast<Runner*>(runner);
+    if (!r || !logits_host) return TB_ERR_INVALID_ARG;
+    TB_CUDA_TRY(cudaMemcpyAsync(logits_host, r->logits, (size_t)r->cfg.vocab * sizeof(float),
+                                cudaMemcpyDeviceToHost, r->stream));
+    TB_CUDA_TRY(cudaStreamSynchronize(r->stream));
+    return TB_OK;
+}
+
+extern "C" int tb_b200_runner_reset(void* runner) {
+    Runner* r = static_cast<Runner*>(runner);
+    if (!r) return TB_ERR_INVALID_ARG;
+    TB_CUDA_TRY(cudaMemsetAsync(r->dstate, 0, sizeof(int32_t), r->stream));
+    r->pos = 0;
+    return TB_OK;
+}
+
+extern "C" int tb_b200_runner_position(void* runner, int* position) {
+    Runner* r = static_cast<Runner*>(runner);
+    if (!r || !position) return TB_ERR_INVALID_ARG;
+    *position = r->pos;
+    return TB_OK;
+}
+
+extern "C" int tb_b200_runner_stream(void* runner, void** stream) {
+    Runner* r = static_cast<Runner*>(runner);
+    if (!r || !stream) return TB_ERR_INVALID_ARG;
+    *stream = r->stream;
+    return TB_OK;
+}
+
+extern "C" int tb_b200_runner_launches_per_token(void* runner, int* launches) {
+    Runner* r = static_cast<Runner*>(runner);
+    if (!r || !launches) return TB_ERR_INVALID_ARG;
+    *launches = r->launches;
+    return TB_OK;
+}
+
+extern "C" int tb_b200_runner_destroy(void* runner) {
+    release(static_cast<Runner*>(runner));
+    return TB_OK;
+}

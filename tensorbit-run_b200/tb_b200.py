@@ -72,6 +72,27 @@ _lib = None
 vp, i64, i32, f32 = C.c_void_p, C.c_int64, C.c_int, C.c_float
 P = C.POINTER
 
+INT8, INT4 = 7, 8  # TbDtype codes of quantized weights
+ATTN_REFERENCE, ATTN_STANDARD = 0, 1
+FLAG_POSITION_RANGE = 0x4
+PROJECTIONS = ("q", "k", "v", "o", "gate", "up", "down")
+
+
+class Weight(C.Structure):  # TbB200Weight
+    _fields_ = [("data", vp), ("dtype", i32), ("rows", i64), ("cols", i64), ("mask", vp),
+                ("scales", vp), ("n_scales", i64), ("group_size", C.c_uint32)]
+
+
+class RunnerLayer(C.Structure):  # TbB200RunnerLayer
+    _fields_ = [(n, Weight) for n in PROJECTIONS] + [("input_norm", vp), ("post_norm", vp)]
+
+
+class RunnerDesc(C.Structure):  # TbB200RunnerDesc
+    _fields_ = [(n, i32) for n in ("hidden", "n_heads", "n_kv_heads", "head_dim", "intermediate",
+                                   "vocab", "max_seq", "layers")] + [
+        ("norm_eps", f32), ("rope_theta", f32), ("attention", i32), ("use_graph", i32),
+        ("embed", Weight), ("final_norm", vp), ("lm_head", Weight), ("layer", P(RunnerLayer))]
+
 # name -> (restype, argtypes); every entry point of include/tb_b200.h and tb_backend.h.
 SIGNATURES = {
     "tb_b200_version": (i32, []),
@@ -115,6 +136,15 @@ SIGNATURES = {
     "tb_b200_embedding_host_ids": (i32, [i32, i64, i64, i64, vp, vp, vp, vp]),
     "tb_b200_embedding_host_ids_static": (i32, [i32, i64, i64, i64, vp, vp, vp, vp]),
     "tb_b200_layer_chain": (i32, [P(LayerChain), vp]),
+    "tb_b200_decode_attention": (i32, [i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "tb_b200_runner_create": (i32, [P(RunnerDesc), P(vp)]),
+    "tb_b200_runner_forward": (i32, [vp, C.c_int32, P(vp)]),
+    "tb_b200_runner_logits": (i32, [vp, vp]),
+    "tb_b200_runner_reset": (i32, [vp]),
+    "tb_b200_runner_position": (i32, [vp, P(i32)]),
+    "tb_b200_runner_stream": (i32, [vp, P(vp)]),
+    "tb_b200_runner_launches_per_token": (i32, [vp, P(i32)]),
+    "tb_b200_runner_destroy": (i32, [vp]),
     "tb_b200_partition": (i32, [i64, i32, i32, P(i64), P(i64)]),
     "tb_b200_shard_plan": (i32, [i64, i64, i32, i32, vp, vp, vp, vp, vp, vp, vp, P(i64)]),
     "tb_b200_comm_unique_id": (i32, [vp]),
@@ -475,3 +505,133 @@ def embedding_sharded(ids_host, table_shard, vocab: int, y_local=None, stream=No
                                           vocab, ids.ctypes.data, ptr(table_shard), ptr(y_local),
                                           stream or cur_stream()), "embedding_sharded")
     return y_local
+
+
+# ------------------------------------------------ decoder forward (runner)
+def decode_attention(q, k, v, k_cache, v_cache, position, n_heads, n_kv_heads,
+                     mode=ATTN_REFERENCE, out=None, stream=None):
+    """Single-token attention over one layer's f32 KV cache
+    [max_seq, n_kv_heads * head_dim]; `position` a 1-element int32 device
+    tensor.  Also writes k and v into cache row `position`."""
+    torch = _torch()
+    head_dim = q.numel() // n_heads
+    out = torch.empty(n_heads * head_dim, dtype=torch.float32, device=q.device) if out is None else out
+    _dev(q, k, v, k_cache, v_cache, position, out)
+    check(lib().tb_b200_decode_attention(mode, n_heads, n_kv_heads, head_dim, k_cache.shape[0],
+                                         ptr(position), ptr(q), ptr(k), ptr(v), ptr(k_cache),
+                                         ptr(v_cache), ptr(out), stream or cur_stream()),
+          "decode_attention")
+    return out
+
+
+class QuantWeight:
+    """An INT4 (dtype INT4, two weights per byte, low nibble first) or INT8
+    weight tensor [rows, cols] with per-group f32 scales, as a .tbm layer
+    stores it."""
+
+    def __init__(self, data, dtype, rows, cols, scales, group_size):
+        self.data, self.dtype, self.rows, self.cols = data, dtype, rows, cols
+        self.scales, self.group_size = scales, group_size
+
+
+class Runner:
+    """TransformerRunner (include/tensorbit/run/ops.hpp:33-288) on the device.
+
+    cfg: dict with hidden, n_heads, n_kv_heads, head_dim, intermediate,
+    vocab, max_seq, layers, norm_eps, rope_theta.  model: {"embed": W,
+    "final_norm": v, "lm_head": W or None, "layers": [{"q": (W, mask), ...,
+    "in_norm": v, "post_norm": v}]}, where W is an f32 numpy array (copied
+    to the device), an f32 CUDA tensor (borrowed) or a QuantWeight, and a
+    mask is uint8 2:4 group bytes or None (dense)."""
+
+    def __init__(self, cfg, model, attention=ATTN_REFERENCE, use_graph=True):
+        import numpy as np
+        self._keep = []
+        self.vocab = int(cfg["vocab"])
+
+        def addr(a, dt=None):
+            if a is None:
+                return None
+            if hasattr(a, "data_ptr"):
+                self._keep.append(a)
+                return a.data_ptr()
+            a = np.ascontiguousarray(a, dtype=dt)
+            self._keep.append(a)
+            return a.ctypes.data
+
+        def weight(w, mask=None):
+            if w is None:
+                return Weight()
+            if isinstance(w, QuantWeight):
+                sc = addr(w.scales, np.float32)
+                return Weight(addr(w.data, np.uint8), w.dtype, w.rows, w.cols, addr(mask, np.uint8),
+                              sc, 0 if w.scales is None else int(np.size(w.scales) if not hasattr(
+                                  w.scales, "numel") else w.scales.numel()), w.group_size)
+            return Weight(addr(w, np.float32), F32, w.shape[0], w.shape[1], addr(mask, np.uint8),
+                          None, 0, 0)
+
+        n_layers = int(cfg["layers"])
+        layers = (RunnerLayer * max(1, n_layers))()
+        for i, ly in enumerate(model["layers"][:n_layers]):
+            for n in PROJECTIONS:
+                wm = ly.get(n)
+                if wm is not None:
+                    setattr(layers[i], n, weight(wm[0], wm[1] if len(wm) > 1 else None))
+            layers[i].input_norm = addr(ly.get("in_norm"), np.float32)
+            layers[i].post_norm = addr(ly.get("post_norm"), np.float32)
+        d = RunnerDesc(*[int(cfg[n]) for n in ("hidden", "n_heads", "n_kv_heads", "head_dim",
+                                               "intermediate", "vocab", "max_seq", "layers")],
+                       float(cfg.get("norm_eps", 1e-5)), float(cfg.get("rope_theta", 10000.0)),
+                       attention, 1 if use_graph else 0, weight(model["embed"]),
+                       addr(model.get("final_norm"), np.float32), weight(model.get("lm_head")),
+                       layers)
+        h = vp()
+        check(lib().tb_b200_runner_create(C.byref(d), C.byref(h)), "runner_create")
+        self._h = h
+        # host arrays were copied during create; device tensors stay borrowed
+        self._keep = [a for a in self._keep if hasattr(a, "data_ptr")]
+
+    def forward(self, token):
+        """Run one token; returns the device logits address (valid until the
+        next forward)."""
+        out = vp()
+        check(lib().tb_b200_runner_forward(self._h, int(token), C.byref(out)), "runner_forward")
+        return out.value
+
+    def logits(self):
+        import numpy as np
+        out = np.empty(self.vocab, dtype=np.float32)
+        check(lib().tb_b200_runner_logits(self._h, out.ctypes.data), "runner_logits")
+        return out
+
+    def reset(self):
+        check(lib().tb_b200_runner_reset(self._h), "runner_reset")
+
+    @property
+    def position(self):
+        p = i32()
+        check(lib().tb_b200_runner_position(self._h, C.byref(p)), "runner_position")
+        return p.value
+
+    @property
+    def stream(self):
+        s = vp()
+        check(lib().tb_b200_runner_stream(self._h, C.byref(s)), "runner_stream")
+        return s
+
+    @property
+    def launches_per_token(self):
+        n = i32()
+        check(lib().tb_b200_runner_launches_per_token(self._h, C.byref(n)), "runner_launches")
+        return n.value
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().tb_b200_runner_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

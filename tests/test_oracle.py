@@ -306,3 +306,88 @@ def test_linear_restatement_matches_reference(out_f, in_f, n, m, with_bias):
         got = O.linear(x, w, msk, b, n, m, O.PORT)
         want = O.linear(x, w, msk, b, n, m, O.REF)
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+# ------------------------------------------------- decoder forward (runner)
+needs_pin_runner = pytest.mark.skipif(not O.pin_runner_available(),
+                                      reason="reference runner (oracle/_ref) not built")
+
+
+@needs_pin_runner
+@pytest.mark.parametrize("masks,norms,tokens", [("mock", "ones", 64), ("rand", "rand", 24)])
+def test_runner_restatement_matches_reference(masks, norms, tokens):
+    """The reference's own TransformerRunner (ops.hpp:79-288 over its CPU
+    backend) on the engine's mock shape: the restatement's logits after
+    every token equal it bit for bit."""
+    from runner_models import mock
+    cfg, model = mock(seed=11, masks=masks, norms=norms)
+    toks = np.random.default_rng(3).integers(0, cfg["vocab"], tokens).astype(np.int32)
+    a = O.runner_run(cfg, model, toks, O.PORT)
+    b = O.runner_run(cfg, model, toks, O.REF)
+    assert np.array_equal(a, b)
+    assert np.isfinite(a).all() and np.abs(a).max() > 0
+
+
+@needs_pin_runner
+def test_runner_dense_projections_match_reference_all_ones_masks():
+    """A dense projection is the reference's 2:4 path with every mask bit
+    set (all weights kept in order); the two differ only by FMA
+    contraction in the inner loop."""
+    from runner_models import mock
+    cfg, model = mock(seed=12, masks="none", layers=1)
+    toks = np.arange(10, dtype=np.int32)
+    a = O.runner_run(cfg, model, toks, O.PORT)
+    b = O.runner_run(cfg, model, toks, O.REF)
+    assert np.abs(a - b).max() <= 1e-6 * np.abs(b).max()
+
+
+def _attention_rows_np(q, kc, vc, pos, n_heads, n_kv, d, mode):
+    """Float64 decode attention over a cache [pos+1, n_kv*d]."""
+    cur = pos + 1
+    out = np.zeros((n_heads, d))
+    for r in range(n_heads):
+        h, last = (r // cur, r % cur) if mode == O.ATTN_REFERENCE else (r, pos)
+        g = h // (n_heads // n_kv)
+        keys = kc[:last + 1, g * d:(g + 1) * d].astype(np.float64)
+        vals = vc[:last + 1, g * d:(g + 1) * d].astype(np.float64)
+        s = keys @ q[h * d:(h + 1) * d].astype(np.float64) / math.sqrt(d)
+        p = np.exp(s - s.max())
+        out[r] = (p / p.sum()) @ vals
+    return out.reshape(-1)
+
+
+@pytest.mark.parametrize("mode", [O.ATTN_REFERENCE, O.ATTN_STANDARD])
+@pytest.mark.parametrize("heads,kv", [(8, 8), (8, 2)])
+def test_runner_attention_rows_follow_their_definition(mode, heads, kv):
+    """One layer with dense q/k/v, an identity output projection and lm
+    head, no MLP and no norm weights: the logits after token t are
+    rms_norm(x + attn) with x = rms_norm(embed[token]), so the attention
+    rows (both layouts, MHA and GQA) can be replayed in float64 from their
+    definition: softmax(q_h . k_j / sqrt(d)) over keys 0 .. last of kv head
+    h / (heads / kv), weighted over v."""
+    rng = np.random.default_rng(4)
+    d, hidden = 16, 8 * 16
+    kvd = kv * d
+    cfg = dict(hidden=hidden, n_heads=heads, n_kv_heads=kv, head_dim=d, intermediate=0,
+               vocab=hidden, max_seq=16, layers=1, norm_eps=1e-6, rope_theta=10000.0,
+               attention=mode)
+    wq = rng.standard_normal((heads * d, hidden)).astype(np.float32) * 0.3
+    wk = rng.standard_normal((kvd, hidden)).astype(np.float32) * 0.3
+    wv = rng.standard_normal((kvd, hidden)).astype(np.float32) * 0.3
+    eye = np.eye(hidden, dtype=np.float32)
+    embed = rng.standard_normal((hidden, hidden)).astype(np.float32)
+    layer = dict(q=(wq, None), k=(wk, None), v=(wv, None), o=(eye, None))
+    model = dict(embed=embed, final_norm=None, lm_head=eye, layers=[layer])
+    toks = rng.integers(0, hidden, 9).astype(np.int32)
+    got = O.runner_run(cfg, model, toks)
+    kc = np.zeros((16, kvd), np.float32)
+    vc = np.zeros((16, kvd), np.float32)
+    for t, tok in enumerate(toks):
+        x = O.rms_norm_vec(embed[tok], None, 1e-6)
+        q, k = O.rope((wq @ x).reshape(1, heads, d), (wk @ x).reshape(1, kv, d),
+                      np.array([t], np.int32), 10000.0)
+        kc[t], vc[t] = k.reshape(-1), wv @ x
+        att = _attention_rows_np(q.reshape(-1), kc, vc, t, heads, kv, d, mode)
+        h = x.astype(np.float64) + att
+        want = h / np.sqrt(((h * h).sum() + 1e-6) / hidden)  # src/ops/norm.c:8-13
+        np.testing.assert_allclose(got[t], want, rtol=0, atol=2e-5 * np.abs(want).max())
