@@ -261,6 +261,25 @@ typedef struct {
 
 int tb_b200_layer_chain(const TbB200LayerChain* chain, void* stream);
 
+/* 2:4 sparse weights in packed form: per pair of 4-column groups, one
+ * float4 of the kept weights (column order within each group, 0 in an
+ * unused slot) and one index byte (2 bits per slot: the kept column within
+ * its group).  Half the bytes of the reference's dense-with-mask layout
+ * (src/ops/linear.c:4-35), the same products summed.
+ * pack: w [out, in] f32 and mask [out, in/4] bytes (bits 0..3 of a byte
+ * keep columns of its group) -> vals (16-byte aligned, out * P float4s) and
+ * idx (out * P bytes), P = ceil((in/4) / 2).  A group with more than two
+ * mask bits set sets *unpackable_dev to 1 (the layer must stay dense-with-
+ * mask); the caller zeroes it first and reads it after the stream.
+ * linear: y = W x (+ bias) from the packed form; (in/4) must be even, x and
+ * vals 16-byte aligned; bias may alias y. */
+int tb_b200_sparse24_pack(int64_t out_features, int64_t in_features, const float* w,
+                          const uint8_t* mask, void* vals, uint8_t* idx, int* unpackable_dev,
+                          void* stream);
+int tb_b200_sparse24_linear(int64_t out_features, int64_t in_features, const float* x,
+                            const void* vals, const uint8_t* idx, const float* bias, float* y,
+                            void* stream);
+
 /* ======================================================================
  * Decoder forward on the device (TransformerRunner)
  * ====================================================================== */
@@ -339,7 +358,9 @@ typedef struct {
  * `hidden` floats (the reference normalises its max(hidden, vocab) state
  * vector, reading past the hidden-sized norm weights when vocab > hidden).
  * create: uploads / dequantises what is not already f32 on the device
- * (borrowed device tensors must outlive the runner), allocates the cache,
+ * (borrowed device tensors must outlive the runner), packs every masked
+ * projection whose groups keep at most two weights (tb_b200_sparse24_pack;
+ * an uploaded dense copy is freed after packing), allocates the cache and
  * builds the RoPE table with the host C library. */
 int tb_b200_runner_create(const TbB200RunnerDesc* desc, void** runner);
 /* Run one token at the next position; *logits_dev (optional) receives the

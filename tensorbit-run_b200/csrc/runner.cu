@@ -37,6 +37,8 @@ __global__ void k_advance(int32_t* pos) { *pos += 1; }
 struct Proj {
     const float* w = nullptr;
     const uint8_t* mask = nullptr;
+    const void* vals = nullptr;  // packed 2:4 form, when the mask allows it
+    const uint8_t* idx = nullptr;
     int64_t rows = 0, cols = 0;
 };
 
@@ -59,6 +61,7 @@ struct Runner {
     float *xm = nullptr, *g = nullptr, *u = nullptr, *logits = nullptr;
     float *kc = nullptr, *vc = nullptr, *rope = nullptr;
     int32_t* dstate = nullptr;  // [0] position, [1] token
+    int* flag = nullptr;        // packing verdict of one layer
     int pos = 0;
     int launches = 0;
     cudaGraphExec_t exec = nullptr;
@@ -148,6 +151,46 @@ int materialize_mask(Runner* r, const TbB200Weight& w, const uint8_t** out) {
     return TB_OK;
 }
 
+void free_owned(Runner* r, const void* p) {
+    for (size_t i = 0; i < r->owned.size(); ++i)
+        if (r->owned[i] == p) {
+            cudaFree(r->owned[i]);
+            r->owned.erase(r->owned.begin() + (long)i);
+            return;
+        }
+}
+
+// Packed 2:4 form of a masked projection, when every group keeps at most
+// two weights and the groups pair up.
+int pack(Runner* r, Proj* p) {
+    const int64_t groups = p->cols / 4;
+    if (!p->mask || groups == 0 || groups % 2) return TB_OK;
+    const int64_t pairs = groups / 2;
+    void *vals = nullptr, *idx = nullptr;
+    int rc;
+    if ((rc = dev_alloc(r, (size_t)(p->rows * pairs) * 16, &vals))) return rc;
+    if ((rc = dev_alloc(r, (size_t)(p->rows * pairs), &idx))) return rc;
+    TB_CUDA_TRY(cudaMemsetAsync(r->flag, 0, sizeof(int), r->stream));
+    if ((rc = tb_b200_sparse24_pack(p->rows, p->cols, p->w, p->mask, vals, (uint8_t*)idx, r->flag,
+                                    r->stream)))
+        return rc;
+    int bad = 0;
+    TB_CUDA_TRY(cudaMemcpyAsync(&bad, r->flag, sizeof(int), cudaMemcpyDeviceToHost, r->stream));
+    TB_CUDA_TRY(cudaStreamSynchronize(r->stream));
+    if (bad) {  // three or four weights kept in some group: dense-with-mask
+        free_owned(r, vals);
+        free_owned(r, idx);
+        return TB_OK;
+    }
+    p->vals = vals;
+    p->idx = static_cast<const uint8_t*>(idx);
+    free_owned(r, p->w);    // uploaded dense copies are no longer needed
+    free_owned(r, p->mask);
+    p->w = static_cast<const float*>(vals);  // non-null: the projection exists
+    p->mask = nullptr;
+    return TB_OK;
+}
+
 int make_proj(Runner* r, const TbB200Weight& w, int64_t rows, int64_t cols, Proj* p) {
     *p = Proj{};
     if (!w.data) return TB_OK;
@@ -158,12 +201,14 @@ int make_proj(Runner* r, const TbB200Weight& w, int64_t rows, int64_t cols, Proj
     if (rc) return rc;
     p->rows = rows;
     p->cols = cols;
-    return TB_OK;
+    return pack(r, p);
 }
 
 // y = W x, plus `res` (which may be y itself) when given.
 int project(Runner* r, const Proj& p, const float* x, const float* res, float* y) {
     r->launches++;
+    if (p.vals)
+        return tb_b200_sparse24_linear(p.rows, p.cols, x, p.vals, p.idx, res, y, r->stream);
     if (p.mask)  // the runner's projections run as 2:4 groups (registry.c:93)
         return tb_b200_sparse_linear(p.rows, p.cols, x, p.w, p.mask, res, y, 2, 4, r->stream);
     return tb_b200_dense_linear(p.rows, p.cols, x, p.w, res, y, r->stream);
@@ -256,6 +301,9 @@ int create(const TbB200RunnerDesc* d, Runner* r) {
     } else {
         r->lm_head = r->embed;  // ops.hpp:269-273
     }
+    void* fp = nullptr;
+    if ((rc = dev_alloc(r, sizeof(int), &fp))) return rc;
+    r->flag = static_cast<int*>(fp);
     r->layers.resize((size_t)c.layers);
     for (int l = 0; l < c.layers; l++) {
         const TbB200RunnerLayer& s = c.layer[l];

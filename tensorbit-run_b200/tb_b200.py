@@ -136,6 +136,8 @@ SIGNATURES = {
     "tb_b200_embedding_host_ids": (i32, [i32, i64, i64, i64, vp, vp, vp, vp]),
     "tb_b200_embedding_host_ids_static": (i32, [i32, i64, i64, i64, vp, vp, vp, vp]),
     "tb_b200_layer_chain": (i32, [P(LayerChain), vp]),
+    "tb_b200_sparse24_pack": (i32, [i64, i64, vp, vp, vp, vp, vp, vp]),
+    "tb_b200_sparse24_linear": (i32, [i64, i64, vp, vp, vp, vp, vp, vp]),
     "tb_b200_decode_attention": (i32, [i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp]),
     "tb_b200_runner_create": (i32, [P(RunnerDesc), P(vp)]),
     "tb_b200_runner_forward": (i32, [vp, C.c_int32, P(vp)]),
@@ -392,6 +394,32 @@ def linear(x, w, mask=None, bias=None, nm_n=2, nm_m=4, y=None, stream=None):
         rc = lib().tb_b200_dense_linear(out_f, in_f, ptr(x), ptr(w), b, ptr(y),
                                         stream or cur_stream())
     check(rc, "linear")
+    return y
+
+
+def sparse24_pack(w, mask, stream=None):
+    """Pack a 2:4-masked f32 [out, in] weight: (vals float32 [out, P, 4],
+    idx uint8 [out, P], packable) with P = ceil((in / 4) / 2)."""
+    torch = _torch()
+    out_f, in_f = w.shape
+    pairs = (in_f // 4 + 1) // 2
+    vals = torch.empty((out_f, pairs, 4), dtype=torch.float32, device=w.device)
+    idx = torch.empty((out_f, pairs), dtype=torch.uint8, device=w.device)
+    flag = torch.zeros(1, dtype=torch.int32, device=w.device)
+    _dev(w, mask)
+    check(lib().tb_b200_sparse24_pack(out_f, in_f, ptr(w), ptr(mask), ptr(vals), ptr(idx),
+                                      ptr(flag), stream or cur_stream()), "sparse24_pack")
+    return vals, idx, int(flag.item()) == 0
+
+
+def sparse24_linear(x, vals, idx, in_features, bias=None, y=None, stream=None):
+    torch = _torch()
+    out_f = vals.shape[0]
+    y = torch.empty(out_f, dtype=torch.float32, device=x.device) if y is None else y
+    _dev(x, vals, idx, y)
+    check(lib().tb_b200_sparse24_linear(out_f, in_features, ptr(x), ptr(vals), ptr(idx),
+                                        ptr(bias) if bias is not None else None, ptr(y),
+                                        stream or cur_stream()), "sparse24_linear")
     return y
 
 

@@ -28,6 +28,8 @@ def mock(seed=0, hidden=256, inter=1024, layers=2, vocab=100, heads=8, kv=8, max
             return None
         if masks == "mock":
             return np.full((r, c // 4), 0x3, np.uint8)
+        if masks == "mixed":  # some groups keep three or four weights
+            return np.array([0x3, 0x7, 0xF, 0x5], np.uint8)[rng.integers(0, 4, (r, c // 4))]
         return PATTERNS_2_4[rng.integers(0, PATTERNS_2_4.size, (r, c // 4))]
 
     def nv():

@@ -72,7 +72,7 @@ def test_graph_and_eager_are_identical(dev):
     assert np.array_equal(a, b)
 
 
-@pytest.mark.parametrize("masks,norms", [("rand", "rand"), ("none", "rand")])
+@pytest.mark.parametrize("masks,norms", [("rand", "rand"), ("none", "rand"), ("mixed", "ones")])
 def test_random_masks_and_dense_projections(dev, masks, norms):
     cfg, model = mock(seed=17, masks=masks, norms=norms, layers=3)
     toks = tokens(32, cfg["vocab"])
