@@ -268,7 +268,10 @@ int tb_b200_layer_chain(const TbB200LayerChain* chain, void* stream);
  * (src/ops/linear.c:4-35), the same products summed.
  * pack: w [out, in] f32 and mask [out, in/4] bytes (bits 0..3 of a byte
  * keep columns of its group) -> vals (16-byte aligned, out * P float4s) and
- * idx (out * P bytes), P = ceil((in/4) / 2).  A group with more than two
+ * idx (out * S bytes), P = ceil((in/4) / 2), S = P rounded up to a multiple
+ * of 128; within a row the byte of pair p = 128 s + 32 u + l (l < 32,
+ * u < 4) is at 128 s + 4 l + u, so a lane loads its four bytes of a
+ * 128-pair step as one 32-bit word.  A group with more than two
  * mask bits set sets *unpackable_dev to 1 (the layer must stay dense-with-
  * mask); the caller zeroes it first and reads it after the stream.
  * linear: y = W x (+ bias) from the packed form; (in/4) must be even, x and

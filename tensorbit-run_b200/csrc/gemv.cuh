@@ -1,0 +1,144 @@
+// gemv.cuh -- per-warp row dot products of the decoder's GEMVs: dense f32
+// rows, and 2:4 rows in the packed form of k_sparse24.cu.
+//
+// A warp takes two output rows at once, so every float4 of x it loads
+// (through L1) serves both.  Lanes stride over the row in steps of 128
+// float4s (dense) or 128 group pairs (packed), four per lane per row in
+// flight, with no bounds checks inside a full step; the last partial step
+// goes element by element.  The result is each lane's partial sum; the
+// caller adds the lanes (warp_sum2).
+//
+// Packed form, per row: P = (in/4)/2 pairs of 4-column groups; vals holds a
+// float4 per pair (group 2p's two kept weights, then group 2p+1's) and idx a
+// byte per pair (2 bits per slot: the kept column within its group), laid
+// out so that one 32-bit load gives a lane its four bytes of a step: the
+// byte of pair p = 128 s + 32 u + l is at 128 s + 4 l + u, and a row of idx
+// is padded to a multiple of 128 bytes.
+#pragma once
+#include "tb_device.cuh"
+
+namespace tbk {
+
+constexpr int kGemvStep = 128;  // float4s (dense) or pairs (packed) per warp step
+
+__host__ __device__ inline int64_t packed_idx_stride(int64_t pairs) {
+    return (pairs + kGemvStep - 1) / kGemvStep * kGemvStep;
+}
+
+// x[4 g + k] for k = the 2-bit field's value.
+__device__ __forceinline__ float pick4(const float4& x, uint32_t k) {
+    const float lo = (k & 1u) ? x.y : x.x;
+    const float hi = (k & 1u) ? x.w : x.z;
+    return (k & 2u) ? hi : lo;
+}
+
+// The four kept weights of a pair against x columns 8p .. 8p+7.
+__device__ __forceinline__ float pair_dot(const float4& v, uint32_t ib, const float4& xa,
+                                          const float4& xb, float acc) {
+    acc = __fmaf_rn(v.x, pick4(xa, ib), acc);
+    acc = __fmaf_rn(v.y, pick4(xa, ib >> 2), acc);
+    acc = __fmaf_rn(v.z, pick4(xb, ib >> 4), acc);
+    acc = __fmaf_rn(v.w, pick4(xb, ib >> 6), acc);
+    return acc;
+}
+
+// Partial sums of two packed rows (v0/i0 and v1/i1; pass the same row twice
+// for one).  pairs: P; istride: the padded idx row length in bytes.
+__device__ __forceinline__ void packed_dot2(const float4* __restrict__ v0,
+                                            const uint8_t* __restrict__ i0,
+                                            const float4* __restrict__ v1,
+                                            const uint8_t* __restrict__ i1, int64_t pairs,
+                                            const float4* __restrict__ x4, int lane, float& a0,
+                                            float& a1) {
+    const int64_t full = pairs / kGemvStep;
+    const float4* p0 = v0 + lane;
+    const float4* p1 = v1 + lane;
+    const uint32_t* q0 = reinterpret_cast<const uint32_t*>(i0) + lane;
+    const uint32_t* q1 = reinterpret_cast<const uint32_t*>(i1) + lane;
+    const float4* xp = x4 + 2 * lane;
+    for (int64_t s = 0; s < full; ++s) {
+        float4 w0[4], w1[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            w0[u] = __ldcs(p0 + 32 * u);
+            w1[u] = __ldcs(p1 + 32 * u);
+        }
+        const uint32_t b0 = __ldcs(q0), b1 = __ldcs(q1);
+        p0 += kGemvStep;
+        p1 += kGemvStep;
+        q0 += 32;
+        q1 += 32;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const float4 xa = __ldg(xp + 64 * u), xb = __ldg(xp + 64 * u + 1);
+            a0 = pair_dot(w0[u], b0 >> (8 * u), xa, xb, a0);
+            a1 = pair_dot(w1[u], b1 >> (8 * u), xa, xb, a1);
+        }
+        xp += 2 * kGemvStep;
+    }
+    for (int u = 0; u < 4; ++u) {  // the partial step
+        const int64_t p = full * kGemvStep + 32 * u + lane;
+        if (p >= pairs) break;
+        const float4 xa = __ldg(x4 + 2 * p), xb = __ldg(x4 + 2 * p + 1);
+        const int64_t ib = full * kGemvStep + 4 * lane + u;
+        a0 = pair_dot(__ldcs(v0 + p), i0[ib], xa, xb, a0);
+        a1 = pair_dot(__ldcs(v1 + p), i1[ib], xa, xb, a1);
+    }
+}
+
+// Partial sums of two dense rows of n4 float4s each.
+__device__ __forceinline__ void dense_dot2(const float4* __restrict__ w0,
+                                           const float4* __restrict__ w1, int64_t n4,
+                                           const float4* __restrict__ x4, int lane, float& a0,
+                                           float& a1) {
+    const int64_t full = n4 / kGemvStep;
+    const float4* p0 = w0 + lane;
+    const float4* p1 = w1 + lane;
+    const float4* xp = x4 + lane;
+    for (int64_t s = 0; s < full; ++s) {
+        float4 r0[4], r1[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            r0[u] = __ldcs(p0 + 32 * u);
+            r1[u] = __ldcs(p1 + 32 * u);
+        }
+        p0 += kGemvStep;
+        p1 += kGemvStep;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const float4 xv = __ldg(xp + 32 * u);
+            a0 = __fmaf_rn(xv.x, r0[u].x, a0);
+            a0 = __fmaf_rn(xv.y, r0[u].y, a0);
+            a0 = __fmaf_rn(xv.z, r0[u].z, a0);
+            a0 = __fmaf_rn(xv.w, r0[u].w, a0);
+            a1 = __fmaf_rn(xv.x, r1[u].x, a1);
+            a1 = __fmaf_rn(xv.y, r1[u].y, a1);
+            a1 = __fmaf_rn(xv.z, r1[u].z, a1);
+            a1 = __fmaf_rn(xv.w, r1[u].w, a1);
+        }
+        xp += kGemvStep;
+    }
+    for (int u = 0; u < 4; ++u) {
+        const int64_t v = full * kGemvStep + 32 * u + lane;
+        if (v >= n4) break;
+        const float4 xv = __ldg(x4 + v), r0 = __ldcs(w0 + v), r1 = __ldcs(w1 + v);
+        a0 = __fmaf_rn(xv.x, r0.x, a0);
+        a0 = __fmaf_rn(xv.y, r0.y, a0);
+        a0 = __fmaf_rn(xv.z, r0.z, a0);
+        a0 = __fmaf_rn(xv.w, r0.w, a0);
+        a1 = __fmaf_rn(xv.x, r1.x, a1);
+        a1 = __fmaf_rn(xv.y, r1.y, a1);
+        a1 = __fmaf_rn(xv.z, r1.z, a1);
+        a1 = __fmaf_rn(xv.w, r1.w, a1);
+    }
+}
+
+__device__ __forceinline__ void warp_sum2(float& a0, float& a1) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        a0 = __fadd_rn(a0, __shfl_xor_sync(kFull, a0, o));
+        a1 = __fadd_rn(a1, __shfl_xor_sync(kFull, a1, o));
+    }
+}
+
+}  // namespace tbk

@@ -25,6 +25,7 @@
 // from device memory, so a captured CUDA graph replays unchanged.
 #include <atomic>
 
+#include "runner_kernels.h"
 #include "tb_device.cuh"
 #include "tb_internal.h"
 
@@ -42,6 +43,10 @@ k_decode_attention(int mode, int hq, int hkv, int d, int max_seq, const int32_t*
                    float scale, unsigned* status) {
     extern __shared__ float sm[];
     __shared__ float red[kWarps];
+    // under programmatic dependent launch, wait for the producer of q/k/v
+    // (returns at once otherwise)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int pos = *pos_p;
     if (pos < 0 || pos >= max_seq) {  // nothing is read or written
         if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(status, TB_B200_FLAG_POSITION_RANGE);
@@ -166,6 +171,16 @@ extern "C" int tb_b200_decode_attention(int mode, int n_heads, int n_kv_heads, i
                                         int max_seq, const int32_t* position, const float* q,
                                         const float* k, const float* v, float* k_cache,
                                         float* v_cache, float* out, void* stream) {
+    return tbh::decode_attention_launch(mode, n_heads, n_kv_heads, head_dim, max_seq, position, q,
+                                        k, v, k_cache, v_cache, out, tbh::stream_of(stream),
+                                        false);
+}
+
+// Launch, optionally with programmatic dependent launch (the runner's step).
+int tbh::decode_attention_launch(int mode, int n_heads, int n_kv_heads, int head_dim,
+                                 int max_seq, const int32_t* position, const float* q,
+                                 const float* k, const float* v, float* k_cache, float* v_cache,
+                                 float* out, cudaStream_t s, bool pdl) {
     if (mode != TB_B200_ATTN_REFERENCE && mode != TB_B200_ATTN_STANDARD) return TB_ERR_INVALID_ARG;
     if (n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || head_dim <= 0 ||
         head_dim > kMaxD || max_seq <= 0)
@@ -179,16 +194,28 @@ extern "C" int tb_b200_decode_attention(int mode, int n_heads, int n_kv_heads, i
         if (rc != TB_OK) return rc;
     }
     const float scale = 1.f / sqrtf((float)head_dim);  // ops.hpp:175
-    cudaStream_t s = tbh::stream_of(stream);
     const bool vec = head_dim % 4 == 0 && tbh::aligned16(k) && tbh::aligned16(k_cache);
-    if (vec)
-        k_decode_attention<4><<<n_heads, kT, bytes, s>>>(mode, n_heads, n_kv_heads, head_dim, max_seq,
-                                                         position, q, k, v, k_cache, v_cache, out,
-                                                         scale, ds->status);
-    else
-        k_decode_attention<1><<<n_heads, kT, bytes, s>>>(mode, n_heads, n_kv_heads, head_dim, max_seq,
-                                                         position, q, k, v, k_cache, v_cache, out,
-                                                         scale, ds->status);
-    TB_LAUNCH_CHECK("decode attention kernel");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)n_heads);
+    cfg.blockDim = dim3(kT);
+    cfg.dynamicSmemBytes = bytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    const cudaError_t e =
+        vec ? cudaLaunchKernelEx(&cfg, k_decode_attention<4>, mode, n_heads, n_kv_heads, head_dim,
+                                 max_seq, position, q, k, v, k_cache, v_cache, out, scale,
+                                 ds->status)
+            : cudaLaunchKernelEx(&cfg, k_decode_attention<1>, mode, n_heads, n_kv_heads, head_dim,
+                                 max_seq, position, q, k, v, k_cache, v_cache, out, scale,
+                                 ds->status);
+    tbh::count_launch();
+    if (e != cudaSuccess) {
+        tbh::set_error("decode attention kernel", e);
+        return TB_ERR_DEVICE;
+    }
     return TB_OK;
 }

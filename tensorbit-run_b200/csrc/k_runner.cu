@@ -1,0 +1,229 @@
+// k_runner.cu -- the fused kernels of the device decoder step (runner.cu):
+// one GEMV launch per group of projections that share an input, with the
+// step that follows each group folded into its epilogue, and the RMSNorm of
+// the state vector.
+//
+// Reference steps (TransformerRunner::forward, include/tensorbit/run/
+// ops.hpp) and the epilogue that replaces each:
+//   q, k, v = W x; rope(q, k) at the position         (:140-159)  kRope
+//   x = x + Wo attn                                    (:207-218)  kResidual
+//   g = silu(Wg x_mlp) * (Wu x_mlp)                    (:226-248)  kSwiglu
+//   x = x + Wd g                                       (:250-256)  kResidual
+//   logits = Wlm x; position += 1                      (:269-284)  kPlain
+// The arithmetic of each epilogue is the separate kernel's: the rotation of
+// tbk::rope_rotate over the host-built cos/sin table, tbk::silu_f(g) * u, and
+// one f32 add for the residual.
+//
+// Each warp computes two output rows (gemv.cuh): two consecutive rows of a
+// projection -- for q and k exactly the pair (2i, 2i+1) RoPE rotates
+// together -- or row j of the gate and up projections.  Every kernel here is
+// launched with programmatic dependent launch: a CTA first asks L2 to fetch
+// its first rows of weights (they do not depend on the previous kernel),
+// then waits (griddepcontrol.wait) for the previous kernel's results, so the
+// weight stream starts during that kernel's tail.
+#include "bodies.cuh"
+#include "gemv.cuh"
+#include "tb_internal.h"
+#include "tma.cuh"
+
+#include "runner_kernels.h"
+
+namespace {
+
+using tbh::GemvArgs;
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+
+__device__ __forceinline__ void pdl_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Unit u -> (segment, first row, second row).  A unit is two consecutive
+// rows of one segment (the last row twice when a segment's count is odd),
+// or for kSwiglu row u of segment 0 (gate) and of segment 1 (up).
+template <int EPI>
+__device__ __forceinline__ bool unit_rows(const GemvArgs& a, int64_t u, int& s, int64_t& r0,
+                                          int64_t& r1) {
+    if constexpr (EPI == tbh::kSwiglu) {
+        if (u >= a.seg[0].rows) return false;
+        s = 0;
+        r0 = r1 = u;
+        return true;
+    } else {
+        for (s = 0; s < a.nseg; ++s) {
+            const int64_t n = (a.seg[s].rows + 1) / 2;
+            if (u < n) {
+                r0 = 2 * u;
+                r1 = r0 + 1 < a.seg[s].rows ? r0 + 1 : r0;
+                return true;
+            }
+            u -= n;
+        }
+        return false;
+    }
+}
+
+template <int LAYOUT>
+__device__ __forceinline__ void row_ptrs(const tbh::GemvSeg& g, int64_t cols, int64_t r,
+                                         const float4*& v, const uint8_t*& ib) {
+    if (LAYOUT == tbh::kDense) {
+        v = static_cast<const float4*>(g.w) + r * (cols / 4);
+        ib = nullptr;
+    } else {
+        const int64_t pairs = cols / 8;
+        v = static_cast<const float4*>(g.w) + r * pairs;
+        ib = g.idx + r * tbk::packed_idx_stride(pairs);
+    }
+}
+
+// L2 prefetch of one weight row (at most 64 KB of it; sizes are multiples
+// of 16 bytes and rows start 16-byte aligned).
+template <int LAYOUT>
+__device__ __forceinline__ void prefetch_row(int64_t cols, const float4* v, const uint8_t* ib) {
+    constexpr int64_t kCap = 64 * 1024;
+    if (LAYOUT == tbh::kDense) {
+        tbk::prefetch_l2(v, (uint32_t)min(cols * 4, kCap));
+    } else {
+        const int64_t pairs = cols / 8;
+        tbk::prefetch_l2(v, (uint32_t)min(pairs * 16, kCap));
+        tbk::prefetch_l2(ib, (uint32_t)min(tbk::packed_idx_stride(pairs), kCap));
+    }
+}
+
+template <int LAYOUT, int EPI>
+__global__ void __launch_bounds__(kThreads) k_fgemv(const __grid_constant__ GemvArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * kWarps;
+    const int64_t first = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+    {  // weights do not depend on the previous kernel: start their stream
+        int s;
+        int64_t r0, r1;
+        if (lane == 0 && unit_rows<EPI>(a, first, s, r0, r1)) {
+            const float4* v;
+            const uint8_t* ib;
+            const tbh::GemvSeg& g0 = a.seg[s];
+            row_ptrs<LAYOUT>(g0, a.cols, r0, v, ib);
+            prefetch_row<LAYOUT>(a.cols, v, ib);
+            const tbh::GemvSeg& g1 = EPI == tbh::kSwiglu ? a.seg[1] : a.seg[s];
+            row_ptrs<LAYOUT>(g1, a.cols, r1, v, ib);
+            prefetch_row<LAYOUT>(a.cols, v, ib);
+        }
+    }
+    pdl_wait();
+    if (a.advance && blockIdx.x == 0 && threadIdx.x == 0) *a.advance += 1;
+    const float4* x4 = reinterpret_cast<const float4*>(a.x);
+    int pos = 0;
+    if (EPI == tbh::kRope) pos = *a.pos;
+    for (int64_t u = first;; u += warps) {
+        int s;
+        int64_t r0, r1;
+        if (!unit_rows<EPI>(a, u, s, r0, r1)) break;
+        const tbh::GemvSeg& g0 = a.seg[s];
+        const tbh::GemvSeg& g1 = EPI == tbh::kSwiglu ? a.seg[1] : a.seg[s];
+        const float4 *v0, *v1;
+        const uint8_t *i0, *i1;
+        row_ptrs<LAYOUT>(g0, a.cols, r0, v0, i0);
+        row_ptrs<LAYOUT>(g1, a.cols, r1, v1, i1);
+        float a0 = 0.0f, a1 = 0.0f;
+        if (LAYOUT == tbh::kDense)
+            tbk::dense_dot2(v0, v1, a.cols / 4, x4, lane, a0, a1);
+        else
+            tbk::packed_dot2(v0, i0, v1, i1, a.cols / 8, x4, lane, a0, a1);
+        tbk::warp_sum2(a0, a1);
+        if (lane != 0) continue;
+        if (EPI == tbh::kSwiglu) {
+            a.act[r0] = __fmul_rn(tbk::silu_f(a0), a1);
+        } else if (EPI == tbh::kResidual) {
+            g0.y[r0] = __fadd_rn(a.res[r0], a0);
+            if (r1 != r0) g0.y[r1] = __fadd_rn(a.res[r1], a1);
+        } else {
+            if (EPI == tbh::kRope && s < a.rope_segs && r1 != r0) {
+                if (pos >= 0 && pos < a.rope_positions) {
+                    const int half = a.head_dim / 2;
+                    const float2 cs = a.rope[(int64_t)pos * half + (r0 % a.head_dim) / 2];
+                    tbk::rope_rotate(a0, a1, cs.x, cs.y);
+                } else {
+                    atomicOr(a.status, TB_B200_FLAG_POSITION_RANGE);
+                }
+            }
+            g0.y[r0] = a0;
+            if (r1 != r0) g0.y[r1] = a1;
+        }
+    }
+}
+
+// RMSNorm of one vector (tb_cpu_rms_norm_f32, src/ops/norm.c:4-26): one CTA.
+__global__ void __launch_bounds__(1024)
+k_rnorm(int64_t n, const float* x, const float* __restrict__ w, float* y, float eps) {
+    __shared__ float red[32];
+    pdl_wait();
+    float ss = 0.0f;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) ss = __fmaf_rn(x[i], x[i], ss);
+    ss = tbk::group_sum(ss, blockDim.x, red);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(__fadd_rn(ss, eps), (float)n)));
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+        float o = __fmul_rn(x[i], scale);
+        if (w) o = __fmul_rn(o, w[i]);
+        y[i] = o;
+    }
+}
+
+template <typename... P, typename... A>
+int launch_pdl(void (*kernel)(P...), int grid, int threads, cudaStream_t s, A&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3((unsigned)threads);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<A>(args)...);
+    tbh::count_launch();
+    if (e != cudaSuccess) {
+        tbh::set_error("runner kernel launch", e);
+        return TB_ERR_DEVICE;
+    }
+    return TB_OK;
+}
+
+template <int LAYOUT>
+int fgemv_layout(const GemvArgs& a, int epi, int grid, cudaStream_t s) {
+    switch (epi) {
+        case tbh::kPlain: return launch_pdl(k_fgemv<LAYOUT, tbh::kPlain>, grid, kThreads, s, a);
+        case tbh::kResidual: return launch_pdl(k_fgemv<LAYOUT, tbh::kResidual>, grid, kThreads, s, a);
+        case tbh::kRope: return launch_pdl(k_fgemv<LAYOUT, tbh::kRope>, grid, kThreads, s, a);
+        case tbh::kSwiglu: return launch_pdl(k_fgemv<LAYOUT, tbh::kSwiglu>, grid, kThreads, s, a);
+        default: return TB_ERR_INVALID_ARG;
+    }
+}
+
+}  // namespace
+
+namespace tbh {
+
+int fused_gemv(const GemvArgs& a, int layout, int epi, cudaStream_t s) {
+    const DeviceState* ds = current_device_state();
+    if (!ds) return TB_ERR_DEVICE;
+    if (a.nseg < 1 || a.nseg > 3 || (epi == kSwiglu && a.nseg != 2)) return TB_ERR_INVALID_ARG;
+    int64_t units = 0;
+    if (epi == kSwiglu) {
+        if (a.seg[0].rows != a.seg[1].rows) return TB_ERR_INVALID_SHAPE;
+        units = a.seg[0].rows;
+    } else {
+        for (int i = 0; i < a.nseg; ++i) units += (a.seg[i].rows + 1) / 2;
+    }
+    if (units == 0) return TB_OK;
+    const int grid = ew_grid(units, kWarps, ds, 8);
+    return layout == kDense ? fgemv_layout<kDense>(a, epi, grid, s)
+                            : fgemv_layout<kPacked>(a, epi, grid, s);
+}
+
+int runner_norm(int64_t n, const float* x, const float* w, float* y, float eps, cudaStream_t s) {
+    return launch_pdl(k_rnorm, 1, 1024, s, n, x, w, y, eps);
+}
+
+}  // namespace tbh

@@ -14,16 +14,16 @@
 //
 // Packing runs once (a model load); a group with three or four mask bits set
 // cannot be packed and is reported, so the caller keeps the dense layout.
-// The GEMV gives each warp two output rows, so each float4 of x loaded
-// through L1 serves both; lanes take consecutive group pairs, four in flight.
-#include "tb_device.cuh"
+// The GEMV is tbk::packed_dot2 (gemv.cuh): two output rows per warp, so each
+// float4 of x loaded through L1 serves both, four pairs per lane and row in
+// flight, the index bytes laid out so each lane loads its four as one word.
+#include "gemv.cuh"
 #include "tb_internal.h"
 
 namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kU = 4;  // group pairs in flight per lane and row
 
 // Pack pair p of row j: groups 2p and 2p+1 (columns 8p .. 8p+7).
 __global__ void __launch_bounds__(kThreads)
@@ -31,6 +31,7 @@ k_pack24(int64_t rows, int64_t groups, int64_t in_f, const float* __restrict__ w
          const uint8_t* __restrict__ mask, float4* __restrict__ vals, uint8_t* __restrict__ idx,
          int* __restrict__ unpackable) {
     const int64_t pairs = (groups + 1) / 2;
+    const int64_t istride = tbk::packed_idx_stride(pairs);
     const int64_t total = rows * pairs;
     for (int64_t t = (int64_t)blockIdx.x * kThreads + threadIdx.x; t < total;
          t += (int64_t)gridDim.x * kThreads) {
@@ -58,68 +59,29 @@ k_pack24(int64_t rows, int64_t groups, int64_t in_f, const float* __restrict__ w
             if (slot == 1) ib |= (uint32_t)first << (4 * h + 2);  // unused slot: value 0
         }
         vals[t] = make_float4(v[0], v[1], v[2], v[3]);
-        idx[t] = (uint8_t)ib;
+        const int64_t r = p % tbk::kGemvStep;  // byte of pair p: 128 s + 4 l + u
+        idx[j * istride + (p - r) + 4 * (r % 32) + r / 32] = (uint8_t)ib;
     }
 }
 
-__device__ __forceinline__ float pick(const float4& x, uint32_t k) {
-    return k == 0 ? x.x : k == 1 ? x.y : k == 2 ? x.z : x.w;
-}
-
-__device__ __forceinline__ float pair_dot(const float4& v, uint32_t ib, const float4& xa,
-                                          const float4& xb, float acc) {
-    acc = __fmaf_rn(v.x, pick(xa, ib & 3u), acc);
-    acc = __fmaf_rn(v.y, pick(xa, (ib >> 2) & 3u), acc);
-    acc = __fmaf_rn(v.z, pick(xb, (ib >> 4) & 3u), acc);
-    acc = __fmaf_rn(v.w, pick(xb, ib >> 6), acc);
-    return acc;
-}
-
-// Two output rows per warp; `pairs` group pairs per row (groups even).
+// Two output rows per warp (the same row twice for an odd last row).
 __global__ void __launch_bounds__(kThreads)
-k_linear24(int64_t rows, int64_t pairs, const float* __restrict__ x,
-           const float4* __restrict__ vals, const uint8_t* __restrict__ idx,
-           const float* bias, float* y) {
+k_linear24(int64_t rows, int64_t pairs, int64_t istride, const float* __restrict__ x,
+           const float4* __restrict__ vals, const uint8_t* __restrict__ idx, const float* bias,
+           float* y) {
     const int lane = threadIdx.x & 31;
     const int64_t warps = (int64_t)gridDim.x * kWarps;
     const float4* x4 = reinterpret_cast<const float4*>(x);
     for (int64_t j0 = 2 * ((int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5)); j0 < rows;
          j0 += 2 * warps) {
-        const bool two = j0 + 1 < rows;
-        const float4* v0 = vals + j0 * pairs;
-        const float4* v1 = two ? v0 + pairs : v0;
-        const uint8_t* i0 = idx + j0 * pairs;
-        const uint8_t* i1 = two ? i0 + pairs : i0;
+        const int64_t j1 = j0 + 1 < rows ? j0 + 1 : j0;
         float a0 = 0.0f, a1 = 0.0f;
-        for (int64_t p0 = lane; p0 < pairs; p0 += 32 * kU) {
-            float4 w0[kU], w1[kU];
-            uint32_t b0[kU], b1[kU];
-#pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                const int64_t p = p0 + 32 * u;
-                const bool in = p < pairs;
-                w0[u] = in ? __ldcs(v0 + p) : make_float4(0.f, 0.f, 0.f, 0.f);
-                w1[u] = in ? __ldcs(v1 + p) : make_float4(0.f, 0.f, 0.f, 0.f);
-                b0[u] = in ? (uint32_t)__ldcs(i0 + p) : 0u;
-                b1[u] = in ? (uint32_t)__ldcs(i1 + p) : 0u;
-            }
-#pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                const int64_t p = p0 + 32 * u;
-                if (p >= pairs) break;
-                const float4 xa = __ldg(x4 + 2 * p), xb = __ldg(x4 + 2 * p + 1);
-                a0 = pair_dot(w0[u], b0[u], xa, xb, a0);
-                a1 = pair_dot(w1[u], b1[u], xa, xb, a1);
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            a0 = __fadd_rn(a0, __shfl_xor_sync(tbk::kFull, a0, o));
-            a1 = __fadd_rn(a1, __shfl_xor_sync(tbk::kFull, a1, o));
-        }
+        tbk::packed_dot2(vals + j0 * pairs, idx + j0 * istride, vals + j1 * pairs,
+                         idx + j1 * istride, pairs, x4, lane, a0, a1);
+        tbk::warp_sum2(a0, a1);
         if (lane == 0) {
             y[j0] = bias ? __fadd_rn(bias[j0], a0) : a0;
-            if (two) y[j0 + 1] = bias ? __fadd_rn(bias[j0 + 1], a1) : a1;
+            if (j1 != j0) y[j1] = bias ? __fadd_rn(bias[j1], a1) : a1;
         }
     }
 }
@@ -153,7 +115,8 @@ extern "C" int tb_b200_sparse24_linear(int64_t out_features, int64_t in_features
     if (out_features == 0) return TB_OK;
     const int64_t groups = in_features / 4;
     if (groups % 2) return TB_ERR_INVALID_SHAPE;  // whole pairs: in_features / 4 even
-    if (!tbh::aligned16(x) || !tbh::aligned16(vals)) return TB_ERR_INVALID_ARG;
+    if (!tbh::aligned16(x) || !tbh::aligned16(vals) || reinterpret_cast<uintptr_t>(idx) % 4)
+        return TB_ERR_INVALID_ARG;
     const tbh::DeviceState* ds = tbh::current_device_state();
     if (!ds) return TB_ERR_DEVICE;
     cudaStream_t s = tbh::stream_of(stream);
@@ -165,7 +128,8 @@ extern "C" int tb_b200_sparse24_linear(int64_t out_features, int64_t in_features
         return TB_OK;
     }
     const int grid = tbh::ew_grid((out_features + 1) / 2, kWarps, ds, 16);
-    k_linear24<<<grid, kThreads, 0, s>>>(out_features, groups / 2, x,
+    k_linear24<<<grid, kThreads, 0, s>>>(out_features, groups / 2,
+                                         tbk::packed_idx_stride(groups / 2), x,
                                          static_cast<const float4*>(vals), idx, bias, y);
     TB_LAUNCH_CHECK("2:4 packed linear kernel");
     return TB_OK;

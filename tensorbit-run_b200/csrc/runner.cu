@@ -21,14 +21,14 @@
 // use, to the same values).
 #include <cmath>
 #include <cstring>
+#include <initializer_list>
 #include <new>
 #include <vector>
 
+#include "gemv.cuh"
 #include "tb_internal.h"
 
-namespace tbh {
-int decode_attention_setup(int head_dim, int max_seq);
-}
+#include "runner_kernels.h"
 
 namespace {
 
@@ -169,7 +169,7 @@ int pack(Runner* r, Proj* p) {
     void *vals = nullptr, *idx = nullptr;
     int rc;
     if ((rc = dev_alloc(r, (size_t)(p->rows * pairs) * 16, &vals))) return rc;
-    if ((rc = dev_alloc(r, (size_t)(p->rows * pairs), &idx))) return rc;
+    if ((rc = dev_alloc(r, (size_t)(p->rows * tbk::packed_idx_stride(pairs)), &idx))) return rc;
     TB_CUDA_TRY(cudaMemsetAsync(r->flag, 0, sizeof(int), r->stream));
     if ((rc = tb_b200_sparse24_pack(p->rows, p->cols, p->w, p->mask, vals, (uint8_t*)idx, r->flag,
                                     r->stream)))
@@ -214,53 +214,134 @@ int project(Runner* r, const Proj& p, const float* x, const float* res, float* y
     return tb_b200_dense_linear(p.rows, p.cols, x, p.w, res, y, r->stream);
 }
 
-// The token's decoder step, queued on the runner's stream.
+// The fused-GEMV layout a projection can take (k_runner.cu), or -1.
+int fused_layout(const Proj& p) {
+    if (!p.w) return -1;
+    if (p.vals) return p.cols % 8 == 0 ? tbh::kPacked : -1;
+    if (p.mask) return -1;  // dense-with-mask: the library's sparse GEMV
+    return p.cols % 4 == 0 && tbh::aligned16(p.w) ? tbh::kDense : -1;
+}
+
+int common_layout(const Proj& a, const Proj& b, const Proj* c = nullptr) {
+    const int l = fused_layout(a);
+    if (l < 0 || fused_layout(b) != l || (c && fused_layout(*c) != l)) return -1;
+    return l;
+}
+
+tbh::GemvSeg seg_of(const Proj& p, float* y) {
+    tbh::GemvSeg g;
+    g.w = p.vals ? p.vals : p.w;
+    g.idx = p.idx;
+    g.y = y;
+    g.rows = p.rows;
+    return g;
+}
+
+// One fused GEMV over 1-3 projections sharing the input x.
+int fused(Runner* r, int layout, int epi, std::initializer_list<tbh::GemvSeg> segs,
+          const float* x, int64_t cols, float* act = nullptr, int32_t* advance = nullptr) {
+    const TbB200RunnerDesc& c = r->cfg;
+    tbh::GemvArgs a{};
+    int n = 0;
+    for (const tbh::GemvSeg& g : segs) a.seg[n++] = g;
+    a.nseg = n;
+    a.cols = cols;
+    a.x = x;
+    a.res = epi == tbh::kResidual ? a.seg[0].y : nullptr;
+    a.act = act;
+    a.rope = reinterpret_cast<const float2*>(r->rope);
+    a.rope_positions = c.max_seq;
+    a.pos = r->dstate;
+    a.head_dim = c.head_dim;
+    a.rope_segs = 2;
+    a.advance = advance;
+    const tbh::DeviceState* ds = tbh::current_device_state();
+    a.status = ds ? ds->status : nullptr;
+    r->launches++;
+    return tbh::fused_gemv(a, layout, epi, r->stream);
+}
+
+// The token's decoder step, queued on the runner's stream: 7 launches per
+// layer when every projection group shares a fused layout.
 int enqueue(Runner* r) {
     const TbB200RunnerDesc& c = r->cfg;
     const int H = c.hidden;
-    void* s = r->stream;
+    cudaStream_t s = r->stream;
     int rc;
     r->launches = 0;
-#define TRY(call)                    \
-    do {                             \
+#define TRY(call)                              \
+    do {                                       \
         if ((rc = (call)) != TB_OK) return rc; \
     } while (0)
     TRY(tb_b200_embedding(TB_DTYPE_F32, 1, H, c.vocab, r->dstate + 1, r->embed, r->x, s));
     r->launches++;
     for (const Layer& L : r->layers) {
         if (!L.q.w || !L.k.w || !L.v.w) continue;  // ops.hpp:109
-        TRY(tb_b200_rms_norm(TB_DTYPE_F32, 1, H, r->x, L.in_norm, r->x, c.norm_eps, s));
+        TRY(tbh::runner_norm(H, r->x, L.in_norm, r->x, c.norm_eps, s));
         r->launches++;
-        TRY(project(r, L.q, r->x, nullptr, r->q));
-        TRY(project(r, L.k, r->x, nullptr, r->k));
-        TRY(project(r, L.v, r->x, nullptr, r->v));
-        TRY(tb_b200_rope_rows(TB_DTYPE_F32, 1, c.n_heads, c.n_kv_heads, c.head_dim, r->q, r->k,
-                              r->dstate, c.rope_theta, r->rope, c.max_seq, s));
-        r->launches++;
+        const int lqkv = common_layout(L.q, L.k, &L.v);
+        if (lqkv >= 0) {
+            TRY(fused(r, lqkv, tbh::kRope,
+                      {seg_of(L.q, r->q), seg_of(L.k, r->k), seg_of(L.v, r->v)}, r->x, H));
+        } else {
+            TRY(project(r, L.q, r->x, nullptr, r->q));
+            TRY(project(r, L.k, r->x, nullptr, r->k));
+            TRY(project(r, L.v, r->x, nullptr, r->v));
+            TRY(tb_b200_rope_rows(TB_DTYPE_F32, 1, c.n_heads, c.n_kv_heads, c.head_dim, r->q, r->k,
+                                  r->dstate, c.rope_theta, r->rope, c.max_seq, s));
+            r->launches++;
+        }
         const size_t layer_off = (size_t)(&L - r->layers.data()) * (size_t)c.max_seq *
                                  (size_t)c.n_kv_heads * (size_t)c.head_dim;
-        TRY(tb_b200_decode_attention(c.attention, c.n_heads, c.n_kv_heads, c.head_dim, c.max_seq,
-                                     r->dstate, r->q, r->k, r->v, r->kc + layer_off,
-                                     r->vc + layer_off, r->attn, s));
+        TRY(tbh::decode_attention_launch(c.attention, c.n_heads, c.n_kv_heads, c.head_dim,
+                                         c.max_seq, r->dstate, r->q, r->k, r->v,
+                                         r->kc + layer_off, r->vc + layer_off, r->attn, s, true));
         r->launches++;
-        if (L.o.w) TRY(project(r, L.o, r->attn, r->x, r->x));  // ops.hpp:207-218
-        TRY(tb_b200_rms_norm(TB_DTYPE_F32, 1, H, r->x, L.post_norm, r->xm, c.norm_eps, s));
+        if (L.o.w) {  // ops.hpp:207-218
+            const int lo = fused_layout(L.o);
+            if (lo >= 0)
+                TRY(fused(r, lo, tbh::kResidual, {seg_of(L.o, r->x)}, r->attn, L.o.cols));
+            else
+                TRY(project(r, L.o, r->attn, r->x, r->x));
+        }
+        TRY(tbh::runner_norm(H, r->x, L.post_norm, r->xm, c.norm_eps, s));
         r->launches++;
         if (L.gate.w && L.up.w && c.intermediate > 0) {  // ops.hpp:226-256
-            TRY(project(r, L.gate, r->xm, nullptr, r->g));
-            TRY(project(r, L.up, r->xm, nullptr, r->u));
-            TRY(tb_b200_swiglu(TB_DTYPE_F32, c.intermediate, r->g, r->u, r->g, s));
-            r->launches++;
-            if (L.down.w) TRY(project(r, L.down, r->g, r->x, r->x));
+            const int lgu = common_layout(L.gate, L.up);
+            if (lgu >= 0) {
+                TRY(fused(r, lgu, tbh::kSwiglu, {seg_of(L.gate, r->g), seg_of(L.up, r->u)}, r->xm,
+                          H, r->g));
+            } else {
+                TRY(project(r, L.gate, r->xm, nullptr, r->g));
+                TRY(project(r, L.up, r->xm, nullptr, r->u));
+                TRY(tb_b200_swiglu(TB_DTYPE_F32, c.intermediate, r->g, r->u, r->g, s));
+                r->launches++;
+            }
+            if (L.down.w) {
+                const int ld = fused_layout(L.down);
+                if (ld >= 0)
+                    TRY(fused(r, ld, tbh::kResidual, {seg_of(L.down, r->x)}, r->g, L.down.cols));
+                else
+                    TRY(project(r, L.down, r->g, r->x, r->x));
+            }
         }
     }
-    TRY(tb_b200_rms_norm(TB_DTYPE_F32, 1, H, r->x, r->final_norm, r->x, c.norm_eps, s));
+    TRY(tbh::runner_norm(H, r->x, r->final_norm, r->x, c.norm_eps, s));
     r->launches++;
-    TRY(tb_b200_dense_linear(c.vocab, H, r->x, r->lm_head, nullptr, r->logits, s));
-    r->launches++;
-    k_advance<<<1, 1, 0, r->stream>>>(r->dstate);
-    TB_LAUNCH_CHECK("runner position kernel");
-    r->launches++;
+    Proj lm;
+    lm.w = r->lm_head;
+    lm.rows = c.vocab;
+    lm.cols = H;
+    const int ll = fused_layout(lm);
+    if (ll >= 0) {  // the logits, then position += 1 (ops.hpp:269-284)
+        TRY(fused(r, ll, tbh::kPlain, {seg_of(lm, r->logits)}, r->x, H, nullptr, r->dstate));
+    } else {
+        TRY(tb_b200_dense_linear(c.vocab, H, r->x, r->lm_head, nullptr, r->logits, s));
+        r->launches++;
+        k_advance<<<1, 1, 0, s>>>(r->dstate);
+        TB_LAUNCH_CHECK("runner position kernel");
+        r->launches++;
+    }
 #undef TRY
     return TB_OK;
 }

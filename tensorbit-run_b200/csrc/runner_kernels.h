@@ -1,0 +1,48 @@
+// runner_kernels.h -- the fused kernels of the device decoder step
+// (k_runner.cu, k_attention.cu) as runner.cu launches them.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace tbh {
+
+struct GemvSeg {
+    const void* w;       // dense f32 [rows, cols], or the packed float4 values
+    const uint8_t* idx;  // packed index bytes (packed layout only)
+    float* y;            // output [rows]
+    int64_t rows;
+};
+
+enum GemvLayout { kDense = 0, kPacked = 1 };
+enum GemvEpi { kPlain = 0, kResidual = 1, kRope = 2, kSwiglu = 3 };
+
+struct GemvArgs {
+    GemvSeg seg[3];
+    int nseg;
+    int64_t cols;        // input features
+    const float* x;      // input vector [cols]
+    const float* res;    // kResidual: y = res + W x (res may be y)
+    float* act;          // kSwiglu: output [rows]
+    const float2* rope;  // kRope: (cos, sin) table [rope_positions, head_dim / 2]
+    int rope_positions;
+    const int32_t* pos;  // kRope: device position
+    int head_dim;
+    int rope_segs;       // segments 0 .. rope_segs-1 are rotated
+    int32_t* advance;    // non-null: *advance += 1 once the kernel has run
+    unsigned* status;
+};
+
+// One fused GEMV launch over 1-3 segments sharing x (programmatic dependent
+// launch).  layout kDense needs cols % 4 == 0, kPacked cols % 8 == 0; x and
+// the weights 16-byte aligned.  kSwiglu takes two segments of equal rows.
+int fused_gemv(const GemvArgs& a, int layout, int epi, cudaStream_t s);
+// RMSNorm of one f32 vector, one CTA, programmatic dependent launch.
+int runner_norm(int64_t n, const float* x, const float* w, float* y, float eps, cudaStream_t s);
+// Opt the attention kernels in to the shared memory max_seq keys need.
+int decode_attention_setup(int head_dim, int max_seq);
+int decode_attention_launch(int mode, int n_heads, int n_kv_heads, int head_dim, int max_seq,
+                            const int32_t* position, const float* q, const float* k,
+                            const float* v, float* k_cache, float* v_cache, float* out,
+                            cudaStream_t s, bool pdl);
+
+}  // namespace tbh

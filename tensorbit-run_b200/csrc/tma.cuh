@@ -85,6 +85,12 @@ __device__ __forceinline__ void prefetch_l2_hint(const void* src_gmem, uint32_t 
                  : "memory");
 }
 
+// The same prefetch with the default L2 policy.
+__device__ __forceinline__ void prefetch_l2(const void* src_gmem, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src_gmem), "r"(bytes)
+                 : "memory");
+}
+
 // 16-byte global load, not allocated in L1, with an L2 cache policy.
 __device__ __forceinline__ float4 ld_f4_hint(const float4* p, uint64_t policy) {
     float4 v;

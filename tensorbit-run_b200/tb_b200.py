@@ -399,12 +399,13 @@ def linear(x, w, mask=None, bias=None, nm_n=2, nm_m=4, y=None, stream=None):
 
 def sparse24_pack(w, mask, stream=None):
     """Pack a 2:4-masked f32 [out, in] weight: (vals float32 [out, P, 4],
-    idx uint8 [out, P], packable) with P = ceil((in / 4) / 2)."""
+    idx uint8 [out, S], packable) with P = ceil((in / 4) / 2) and S = P
+    rounded up to a multiple of 128."""
     torch = _torch()
     out_f, in_f = w.shape
     pairs = (in_f // 4 + 1) // 2
     vals = torch.empty((out_f, pairs, 4), dtype=torch.float32, device=w.device)
-    idx = torch.empty((out_f, pairs), dtype=torch.uint8, device=w.device)
+    idx = torch.empty((out_f, (pairs + 127) // 128 * 128), dtype=torch.uint8, device=w.device)
     flag = torch.zeros(1, dtype=torch.int32, device=w.device)
     _dev(w, mask)
     check(lib().tb_b200_sparse24_pack(out_f, in_f, ptr(w), ptr(mask), ptr(vals), ptr(idx),
