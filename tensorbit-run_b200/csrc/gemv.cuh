@@ -42,13 +42,23 @@ __device__ __forceinline__ float pair_dot(const float4& v, uint32_t ib, const fl
     return acc;
 }
 
+// x through the read-only path from global memory, or from shared memory.
+template <bool XS>
+__device__ __forceinline__ float4 ldx(const float4* p) {
+    if constexpr (XS)
+        return *p;
+    else
+        return __ldg(p);
+}
+
 // Partial sums of two packed rows (v0/i0 and v1/i1; pass the same row twice
-// for one).  pairs: P; istride: the padded idx row length in bytes.
+// for one).  pairs: P.  XS: x4 points to shared memory.
+template <bool XS = false>
 __device__ __forceinline__ void packed_dot2(const float4* __restrict__ v0,
                                             const uint8_t* __restrict__ i0,
                                             const float4* __restrict__ v1,
                                             const uint8_t* __restrict__ i1, int64_t pairs,
-                                            const float4* __restrict__ x4, int lane, float& a0,
+                                            const float4* x4, int lane, float& a0,
                                             float& a1) {
     const int64_t full = pairs / kGemvStep;
     const float4* p0 = v0 + lane;
@@ -70,7 +80,7 @@ __device__ __forceinline__ void packed_dot2(const float4* __restrict__ v0,
         q1 += 32;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-            const float4 xa = __ldg(xp + 64 * u), xb = __ldg(xp + 64 * u + 1);
+            const float4 xa = ldx<XS>(xp + 64 * u), xb = ldx<XS>(xp + 64 * u + 1);
             a0 = pair_dot(w0[u], b0 >> (8 * u), xa, xb, a0);
             a1 = pair_dot(w1[u], b1 >> (8 * u), xa, xb, a1);
         }
@@ -79,7 +89,7 @@ __device__ __forceinline__ void packed_dot2(const float4* __restrict__ v0,
     for (int u = 0; u < 4; ++u) {  // the partial step
         const int64_t p = full * kGemvStep + 32 * u + lane;
         if (p >= pairs) break;
-        const float4 xa = __ldg(x4 + 2 * p), xb = __ldg(x4 + 2 * p + 1);
+        const float4 xa = ldx<XS>(x4 + 2 * p), xb = ldx<XS>(x4 + 2 * p + 1);
         const int64_t ib = full * kGemvStep + 4 * lane + u;
         a0 = pair_dot(__ldcs(v0 + p), i0[ib], xa, xb, a0);
         a1 = pair_dot(__ldcs(v1 + p), i1[ib], xa, xb, a1);
@@ -87,9 +97,10 @@ __device__ __forceinline__ void packed_dot2(const float4* __restrict__ v0,
 }
 
 // Partial sums of two dense rows of n4 float4s each.
+template <bool XS = false>
 __device__ __forceinline__ void dense_dot2(const float4* __restrict__ w0,
                                            const float4* __restrict__ w1, int64_t n4,
-                                           const float4* __restrict__ x4, int lane, float& a0,
+                                           const float4* x4, int lane, float& a0,
                                            float& a1) {
     const int64_t full = n4 / kGemvStep;
     const float4* p0 = w0 + lane;
@@ -106,7 +117,7 @@ __device__ __forceinline__ void dense_dot2(const float4* __restrict__ w0,
         p1 += kGemvStep;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-            const float4 xv = __ldg(xp + 32 * u);
+            const float4 xv = ldx<XS>(xp + 32 * u);
             a0 = __fmaf_rn(xv.x, r0[u].x, a0);
             a0 = __fmaf_rn(xv.y, r0[u].y, a0);
             a0 = __fmaf_rn(xv.z, r0[u].z, a0);
@@ -121,7 +132,7 @@ __device__ __forceinline__ void dense_dot2(const float4* __restrict__ w0,
     for (int u = 0; u < 4; ++u) {
         const int64_t v = full * kGemvStep + 32 * u + lane;
         if (v >= n4) break;
-        const float4 xv = __ldg(x4 + v), r0 = __ldcs(w0 + v), r1 = __ldcs(w1 + v);
+        const float4 xv = ldx<XS>(x4 + v), r0 = __ldcs(w0 + v), r1 = __ldcs(w1 + v);
         a0 = __fmaf_rn(xv.x, r0.x, a0);
         a0 = __fmaf_rn(xv.y, r0.y, a0);
         a0 = __fmaf_rn(xv.z, r0.z, a0);

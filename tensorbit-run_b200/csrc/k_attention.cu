@@ -14,10 +14,10 @@
 // TB_B200_ATTN_STANDARD computes query row p of every head (every key).
 // Query head h reads k/v head h / (n_heads / n_kv_heads).
 //
-// One CTA per output row.  The scores use one thread per key with the
-// reference's in-order FMA chain over the head dimension, so they match it
-// bit for bit; max and sum are block reductions (a different order from the
-// reference's loops: the sum agrees within its rounding); the weighted sum
+// One CTA per output row.  The scores give each warp a key at a time (four
+// in flight), the lanes across the head dimension with a shuffle-tree sum;
+// max and sum are block reductions -- orders other than the reference's
+// left-to-right loops, so the results agree within f32 rounding; the weighted sum
 // of v gives each warp a contiguous run of keys and each lane its own
 // columns, then adds the warps' partials in warp order.  The token's own
 // key and value are read from the fresh k/v vectors, and CTA 0 writes them
@@ -41,7 +41,8 @@ k_decode_attention(int mode, int hq, int hkv, int d, int max_seq, const int32_t*
                    const float* __restrict__ q, const float* __restrict__ k_new,
                    const float* __restrict__ v_new, float* kc, float* vc, float* __restrict__ out,
                    float scale, unsigned* status) {
-    extern __shared__ float sm[];
+    extern __shared__ float4 sm4[];  // 16-byte aligned for the float4 view of q
+    float* sm = reinterpret_cast<float*>(sm4);
     __shared__ float red[kWarps];
     // under programmatic dependent launch, wait for the producer of q/k/v
     // (returns at once otherwise)
@@ -77,27 +78,43 @@ k_decode_attention(int mode, int hq, int hkv, int d, int max_seq, const int32_t*
     for (int i = threadIdx.x; i < d; i += kT) qs[i] = q[(int64_t)h * d + i];
     __syncthreads();
 
-    // scores: one thread per key, in-order FMA over the head dimension
+    // scores: a warp per key, lanes across the head dimension, four keys in
+    // flight per warp; the lanes' partial dots meet in a shuffle tree
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float lmax = -INFINITY;
-    for (int j = threadIdx.x; j < n; j += kT) {
-        const float* kj = j == pos ? k_new + (int64_t)g * d : kc + (int64_t)j * kv_dim + (int64_t)g * d;
-        float s = 0.0f;
-        if (VEC == 4) {
-            const float4* k4 = reinterpret_cast<const float4*>(kj);
-            for (int i = 0; i < d / 4; ++i) {
-                const float4 kv = k4[i];
-                s = __fmaf_rn(qs[4 * i], kv.x, s);
-                s = __fmaf_rn(qs[4 * i + 1], kv.y, s);
-                s = __fmaf_rn(qs[4 * i + 2], kv.z, s);
-                s = __fmaf_rn(qs[4 * i + 3], kv.w, s);
+    for (int j0 = 4 * warp; j0 < n; j0 += 4 * kWarps) {
+        float sj[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const int j = j0 + t;
+            if (j >= n) break;
+            const float* kj =
+                j == pos ? k_new + (int64_t)g * d : kc + (int64_t)j * kv_dim + (int64_t)g * d;
+            if (VEC == 4) {
+                const float4* k4 = reinterpret_cast<const float4*>(kj);
+                const float4* q4 = reinterpret_cast<const float4*>(qs);
+                for (int i = lane; i < d / 4; i += 32) {
+                    const float4 kv = k4[i], qv = q4[i];
+                    sj[t] = __fmaf_rn(qv.x, kv.x, sj[t]);
+                    sj[t] = __fmaf_rn(qv.y, kv.y, sj[t]);
+                    sj[t] = __fmaf_rn(qv.z, kv.z, sj[t]);
+                    sj[t] = __fmaf_rn(qv.w, kv.w, sj[t]);
+                }
+            } else {
+                for (int i = lane; i < d; i += 32) sj[t] = __fmaf_rn(qs[i], kj[i], sj[t]);
             }
-        } else {
-            for (int i = 0; i < d; ++i) s = __fmaf_rn(qs[i], kj[i], s);
         }
-        s = __fmul_rn(s, scale);
-        sc[j] = s;
-        lmax = fmaxf(lmax, s);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const int j = j0 + t;
+            const float sv = __fmul_rn(tbk::warp_sum(sj[t]), scale);
+            if (j < n) {
+                if (lane == 0) sc[j] = sv;
+                lmax = fmaxf(lmax, sv);
+            }
+        }
     }
+    __syncthreads();  // the scores in shared memory before the other passes
     const float m = tbk::block_max(lmax, red);
     float lsum = 0.0f;
     for (int j = threadIdx.x; j < n; j += kT) {
@@ -112,7 +129,6 @@ k_decode_attention(int mode, int hq, int hkv, int d, int max_seq, const int32_t*
 
     // y = sum_j p_j v_j: warp w takes keys [j0, j1), lane owns columns
     // lane, lane + 32, ...
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int per = (n + kWarps - 1) / kWarps;
     const int j0 = min(n, warp * per), j1 = min(n, j0 + per);
     float acc[kMaxD / 32];

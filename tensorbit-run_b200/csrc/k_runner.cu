@@ -26,6 +26,8 @@
 #include "tb_internal.h"
 #include "tma.cuh"
 
+#include <utility>
+
 #include "runner_kernels.h"
 
 namespace {
@@ -78,11 +80,13 @@ __device__ __forceinline__ void row_ptrs(const tbh::GemvSeg& g, int64_t cols, in
     }
 }
 
-// L2 prefetch of one weight row (at most 64 KB of it; sizes are multiples
-// of 16 bytes and rows start 16-byte aligned).
+// L2 prefetch of the start of one weight row: enough for the warp's first
+// step, little enough that the prefetches of every resident warp stay far
+// below the L2 (whole rows of a 200 MB projection group would evict each
+// other).  Sizes are multiples of 16 bytes; rows start 16-byte aligned.
 template <int LAYOUT>
 __device__ __forceinline__ void prefetch_row(int64_t cols, const float4* v, const uint8_t* ib) {
-    constexpr int64_t kCap = 64 * 1024;
+    constexpr int64_t kCap = 2048;
     if (LAYOUT == tbh::kDense) {
         tbk::prefetch_l2(v, (uint32_t)min(cols * 4, kCap));
     } else {
@@ -92,8 +96,10 @@ __device__ __forceinline__ void prefetch_row(int64_t cols, const float4* v, cons
     }
 }
 
-template <int LAYOUT, int EPI>
+template <int LAYOUT, int EPI, bool NORM>
 __global__ void __launch_bounds__(kThreads) k_fgemv(const __grid_constant__ GemvArgs a) {
+    extern __shared__ float4 xs[];  // NORM: the normalised x
+    __shared__ float red[kWarps];
     const int lane = threadIdx.x & 31;
     const int64_t warps = (int64_t)gridDim.x * kWarps;
     const int64_t first = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
@@ -114,6 +120,41 @@ __global__ void __launch_bounds__(kThreads) k_fgemv(const __grid_constant__ Gemv
     pdl_wait();
     if (a.advance && blockIdx.x == 0 && threadIdx.x == 0) *a.advance += 1;
     const float4* x4 = reinterpret_cast<const float4*>(a.x);
+    const int64_t n4 = a.cols / 4;
+    if constexpr (NORM) {
+        // rms_norm(x) * w (src/ops/norm.c:4-26): every CTA sums the squares
+        // in the same order, so all hold the same scale
+        float ss = 0.0f;
+        for (int64_t i = threadIdx.x; i < n4; i += kThreads) {
+            const float4 v = x4[i];
+            ss = __fmaf_rn(v.x, v.x, ss);
+            ss = __fmaf_rn(v.y, v.y, ss);
+            ss = __fmaf_rn(v.z, v.z, ss);
+            ss = __fmaf_rn(v.w, v.w, ss);
+        }
+        ss = tbk::group_sum(ss, kThreads, red);
+        const float scale =
+            __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(__fadd_rn(ss, a.eps), (float)a.cols)));
+        const float4* w4 = reinterpret_cast<const float4*>(a.norm_w);
+        float4* out4 = blockIdx.x == 0 ? reinterpret_cast<float4*>(a.norm_out) : nullptr;
+        for (int64_t i = threadIdx.x; i < n4; i += kThreads) {
+            float4 v = x4[i];
+            v.x = __fmul_rn(v.x, scale);
+            v.y = __fmul_rn(v.y, scale);
+            v.z = __fmul_rn(v.z, scale);
+            v.w = __fmul_rn(v.w, scale);
+            if (w4) {
+                const float4 w = w4[i];
+                v.x = __fmul_rn(v.x, w.x);
+                v.y = __fmul_rn(v.y, w.y);
+                v.z = __fmul_rn(v.z, w.z);
+                v.w = __fmul_rn(v.w, w.w);
+            }
+            xs[i] = v;
+            if (out4) out4[i] = v;
+        }
+        __syncthreads();
+    }
     int pos = 0;
     if (EPI == tbh::kRope) pos = *a.pos;
     for (int64_t u = first;; u += warps) {
@@ -127,10 +168,11 @@ __global__ void __launch_bounds__(kThreads) k_fgemv(const __grid_constant__ Gemv
         row_ptrs<LAYOUT>(g0, a.cols, r0, v0, i0);
         row_ptrs<LAYOUT>(g1, a.cols, r1, v1, i1);
         float a0 = 0.0f, a1 = 0.0f;
+        const float4* xsrc = NORM ? xs : x4;
         if (LAYOUT == tbh::kDense)
-            tbk::dense_dot2(v0, v1, a.cols / 4, x4, lane, a0, a1);
+            tbk::dense_dot2<NORM>(v0, v1, n4, xsrc, lane, a0, a1);
         else
-            tbk::packed_dot2(v0, i0, v1, i1, a.cols / 8, x4, lane, a0, a1);
+            tbk::packed_dot2<NORM>(v0, i0, v1, i1, a.cols / 8, xsrc, lane, a0, a1);
         tbk::warp_sum2(a0, a1);
         if (lane != 0) continue;
         if (EPI == tbh::kSwiglu) {
@@ -171,10 +213,12 @@ k_rnorm(int64_t n, const float* x, const float* __restrict__ w, float* y, float 
 }
 
 template <typename... P, typename... A>
-int launch_pdl(void (*kernel)(P...), int grid, int threads, cudaStream_t s, A&&... args) {
+int launch_pdl(void (*kernel)(P...), int grid, int threads, size_t smem, cudaStream_t s,
+               A&&... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3((unsigned)threads);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -190,15 +234,28 @@ int launch_pdl(void (*kernel)(P...), int grid, int threads, cudaStream_t s, A&&.
     return TB_OK;
 }
 
+template <int LAYOUT, int EPI>
+int fgemv_norm(const GemvArgs& a, int grid, cudaStream_t s) {
+    if (a.norm)
+        return launch_pdl(k_fgemv<LAYOUT, EPI, true>, grid, kThreads, (size_t)a.cols * 4, s, a);
+    return launch_pdl(k_fgemv<LAYOUT, EPI, false>, grid, kThreads, 0, s, a);
+}
+
 template <int LAYOUT>
 int fgemv_layout(const GemvArgs& a, int epi, int grid, cudaStream_t s) {
     switch (epi) {
-        case tbh::kPlain: return launch_pdl(k_fgemv<LAYOUT, tbh::kPlain>, grid, kThreads, s, a);
-        case tbh::kResidual: return launch_pdl(k_fgemv<LAYOUT, tbh::kResidual>, grid, kThreads, s, a);
-        case tbh::kRope: return launch_pdl(k_fgemv<LAYOUT, tbh::kRope>, grid, kThreads, s, a);
-        case tbh::kSwiglu: return launch_pdl(k_fgemv<LAYOUT, tbh::kSwiglu>, grid, kThreads, s, a);
+        case tbh::kPlain: return fgemv_norm<LAYOUT, tbh::kPlain>(a, grid, s);
+        case tbh::kResidual: return fgemv_norm<LAYOUT, tbh::kResidual>(a, grid, s);
+        case tbh::kRope: return fgemv_norm<LAYOUT, tbh::kRope>(a, grid, s);
+        case tbh::kSwiglu: return fgemv_norm<LAYOUT, tbh::kSwiglu>(a, grid, s);
         default: return TB_ERR_INVALID_ARG;
     }
+}
+
+template <int LAYOUT, int EPI>
+cudaError_t allow_smem(int bytes) {
+    return cudaFuncSetAttribute(k_fgemv<LAYOUT, EPI, true>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
 }  // namespace
@@ -223,7 +280,29 @@ int fused_gemv(const GemvArgs& a, int layout, int epi, cudaStream_t s) {
 }
 
 int runner_norm(int64_t n, const float* x, const float* w, float* y, float eps, cudaStream_t s) {
-    return launch_pdl(k_rnorm, 1, 1024, s, n, x, w, y, eps);
+    return launch_pdl(k_rnorm, 1, 1024, 0, s, n, x, w, y, eps);
+}
+
+// The normalising variants keep x (cols floats) in shared memory.
+int fused_gemv_setup(int64_t cols) {
+    const DeviceState* ds = current_device_state();
+    if (!ds) return TB_ERR_DEVICE;
+    const size_t bytes = (size_t)cols * 4;
+    if (bytes + 64 > ds->smem_optin) return TB_ERR_INVALID_SHAPE;
+    if (bytes <= 48 * 1024) return TB_OK;
+    const int b = (int)bytes;
+    cudaError_t e = cudaSuccess;
+    const cudaError_t r[] = {allow_smem<kDense, kPlain>(b),   allow_smem<kDense, kResidual>(b),
+                             allow_smem<kDense, kRope>(b),    allow_smem<kDense, kSwiglu>(b),
+                             allow_smem<kPacked, kPlain>(b),  allow_smem<kPacked, kResidual>(b),
+                             allow_smem<kPacked, kRope>(b),   allow_smem<kPacked, kSwiglu>(b)};
+    for (cudaError_t x : r)
+        if (x != cudaSuccess) e = x;
+    if (e != cudaSuccess) {
+        set_error("fused GEMV shared memory", e);
+        return TB_ERR_DEVICE;
+    }
+    return TB_OK;
 }
 
 }  // namespace tbh

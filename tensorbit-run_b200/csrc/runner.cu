@@ -57,7 +57,8 @@ struct Runner {
     const float* final_norm = nullptr;
     const float* lm_head = nullptr;
     std::vector<Layer> layers;
-    float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr;
+    float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr,
+          *attn = nullptr;
     float *xm = nullptr, *g = nullptr, *u = nullptr, *logits = nullptr;
     float *kc = nullptr, *vc = nullptr, *rope = nullptr;
     int32_t* dstate = nullptr;  // [0] position, [1] token
@@ -238,8 +239,15 @@ tbh::GemvSeg seg_of(const Proj& p, float* y) {
 }
 
 // One fused GEMV over 1-3 projections sharing the input x.
+struct Norm {  // the RMSNorm a fused GEMV applies to its input first
+    bool on = false;
+    const float* w = nullptr;
+    float* out = nullptr;
+};
+
 int fused(Runner* r, int layout, int epi, std::initializer_list<tbh::GemvSeg> segs,
-          const float* x, int64_t cols, float* act = nullptr, int32_t* advance = nullptr) {
+          const float* x, int64_t cols, const float* res = nullptr, float* act = nullptr,
+          Norm norm = Norm{}, int32_t* advance = nullptr) {
     const TbB200RunnerDesc& c = r->cfg;
     tbh::GemvArgs a{};
     int n = 0;
@@ -247,7 +255,11 @@ int fused(Runner* r, int layout, int epi, std::initializer_list<tbh::GemvSeg> se
     a.nseg = n;
     a.cols = cols;
     a.x = x;
-    a.res = epi == tbh::kResidual ? a.seg[0].y : nullptr;
+    a.res = res;
+    a.norm = norm.on ? 1 : 0;
+    a.norm_w = norm.w;
+    a.eps = c.norm_eps;
+    a.norm_out = norm.out;
     a.act = act;
     a.rope = reinterpret_cast<const float2*>(r->rope);
     a.rope_positions = c.max_seq;
@@ -261,8 +273,9 @@ int fused(Runner* r, int layout, int epi, std::initializer_list<tbh::GemvSeg> se
     return tbh::fused_gemv(a, layout, epi, r->stream);
 }
 
-// The token's decoder step, queued on the runner's stream: 7 launches per
-// layer when every projection group shares a fused layout.
+// The token's decoder step, queued on the runner's stream: 5 launches per
+// layer when every projection group shares a fused layout (the norms run as
+// the prologue of the GEMV that consumes them).
 int enqueue(Runner* r) {
     const TbB200RunnerDesc& c = r->cfg;
     const int H = c.hidden;
@@ -277,19 +290,28 @@ int enqueue(Runner* r) {
     r->launches++;
     for (const Layer& L : r->layers) {
         if (!L.q.w || !L.k.w || !L.v.w) continue;  // ops.hpp:109
-        TRY(tbh::runner_norm(H, r->x, L.in_norm, r->x, c.norm_eps, s));
-        r->launches++;
+        // x = rms_norm(x) * input_norm (ops.hpp:119), then q, k, v and RoPE
+        const float* xn;  // where the normalised x (the new residual stream) is
         const int lqkv = common_layout(L.q, L.k, &L.v);
         if (lqkv >= 0) {
+            Norm nm;
+            nm.on = true;
+            nm.w = L.in_norm;
+            nm.out = r->xn;
             TRY(fused(r, lqkv, tbh::kRope,
-                      {seg_of(L.q, r->q), seg_of(L.k, r->k), seg_of(L.v, r->v)}, r->x, H));
+                      {seg_of(L.q, r->q), seg_of(L.k, r->k), seg_of(L.v, r->v)}, r->x, H,
+                      nullptr, nullptr, nm));
+            xn = r->xn;
         } else {
+            TRY(tbh::runner_norm(H, r->x, L.in_norm, r->x, c.norm_eps, s));
+            r->launches++;
             TRY(project(r, L.q, r->x, nullptr, r->q));
             TRY(project(r, L.k, r->x, nullptr, r->k));
             TRY(project(r, L.v, r->x, nullptr, r->v));
             TRY(tb_b200_rope_rows(TB_DTYPE_F32, 1, c.n_heads, c.n_kv_heads, c.head_dim, r->q, r->k,
                                   r->dstate, c.rope_theta, r->rope, c.max_seq, s));
             r->launches++;
+            xn = r->x;
         }
         const size_t layer_off = (size_t)(&L - r->layers.data()) * (size_t)c.max_seq *
                                  (size_t)c.n_kv_heads * (size_t)c.head_dim;
@@ -297,21 +319,26 @@ int enqueue(Runner* r) {
                                          c.max_seq, r->dstate, r->q, r->k, r->v,
                                          r->kc + layer_off, r->vc + layer_off, r->attn, s, true));
         r->launches++;
-        if (L.o.w) {  // ops.hpp:207-218
+        if (L.o.w) {  // x = x_normalised + Wo attn (ops.hpp:207-218)
             const int lo = fused_layout(L.o);
             if (lo >= 0)
-                TRY(fused(r, lo, tbh::kResidual, {seg_of(L.o, r->x)}, r->attn, L.o.cols));
+                TRY(fused(r, lo, tbh::kResidual, {seg_of(L.o, r->x)}, r->attn, L.o.cols, xn));
             else
-                TRY(project(r, L.o, r->attn, r->x, r->x));
+                TRY(project(r, L.o, r->attn, xn, r->x));
+        } else if (xn != r->x) {
+            TB_CUDA_TRY(cudaMemcpyAsync(r->x, xn, (size_t)H * 4, cudaMemcpyDeviceToDevice, s));
         }
-        TRY(tbh::runner_norm(H, r->x, L.post_norm, r->xm, c.norm_eps, s));
-        r->launches++;
-        if (L.gate.w && L.up.w && c.intermediate > 0) {  // ops.hpp:226-256
+        if (L.gate.w && L.up.w && c.intermediate > 0) {  // ops.hpp:221-256
             const int lgu = common_layout(L.gate, L.up);
             if (lgu >= 0) {
-                TRY(fused(r, lgu, tbh::kSwiglu, {seg_of(L.gate, r->g), seg_of(L.up, r->u)}, r->xm,
-                          H, r->g));
+                Norm nm;
+                nm.on = true;
+                nm.w = L.post_norm;
+                TRY(fused(r, lgu, tbh::kSwiglu, {seg_of(L.gate, r->g), seg_of(L.up, r->u)}, r->x,
+                          H, nullptr, r->g, nm));
             } else {
+                TRY(tbh::runner_norm(H, r->x, L.post_norm, r->xm, c.norm_eps, s));
+                r->launches++;
                 TRY(project(r, L.gate, r->xm, nullptr, r->g));
                 TRY(project(r, L.up, r->xm, nullptr, r->u));
                 TRY(tb_b200_swiglu(TB_DTYPE_F32, c.intermediate, r->g, r->u, r->g, s));
@@ -320,22 +347,28 @@ int enqueue(Runner* r) {
             if (L.down.w) {
                 const int ld = fused_layout(L.down);
                 if (ld >= 0)
-                    TRY(fused(r, ld, tbh::kResidual, {seg_of(L.down, r->x)}, r->g, L.down.cols));
+                    TRY(fused(r, ld, tbh::kResidual, {seg_of(L.down, r->x)}, r->g, L.down.cols,
+                              r->x));
                 else
                     TRY(project(r, L.down, r->g, r->x, r->x));
             }
         }
     }
-    TRY(tbh::runner_norm(H, r->x, r->final_norm, r->x, c.norm_eps, s));
-    r->launches++;
+    // x = rms_norm(x) * final_norm; logits = Wlm x; position += 1 (ops.hpp:260-284)
     Proj lm;
     lm.w = r->lm_head;
     lm.rows = c.vocab;
     lm.cols = H;
     const int ll = fused_layout(lm);
-    if (ll >= 0) {  // the logits, then position += 1 (ops.hpp:269-284)
-        TRY(fused(r, ll, tbh::kPlain, {seg_of(lm, r->logits)}, r->x, H, nullptr, r->dstate));
+    if (ll >= 0) {
+        Norm nm;
+        nm.on = true;
+        nm.w = r->final_norm;
+        TRY(fused(r, ll, tbh::kPlain, {seg_of(lm, r->logits)}, r->x, H, nullptr, nullptr, nm,
+                  r->dstate));
     } else {
+        TRY(tbh::runner_norm(H, r->x, r->final_norm, r->x, c.norm_eps, s));
+        r->launches++;
         TRY(tb_b200_dense_linear(c.vocab, H, r->x, r->lm_head, nullptr, r->logits, s));
         r->launches++;
         k_advance<<<1, 1, 0, s>>>(r->dstate);
@@ -371,6 +404,7 @@ int create(const TbB200RunnerDesc* d, Runner* r) {
     TB_CUDA_TRY(cudaStreamCreateWithFlags(&r->stream, cudaStreamNonBlocking));
     int rc = tbh::decode_attention_setup(c.head_dim, c.max_seq);
     if (rc) return rc;
+    if ((rc = tbh::fused_gemv_setup(c.hidden))) return rc;
     const int64_t H = c.hidden, I = c.intermediate, V = c.vocab;
     const int64_t qd = (int64_t)c.n_heads * c.head_dim, kvd = (int64_t)c.n_kv_heads * c.head_dim;
     if (c.embed.rows != V || c.embed.cols != H) return TB_ERR_INVALID_SHAPE;
@@ -401,6 +435,8 @@ int create(const TbB200RunnerDesc* d, Runner* r) {
     const size_t f = sizeof(float);
     if ((rc = dev_alloc(r, (size_t)H * f, &p))) return rc;
     r->x = (float*)p;
+    if ((rc = dev_alloc(r, (size_t)H * f, &p))) return rc;
+    r->xn = (float*)p;
     if ((rc = dev_alloc(r, (size_t)qd * f, &p))) return rc;
     r->q = (float*)p;
     if ((rc = dev_alloc(r, (size_t)kvd * f, &p))) return rc;

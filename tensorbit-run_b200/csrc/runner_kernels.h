@@ -30,12 +30,19 @@ struct GemvArgs {
     int rope_segs;       // segments 0 .. rope_segs-1 are rotated
     int32_t* advance;    // non-null: *advance += 1 once the kernel has run
     unsigned* status;
+    int norm;            // nonzero: the GEMV reads rms_norm(x) * norm_w instead of x
+    const float* norm_w; // norm weight [cols] or NULL
+    float eps;
+    float* norm_out;     // non-null: CTA 0 also stores the normalised x there
 };
 
 // One fused GEMV launch over 1-3 segments sharing x (programmatic dependent
 // launch).  layout kDense needs cols % 4 == 0, kPacked cols % 8 == 0; x and
 // the weights 16-byte aligned.  kSwiglu takes two segments of equal rows.
+// With norm set, every CTA normalises x into shared memory first (cols * 4
+// bytes; fused_gemv_setup opts in to more than 48 KB).
 int fused_gemv(const GemvArgs& a, int layout, int epi, cudaStream_t s);
+int fused_gemv_setup(int64_t cols);
 // RMSNorm of one f32 vector, one CTA, programmatic dependent launch.
 int runner_norm(int64_t n, const float* x, const float* w, float* y, float eps, cudaStream_t s);
 // Opt the attention kernels in to the shared memory max_seq keys need.
