@@ -53,7 +53,13 @@ CONFIGS = {
     "decode": (W.CONFIGS["decode"], None, "decode 256 sequences x 1 token at the llama7b shape: the "
                                           "fused layer chain (residual+RMSNorm, RoPE, SwiGLU) over "
                                           "32 layers, one CUDA graph"),
+    "runner": (W.CONFIGS["7b"], None, "TransformerRunner decode of one sequence at the llama7b "
+                                      "shape (32 layers, f32 weights, 2:4-pruned projections), "
+                                      "one CUDA graph per token"),
 }
+RUNNER_LAYERS = 32
+RUNNER_MAX_SEQ = 2048
+RUNNER_METRIC = "decode tokens/s"
 DECODE_LAYERS = 32
 CFG, LOGIT_ROWS, WORKLOAD = CONFIGS["7b"]
 E2E_BLOCKS = 8    # row blocks of the end-to-end step
@@ -443,6 +449,211 @@ def run_decode(args, rank, world, local):
     }
 
 
+# ------------------------------------------------------------ runner config
+PATTERNS_2_4 = (0x3, 0x5, 0x6, 0x9, 0xA, 0xC)
+
+
+def runner_cfg(layers):
+    c = CFG
+    return dict(hidden=c.hidden, n_heads=c.n_q_heads, n_kv_heads=c.n_kv_heads,
+                head_dim=c.head_dim, intermediate=c.intermediate, vocab=c.vocab,
+                max_seq=RUNNER_MAX_SEQ, layers=layers, norm_eps=c.eps, rope_theta=c.theta)
+
+
+def runner_shapes(cfg):
+    H, I = cfg["hidden"], cfg["intermediate"]
+    qd, kvd = cfg["n_heads"] * cfg["head_dim"], cfg["n_kv_heads"] * cfg["head_dim"]
+    return dict(q=(qd, H), k=(kvd, H), v=(kvd, H), o=(H, qd), gate=(I, H), up=(I, H),
+                down=(H, I))
+
+
+def runner_token_bytes(cfg, pos):
+    """Algorithmic bytes of one token at position `pos` in the runner's
+    layout: packed 2:4 projections (kept f32 values + index bytes), the
+    dense f32 lm head, the embedding row, the norm weights, and the KV cache
+    (rows 0..pos-1 read for every layer, row pos written)."""
+    H, L = cfg["hidden"], cfg["layers"]
+    kvd = cfg["n_kv_heads"] * cfg["head_dim"]
+    proj = 0
+    for rows, cols in runner_shapes(cfg).values():
+        pairs = cols // 8
+        proj += rows * pairs * 16 + rows * ((pairs + 127) // 128 * 128)
+    return (L * proj + cfg["vocab"] * H * 4 + H * 4 + (2 * L + 1) * H * 4
+            + L * 2 * kvd * 4 * (pos + 1))
+
+
+def runner_model_torch(torch, dev, cfg, seed):
+    """Weights U(-0.01, 0.01) (the engine's mock initialisation), random 2:4
+    masks, norm weights 1 + N(0, 0.1); all f32 on the device."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    pats = torch.tensor(PATTERNS_2_4, dtype=torch.uint8, device=dev)
+
+    def w(r, c):
+        return (torch.rand((r, c), generator=g, device=dev) - 0.5) * 0.02
+
+    def nv():
+        return 1 + 0.1 * torch.randn(cfg["hidden"], generator=g, device=dev)
+
+    layers = []
+    for _ in range(cfg["layers"]):
+        ly = {n: (w(r, c), pats[torch.randint(0, len(PATTERNS_2_4), (r, c // 4), generator=g,
+                                              device=dev)].contiguous())
+              for n, (r, c) in runner_shapes(cfg).items()}
+        ly["in_norm"], ly["post_norm"] = nv(), nv()
+        layers.append(ly)
+    return dict(embed=w(cfg["vocab"], cfg["hidden"]), final_norm=nv(),
+                lm_head=w(cfg["vocab"], cfg["hidden"]), layers=layers)
+
+
+def cpu_sample_runner(seconds=10.0):
+    """The reference runner's arithmetic on the host (the oracle's
+    restatement, oracle/runner.c; the reference's own runner reads past its
+    norm weights at this shape, vocab > hidden): one token through models
+    of 0 and 2 layers of the llama7b shape, scaled to 32 layers."""
+    import numpy as np
+    from oracle import oracle as O
+    rng = np.random.default_rng(7)
+    pats = np.array(PATTERNS_2_4, np.uint8)
+
+    def model(layers):
+        cfg = runner_cfg(layers)
+        lys = []
+        for _ in range(layers):
+            ly = {n: (((rng.random((r, c), dtype=np.float32) - 0.5) * 0.02),
+                      pats[rng.integers(0, 6, (r, c // 4))])
+                  for n, (r, c) in runner_shapes(cfg).items()}
+            ly["in_norm"] = ly["post_norm"] = np.ones(cfg["hidden"], np.float32)
+            lys.append(ly)
+        emb = ((rng.random((cfg["vocab"], cfg["hidden"]), dtype=np.float32) - 0.5) * 0.02)
+        return cfg, dict(embed=emb, final_norm=None, lm_head=None, layers=lys)
+
+    def timed(cfg, m):
+        O.runner_run(cfg, m, np.array([1], np.int32))  # warm-up
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            O.runner_run(cfg, m, np.array([1], np.int32))
+            reps += 1
+            if time.perf_counter() - t0 >= seconds / 2 or reps >= 20:
+                break
+        return (time.perf_counter() - t0) / reps
+
+    t0 = timed(*model(0))
+    t2 = timed(*model(2))
+    per_token = t0 + RUNNER_LAYERS * max(t2 - t0, 0.0) / 2
+    return per_token, ("one token through 0- and 2-layer llama7b-shape models (oracle/runner.c, "
+                       "1 thread), scaled to 32 layers")
+
+
+def run_runner(args, rank, world, local):
+    """One step = one token of a single sequence through the device runner
+    (tb_b200_runner_forward, a CUDA graph), positions counting up from 0;
+    every rank runs its own replica (no exchange on this path)."""
+    import torch
+    import torch.distributed as dist
+    import tb_b200 as T
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = runner_cfg(RUNNER_LAYERS)
+    model = runner_model_torch(torch, dev, cfg, 777 + rank)
+    runner = T.Runner(cfg, model, attention=T.ATTN_STANDARD, use_graph=True)
+    stream = torch.cuda.ExternalStream(runner.stream.value)
+    tokens = torch.randint(0, cfg["vocab"], (args.warmup + 2 * args.steps + 8,),
+                           generator=torch.Generator().manual_seed(5)).tolist()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    it = iter(tokens)
+    for _ in range(args.warmup):
+        runner.forward(next(it))
+    torch.cuda.synchronize()
+    pos0 = runner.position
+    uuid = getattr(torch.cuda.get_device_properties(dev), "uuid", None)
+    uuid = f"GPU-{uuid}" if uuid is not None else None
+    barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local, uuid) as clocks:
+        a.record(stream)
+        for _ in range(args.steps):
+            runner.forward(next(it))
+        b.record(stream)
+        b.synchronize()
+    ms = max_over_ranks(a.elapsed_time(b)) / args.steps
+    launches = runner.launches_per_token * args.steps
+
+    # end to end: the token id in from the host, the logits out to it, every token
+    barrier()
+    torch.cuda.synchronize()
+    n2 = max(3, min(args.steps, 20))
+    a.record(stream)
+    for _ in range(n2):
+        runner.forward(next(it))
+        runner.logits()
+    b.record(stream)
+    b.synchronize()
+    e2e_ms = max_over_ranks(a.elapsed_time(b)) / n2
+    runner.close()
+
+    mean_pos = pos0 + (args.steps - 1) / 2
+    tb = runner_token_bytes(cfg, mean_pos)
+    peak, peak_kind = peaks()
+    achieved = tb / (ms / 1e3) / 1e9
+    tok_s = world * 1e3 / ms
+    return {
+        "metric": RUNNER_METRIC, "value": round(tok_s, 2), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; weights U(-0.01, 0.01) as the engine's mock model, "
+                "random 2:4 masks, norm weights 1 + N(0, 0.1))",
+        "config": {"workload": WORKLOAD, "layers": RUNNER_LAYERS, "hidden": cfg["hidden"],
+                   "heads": [cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"]],
+                   "intermediate": cfg["intermediate"], "vocab": cfg["vocab"],
+                   "max_seq": RUNNER_MAX_SEQ, "attention": "standard (every key of the row)",
+                   "positions": f"{pos0} .. {pos0 + args.steps - 1}",
+                   "bytes_per_token_per_gpu": tb,
+                   "l2": f"inputs larger than L2: {tb / 1e9:.1f} GB of weights per token",
+                   "parallelism": f"replicas x{world}, no data-path collective"},
+        "roofline": {"bound": "hbm", "kernel": "decoder step (every kernel of a token)",
+                     "achieved": round(achieved, 1), "peak": peak, "peak_source": peak_kind,
+                     "unit": "GB/s", "frac": round(achieved / peak, 3), "traffic": None,
+                     "algorithmic_bytes": tb,
+                     "traffic_source": "no ncu capture of the whole step",
+                     "duration": "graph replay time per token"},
+        "e2e": {"value": round(world * 1e3 / e2e_ms, 2), "unit": "tokens/s",
+                "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": cfg["vocab"] * 4,
+                "api": "tb_b200_runner_forward + tb_b200_runner_logits (token id in, logits "
+                       "out, synchronous per token)"},
+        "gpu_launches": int(launches),
+        "clocks": clocks.summary(),
+    }
+
+
+def run_reference_runner(args, world):
+    per_token, sample = cpu_sample_runner()
+    v = round(1.0 / per_token, 4)
+    return {"metric": RUNNER_METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
+            "steps": 1, "warmup": 1, "ms_per_step": round(per_token * 1e3, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded)", "impl": "reference",
+            "config": {"workload": WORKLOAD, "layers": RUNNER_LAYERS},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": 1, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
 # ------------------------------------------------------------------ GPU arm
 def build_inputs(torch, dev, seed, rows=None):
     c = CFG
@@ -685,7 +896,8 @@ def main():
     ap.add_argument("--config", choices=sorted(CONFIGS), default="7b",
                     help="7b (default): the Llama-7B prefill step; 70b: the Llama-70B prefill's "
                          "layer ops and the sweep's 4096 x 128256 softmax/argmax; decode: the "
-                         "32-layer chain over a 256-sequence decode batch")
+                         "32-layer chain over a 256-sequence decode batch; runner: single-"
+                         "sequence decode through the device TransformerRunner")
     ap.add_argument("--rows", type=int, default=None, help="layer-op rows per GPU (config's)")
     args = ap.parse_args()
     global CFG, LOGIT_ROWS, WORKLOAD
@@ -699,7 +911,8 @@ def main():
 
     if args.impl == "reference":
         if rank == 0:
-            print(json.dumps(run_reference(args, world)))
+            print(json.dumps(run_reference_runner(args, world) if args.config == "runner"
+                             else run_reference(args, world)))
         return
 
     import torch
@@ -710,11 +923,18 @@ def main():
                                 device_id=torch.device("cuda", local))
     try:
         decode = args.config == "decode"
-        line = (run_decode if decode else run_gpu)(args, rank, world, local)
+        run = {"decode": run_decode, "runner": run_runner}.get(args.config, run_gpu)
+        line = run(args, rank, world, local)
         if line is None:
             return
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(sample=cpu_sample_decode if decode else cpu_sample)
+            if args.config == "runner":
+                per_token, sample = cpu_sample_runner()
+                line["cpu_baseline"] = {"value": round(1.0 / per_token, 4), "unit": "tokens/s",
+                                        "cores": 1, "kind": "port", "sample": sample}
+            else:
+                line["cpu_baseline"] = cpu_baseline(
+                    sample=cpu_sample_decode if decode else cpu_sample)
         if rank == 0:
             print(json.dumps(line))
     finally:

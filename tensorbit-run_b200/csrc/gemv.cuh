@@ -5,8 +5,10 @@
 // (through L1) serves both.  Lanes stride over the row in steps of 128
 // float4s (dense) or 128 group pairs (packed), four per lane per row in
 // flight, with no bounds checks inside a full step; the last partial step
-// goes element by element.  The result is each lane's partial sum; the
-// caller adds the lanes (warp_sum2).
+// goes element by element.  A call may cover a range of steps [s0, s1) so
+// several warps can split a row (the range holding the partial step takes
+// it).  The result is each lane's partial sum; the caller adds the lanes
+// (warp_sum2).
 //
 // Packed form, per row: P = (in/4)/2 pairs of 4-column groups; vals holds a
 // float4 per pair (group 2p's two kept weights, then group 2p+1's) and idx a
@@ -58,15 +60,19 @@ __device__ __forceinline__ void packed_dot2(const float4* __restrict__ v0,
                                             const uint8_t* __restrict__ i0,
                                             const float4* __restrict__ v1,
                                             const uint8_t* __restrict__ i1, int64_t pairs,
-                                            const float4* x4, int lane, float& a0,
-                                            float& a1) {
+                                            const float4* x4, int lane, float& a0, float& a1,
+                                            int64_t s0 = 0, int64_t s1 = -1) {
+    // steps [s0, s1) of the row (all of it by default); the partial last
+    // step belongs to whoever owns step pairs / 128
     const int64_t full = pairs / kGemvStep;
-    const float4* p0 = v0 + lane;
-    const float4* p1 = v1 + lane;
-    const uint32_t* q0 = reinterpret_cast<const uint32_t*>(i0) + lane;
-    const uint32_t* q1 = reinterpret_cast<const uint32_t*>(i1) + lane;
-    const float4* xp = x4 + 2 * lane;
-    for (int64_t s = 0; s < full; ++s) {
+    if (s1 < 0) s1 = full + 1;
+    const int64_t send = s1 < full ? s1 : full;
+    const float4* p0 = v0 + s0 * kGemvStep + lane;
+    const float4* p1 = v1 + s0 * kGemvStep + lane;
+    const uint32_t* q0 = reinterpret_cast<const uint32_t*>(i0 + s0 * kGemvStep) + lane;
+    const uint32_t* q1 = reinterpret_cast<const uint32_t*>(i1 + s0 * kGemvStep) + lane;
+    const float4* xp = x4 + 2 * (s0 * kGemvStep + lane);
+    for (int64_t s = s0; s < send; ++s) {
         float4 w0[4], w1[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -86,6 +92,7 @@ __device__ __forceinline__ void packed_dot2(const float4* __restrict__ v0,
         }
         xp += 2 * kGemvStep;
     }
+    if (s1 <= full) return;
     for (int u = 0; u < 4; ++u) {  // the partial step
         const int64_t p = full * kGemvStep + 32 * u + lane;
         if (p >= pairs) break;
@@ -100,13 +107,15 @@ __device__ __forceinline__ void packed_dot2(const float4* __restrict__ v0,
 template <bool XS = false>
 __device__ __forceinline__ void dense_dot2(const float4* __restrict__ w0,
                                            const float4* __restrict__ w1, int64_t n4,
-                                           const float4* x4, int lane, float& a0,
-                                           float& a1) {
+                                           const float4* x4, int lane, float& a0, float& a1,
+                                           int64_t s0 = 0, int64_t s1 = -1) {
     const int64_t full = n4 / kGemvStep;
-    const float4* p0 = w0 + lane;
-    const float4* p1 = w1 + lane;
-    const float4* xp = x4 + lane;
-    for (int64_t s = 0; s < full; ++s) {
+    if (s1 < 0) s1 = full + 1;
+    const int64_t send = s1 < full ? s1 : full;
+    const float4* p0 = w0 + s0 * kGemvStep + lane;
+    const float4* p1 = w1 + s0 * kGemvStep + lane;
+    const float4* xp = x4 + s0 * kGemvStep + lane;
+    for (int64_t s = s0; s < send; ++s) {
         float4 r0[4], r1[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -129,6 +138,7 @@ __device__ __forceinline__ void dense_dot2(const float4* __restrict__ w0,
         }
         xp += kGemvStep;
     }
+    if (s1 <= full) return;
     for (int u = 0; u < 4; ++u) {
         const int64_t v = full * kGemvStep + 32 * u + lane;
         if (v >= n4) break;

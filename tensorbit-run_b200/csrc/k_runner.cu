@@ -85,14 +85,20 @@ __device__ __forceinline__ void row_ptrs(const tbh::GemvSeg& g, int64_t cols, in
 // below the L2 (whole rows of a 200 MB projection group would evict each
 // other).  Sizes are multiples of 16 bytes; rows start 16-byte aligned.
 template <int LAYOUT>
-__device__ __forceinline__ void prefetch_row(int64_t cols, const float4* v, const uint8_t* ib) {
+__device__ __forceinline__ void prefetch_row(int64_t cols, const float4* v, const uint8_t* ib,
+                                             int64_t step) {
     constexpr int64_t kCap = 2048;
+    const int64_t off = step * tbk::kGemvStep;  // float4s (dense) or pairs (packed)
     if (LAYOUT == tbh::kDense) {
-        tbk::prefetch_l2(v, (uint32_t)min(cols * 4, kCap));
+        const int64_t left = (cols / 4 - off) * 16;
+        if (left > 0) tbk::prefetch_l2(v + off, (uint32_t)min(left, kCap));
     } else {
         const int64_t pairs = cols / 8;
-        tbk::prefetch_l2(v, (uint32_t)min(pairs * 16, kCap));
-        tbk::prefetch_l2(ib, (uint32_t)min(tbk::packed_idx_stride(pairs), kCap));
+        const int64_t left = (pairs - off) * 16;
+        if (left > 0) {
+            tbk::prefetch_l2(v + off, (uint32_t)min(left, kCap));
+            tbk::prefetch_l2(ib + off, (uint32_t)min(tbk::packed_idx_stride(pairs) - off, kCap));
+        }
     }
 }
 
@@ -100,21 +106,24 @@ template <int LAYOUT, int EPI, bool NORM>
 __global__ void __launch_bounds__(kThreads) k_fgemv(const __grid_constant__ GemvArgs a) {
     extern __shared__ float4 xs[];  // NORM: the normalised x
     __shared__ float red[kWarps];
-    const int lane = threadIdx.x & 31;
-    const int64_t warps = (int64_t)gridDim.x * kWarps;
-    const int64_t first = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+    __shared__ float2 psum[kWarps];  // split rows: each warp's partial sums
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    // a.ks warps share a unit, each over a contiguous range of its steps
+    const int ks = a.ks, upc = kWarps / ks, slot = wid / ks, part = wid % ks;
+    const int64_t per_row = (LAYOUT == tbh::kDense ? a.cols / 4 : a.cols / 8) / tbk::kGemvStep + 1;
+    const int64_t s0 = part * per_row / ks, s1 = (part + 1) * per_row / ks;
     {  // weights do not depend on the previous kernel: start their stream
         int s;
         int64_t r0, r1;
-        if (lane == 0 && unit_rows<EPI>(a, first, s, r0, r1)) {
+        if (lane == 0 && unit_rows<EPI>(a, (int64_t)blockIdx.x * upc + slot, s, r0, r1)) {
             const float4* v;
             const uint8_t* ib;
             const tbh::GemvSeg& g0 = a.seg[s];
             row_ptrs<LAYOUT>(g0, a.cols, r0, v, ib);
-            prefetch_row<LAYOUT>(a.cols, v, ib);
+            prefetch_row<LAYOUT>(a.cols, v, ib, s0);
             const tbh::GemvSeg& g1 = EPI == tbh::kSwiglu ? a.seg[1] : a.seg[s];
             row_ptrs<LAYOUT>(g1, a.cols, r1, v, ib);
-            prefetch_row<LAYOUT>(a.cols, v, ib);
+            prefetch_row<LAYOUT>(a.cols, v, ib, s0);
         }
     }
     pdl_wait();
@@ -157,24 +166,41 @@ __global__ void __launch_bounds__(kThreads) k_fgemv(const __grid_constant__ Gemv
     }
     int pos = 0;
     if (EPI == tbh::kRope) pos = *a.pos;
-    for (int64_t u = first;; u += warps) {
-        int s;
-        int64_t r0, r1;
-        if (!unit_rows<EPI>(a, u, s, r0, r1)) break;
-        const tbh::GemvSeg& g0 = a.seg[s];
-        const tbh::GemvSeg& g1 = EPI == tbh::kSwiglu ? a.seg[1] : a.seg[s];
-        const float4 *v0, *v1;
-        const uint8_t *i0, *i1;
-        row_ptrs<LAYOUT>(g0, a.cols, r0, v0, i0);
-        row_ptrs<LAYOUT>(g1, a.cols, r1, v1, i1);
+    const float4* xsrc = NORM ? xs : x4;
+    // the loop bound is the same for every warp of the CTA (it synchronises)
+    for (int64_t base = (int64_t)blockIdx.x * upc; base < a.units; base += (int64_t)gridDim.x * upc) {
+        int s = 0;
+        int64_t r0 = 0, r1 = 0;
+        const bool have = unit_rows<EPI>(a, base + slot, s, r0, r1);
         float a0 = 0.0f, a1 = 0.0f;
-        const float4* xsrc = NORM ? xs : x4;
-        if (LAYOUT == tbh::kDense)
-            tbk::dense_dot2<NORM>(v0, v1, n4, xsrc, lane, a0, a1);
-        else
-            tbk::packed_dot2<NORM>(v0, i0, v1, i1, a.cols / 8, xsrc, lane, a0, a1);
+        if (have) {
+            const tbh::GemvSeg& g0 = a.seg[s];
+            const tbh::GemvSeg& g1 = EPI == tbh::kSwiglu ? a.seg[1] : a.seg[s];
+            const float4 *v0, *v1;
+            const uint8_t *i0, *i1;
+            row_ptrs<LAYOUT>(g0, a.cols, r0, v0, i0);
+            row_ptrs<LAYOUT>(g1, a.cols, r1, v1, i1);
+            if (LAYOUT == tbh::kDense)
+                tbk::dense_dot2<NORM>(v0, v1, n4, xsrc, lane, a0, a1, s0, s1);
+            else
+                tbk::packed_dot2<NORM>(v0, i0, v1, i1, a.cols / 8, xsrc, lane, a0, a1, s0, s1);
+        }
         tbk::warp_sum2(a0, a1);
-        if (lane != 0) continue;
+        if (ks > 1) {  // the unit's parts, added in part order
+            if (lane == 0) psum[wid] = make_float2(a0, a1);
+            __syncthreads();
+            if (part == 0) {
+                a0 = psum[wid].x;
+                a1 = psum[wid].y;
+                for (int k = 1; k < ks; ++k) {
+                    a0 = __fadd_rn(a0, psum[wid + k].x);
+                    a1 = __fadd_rn(a1, psum[wid + k].y);
+                }
+            }
+            __syncthreads();
+        }
+        if (!have || part != 0 || lane != 0) continue;
+        const tbh::GemvSeg& g0 = a.seg[s];
         if (EPI == tbh::kSwiglu) {
             a.act[r0] = __fmul_rn(tbk::silu_f(a0), a1);
         } else if (EPI == tbh::kResidual) {
@@ -266,6 +292,7 @@ int fused_gemv(const GemvArgs& a, int layout, int epi, cudaStream_t s) {
     const DeviceState* ds = current_device_state();
     if (!ds) return TB_ERR_DEVICE;
     if (a.nseg < 1 || a.nseg > 3 || (epi == kSwiglu && a.nseg != 2)) return TB_ERR_INVALID_ARG;
+    GemvArgs b = a;
     int64_t units = 0;
     if (epi == kSwiglu) {
         if (a.seg[0].rows != a.seg[1].rows) return TB_ERR_INVALID_SHAPE;
@@ -274,9 +301,17 @@ int fused_gemv(const GemvArgs& a, int layout, int epi, cudaStream_t s) {
         for (int i = 0; i < a.nseg; ++i) units += (a.seg[i].rows + 1) / 2;
     }
     if (units == 0) return TB_OK;
-    const int grid = ew_grid(units, kWarps, ds, 8);
-    return layout == kDense ? fgemv_layout<kDense>(a, epi, grid, s)
-                            : fgemv_layout<kPacked>(a, epi, grid, s);
+    // split rows over more warps when there are few of them (two resident
+    // CTAs of 8 warps per SM), at most one part per step of a row
+    const int64_t steps = (layout == kDense ? a.cols / 4 : a.cols / 8) / tbk::kGemvStep + 1;
+    int ks = 1;
+    while (ks < kWarps && units * ks < (int64_t)ds->sm_count * 2 * kWarps && 2 * ks <= steps) ks *= 2;
+    b.units = units;
+    b.ks = ks;
+    const int upc = kWarps / ks;
+    const int grid = ew_grid(units, upc, ds, 8);
+    return layout == kDense ? fgemv_layout<kDense>(b, epi, grid, s)
+                            : fgemv_layout<kPacked>(b, epi, grid, s);
 }
 
 int runner_norm(int64_t n, const float* x, const float* w, float* y, float eps, cudaStream_t s) {

@@ -34,6 +34,8 @@ struct GemvArgs {
     const float* norm_w; // norm weight [cols] or NULL
     float eps;
     float* norm_out;     // non-null: CTA 0 also stores the normalised x there
+    int64_t units;       // set by fused_gemv: row pairs (or gate/up rows)
+    int ks;              // set by fused_gemv: warps sharing one unit
 };
 
 // One fused GEMV launch over 1-3 segments sharing x (programmatic dependent

@@ -189,3 +189,16 @@ def test_decode_attention_kernel(dev, mode, heads, kv, d, pos):
     # the token's k and v were appended at row pos
     assert np.array_equal(g["kc"][pos].cpu().numpy(), k)
     assert np.array_equal(g["vc"][pos].cpu().numpy(), v)
+
+
+@pytest.mark.parametrize("inter,masks", [(16384, "rand"), (8192, "none"), (8192, "rand")])
+def test_rows_split_over_warps(dev, inter, masks):
+    """Few output rows with long rows (a down projection of 128 rows over
+    8192 or 16384 inputs): the fused GEMV splits each row pair over 4 or 8
+    warps and adds their parts in a fixed order."""
+    cfg, model = mock(seed=43, hidden=128, heads=4, kv=4, inter=inter, layers=1, vocab=100,
+                      max_seq=16, masks=masks, norms="rand")
+    toks = tokens(12, cfg["vocab"])
+    a = run_device(cfg, model, toks)
+    assert_logits(a, O.runner_run(cfg, model, toks))
+    assert np.array_equal(a, run_device(cfg, model, toks, use_graph=False))
