@@ -59,6 +59,7 @@ CONFIGS = {
 }
 RUNNER_LAYERS = 32
 RUNNER_MAX_SEQ = 2048
+RUNNER_CONTEXT = 1024  # tokens fed (untimed) before the timed ones: decode at context 1024+
 RUNNER_METRIC = "decode tokens/s"
 DECODE_LAYERS = 32
 CFG, LOGIT_ROWS, WORKLOAD = CONFIGS["7b"]
@@ -510,7 +511,9 @@ def cpu_sample_runner(seconds=10.0):
     """The reference runner's arithmetic on the host (the oracle's
     restatement, oracle/runner.c; the reference's own runner reads past its
     norm weights at this shape, vocab > hidden): one token through models
-    of 0 and 2 layers of the llama7b shape, scaled to 32 layers."""
+    of 0 and 2 layers of the llama7b shape, scaled to 32 layers.  The
+    sample token is at position 0: the host's attention over a 1024-token
+    context is left out, so the baseline is, if anything, fast."""
     import numpy as np
     from oracle import oracle as O
     rng = np.random.default_rng(7)
@@ -547,8 +550,9 @@ def cpu_sample_runner(seconds=10.0):
 
 def run_runner(args, rank, world, local):
     """One step = one token of a single sequence through the device runner
-    (tb_b200_runner_forward, a CUDA graph), positions counting up from 0;
-    every rank runs its own replica (no exchange on this path)."""
+    (tb_b200_runner_forward, a CUDA graph) after a context of RUNNER_CONTEXT
+    tokens, so every timed token attends over 1024+ cached positions; every
+    rank runs its own replica (no exchange on this path)."""
     import torch
     import torch.distributed as dist
     import tb_b200 as T
@@ -559,7 +563,10 @@ def run_runner(args, rank, world, local):
     model = runner_model_torch(torch, dev, cfg, 777 + rank)
     runner = T.Runner(cfg, model, attention=T.ATTN_STANDARD, use_graph=True)
     stream = torch.cuda.ExternalStream(runner.stream.value)
-    tokens = torch.randint(0, cfg["vocab"], (args.warmup + 2 * args.steps + 8,),
+    n_tok = RUNNER_CONTEXT + args.warmup + args.steps + max(3, min(args.steps, 20)) + 8
+    if n_tok > RUNNER_MAX_SEQ:
+        raise SystemExit(f"--config runner: {n_tok} positions exceed max_seq {RUNNER_MAX_SEQ}")
+    tokens = torch.randint(0, cfg["vocab"], (n_tok,),
                            generator=torch.Generator().manual_seed(5)).tolist()
 
     def barrier():
@@ -574,7 +581,7 @@ def run_runner(args, rank, world, local):
         return float(t.item())
 
     it = iter(tokens)
-    for _ in range(args.warmup):
+    for _ in range(RUNNER_CONTEXT + args.warmup):  # the context, then the warm-up tokens
         runner.forward(next(it))
     torch.cuda.synchronize()
     pos0 = runner.position
@@ -620,6 +627,7 @@ def run_runner(args, rank, world, local):
                    "heads": [cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"]],
                    "intermediate": cfg["intermediate"], "vocab": cfg["vocab"],
                    "max_seq": RUNNER_MAX_SEQ, "attention": "standard (every key of the row)",
+                   "context": f"{RUNNER_CONTEXT} tokens fed untimed before the warm-up",
                    "positions": f"{pos0} .. {pos0 + args.steps - 1}",
                    "bytes_per_token_per_gpu": tb,
                    "l2": f"inputs larger than L2: {tb / 1e9:.1f} GB of weights per token",

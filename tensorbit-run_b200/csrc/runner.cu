@@ -62,6 +62,9 @@ struct Runner {
     float *xm = nullptr, *g = nullptr, *u = nullptr, *logits = nullptr;
     float *kc = nullptr, *vc = nullptr, *rope = nullptr;
     int32_t* dstate = nullptr;  // [0] position, [1] token
+    int att_splits = 1;         // CTAs per attention row when rows are long
+    float* att_part = nullptr;  // their partial results
+    int* att_count = nullptr;   // their per-row arrival counters
     int* flag = nullptr;        // packing verdict of one layer
     int pos = 0;
     int launches = 0;
@@ -317,7 +320,8 @@ int enqueue(Runner* r) {
                                  (size_t)c.n_kv_heads * (size_t)c.head_dim;
         TRY(tbh::decode_attention_launch(c.attention, c.n_heads, c.n_kv_heads, c.head_dim,
                                          c.max_seq, r->dstate, r->q, r->k, r->v,
-                                         r->kc + layer_off, r->vc + layer_off, r->attn, s, true));
+                                         r->kc + layer_off, r->vc + layer_off, r->attn, s, true,
+                                         r->att_splits, r->att_part, r->att_count));
         r->launches++;
         if (L.o.w) {  // x = x_normalised + Wo attn (ops.hpp:207-218)
             const int lo = fused_layout(L.o);
@@ -464,6 +468,17 @@ int create(const TbB200RunnerDesc* d, Runner* r) {
         return rc;
     if ((rc = dev_alloc(r, 2 * sizeof(int32_t), &p))) return rc;
     r->dstate = (int32_t*)p;
+    r->att_splits = c.attention == TB_B200_ATTN_STANDARD
+                        ? tbh::decode_attention_splits(c.n_heads, c.max_seq)
+                        : 1;  // the reference's rows attend at most n_heads keys
+    if (r->att_splits > 1) {
+        if ((rc = dev_alloc(r, (size_t)c.n_heads * r->att_splits * (c.head_dim + 2) * f, &p)))
+            return rc;
+        r->att_part = (float*)p;
+        if ((rc = dev_alloc(r, (size_t)c.n_heads * sizeof(int), &p))) return rc;
+        r->att_count = (int*)p;
+        TB_CUDA_TRY(cudaMemsetAsync(r->att_count, 0, (size_t)c.n_heads * sizeof(int), r->stream));
+    }
     TB_CUDA_TRY(cudaMemsetAsync(r->dstate, 0, 2 * sizeof(int32_t), r->stream));
     TB_CUDA_TRY(cudaMemsetAsync(r->x, 0, (size_t)H * f, r->stream));
     TB_CUDA_TRY(cudaStreamSynchronize(r->stream));

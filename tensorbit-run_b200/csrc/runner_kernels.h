@@ -49,9 +49,14 @@ int fused_gemv_setup(int64_t cols);
 int runner_norm(int64_t n, const float* x, const float* w, float* y, float eps, cudaStream_t s);
 // Opt the attention kernels in to the shared memory max_seq keys need.
 int decode_attention_setup(int head_dim, int max_seq);
+// splits > 1: rows of more than 512 keys are split over that many CTAs,
+// which leave (max, sum, weighted v) in part (n_heads * splits * (head_dim
+// + 2) floats) and count themselves in counters (n_heads ints, zero before
+// the first launch; the last CTA of a row resets its counter).
 int decode_attention_launch(int mode, int n_heads, int n_kv_heads, int head_dim, int max_seq,
                             const int32_t* position, const float* q, const float* k,
                             const float* v, float* k_cache, float* v_cache, float* out,
-                            cudaStream_t s, bool pdl);
+                            cudaStream_t s, bool pdl, int splits, float* part, int* counters);
+int decode_attention_splits(int n_rows, int max_seq);
 
 }  // namespace tbh

@@ -202,3 +202,18 @@ def test_rows_split_over_warps(dev, inter, masks):
     a = run_device(cfg, model, toks)
     assert_logits(a, O.runner_run(cfg, model, toks))
     assert np.array_equal(a, run_device(cfg, model, toks, use_graph=False))
+
+
+def test_long_rows_split_over_ctas(dev):
+    """Standard attention past 512 keys: each head's row is split over
+    several CTAs whose partial max, sum and weighted values the last one
+    combines (in a fixed order: graph and eager replays agree bit for
+    bit)."""
+    cfg, model = mock(seed=47, layers=2, max_seq=1024, masks="rand", norms="rand")
+    cfg["attention"] = T.ATTN_STANDARD
+    toks = tokens(700, cfg["vocab"], seed=9)
+    want = O.runner_run(cfg, model, toks)
+    a = run_device(cfg, model, toks, attention=T.ATTN_STANDARD)
+    assert_logits(a, want)
+    b = run_device(cfg, model, toks[:600], attention=T.ATTN_STANDARD, use_graph=False)
+    assert np.array_equal(a[:600], b)
