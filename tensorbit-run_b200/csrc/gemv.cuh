@@ -154,6 +154,106 @@ __device__ __forceinline__ void dense_dot2(const float4* __restrict__ w0,
     }
 }
 
+// ------------------------------------------------------------- INT8 / INT4
+// Quantized rows in the .tbm layout (Model::get_weight_fp32,
+// include/tensorbit/run/model.hpp:181-225): element i of the tensor is byte
+// i (INT8) or the low (even i) / high (odd i) nibble of byte i / 2 (INT4),
+// two's complement, with an f32 scale per group of gs consecutive elements
+// (1.0 past the last scale).  The weight is (float)q * scale -- here too, so
+// each product is the reference's; only the summation order differs.
+//
+// Lanes take consecutive 32-bit words (4 INT8 or 8 INT4 weights), so their
+// float4s of x are contiguous across the warp; eight words per lane and row
+// in flight.  q becomes a float without a conversion instruction: with its
+// sign bit flipped it is an unsigned value u = q + 128 (or + 8), placed in
+// the low mantissa bits of 2^23; subtracting 2^23 + 128 (or + 8) leaves q.
+constexpr int kQU = 8;                  // words per lane per step
+constexpr int kQStep = 32 * kQU;        // words per warp step
+
+template <int BITS>
+__device__ __forceinline__ float qval(uint32_t wx, int k) {  // wx: word with sign bits flipped
+    if constexpr (BITS == 8)
+        return __fsub_rn(__uint_as_float(__byte_perm(wx, 0x4B000000u, 0x7540u | (uint32_t)k)),
+                         8388736.0f);
+    else
+        return __fsub_rn(__uint_as_float(0x4B000000u | ((wx >> (4 * k)) & 0xFu)), 8388616.0f);
+}
+
+template <int BITS>
+__device__ __forceinline__ float qscale(const float* sc, int64_t nsc, int gshift, int64_t f) {
+    const int64_t g = gshift < 0 ? 0 : f >> gshift;
+    return g < nsc ? __ldg(sc + g) : 1.0f;
+}
+
+// One word of a row against x: acc += x[e] * ((float)q[e] * scale).
+template <int BITS, bool XS>
+__device__ __forceinline__ float qword_dot(uint32_t w, float scale, const float4* x4, int64_t word,
+                                           float acc) {
+    const uint32_t wx = w ^ (BITS == 8 ? 0x80808080u : 0x88888888u);
+    constexpr int kPer = 32 / BITS;
+#pragma unroll
+    for (int h = 0; h < kPer / 4; ++h) {
+        const float4 xv = ldx<XS>(x4 + word * (kPer / 4) + h);
+        acc = __fmaf_rn(xv.x, __fmul_rn(qval<BITS>(wx, 4 * h + 0), scale), acc);
+        acc = __fmaf_rn(xv.y, __fmul_rn(qval<BITS>(wx, 4 * h + 1), scale), acc);
+        acc = __fmaf_rn(xv.z, __fmul_rn(qval<BITS>(wx, 4 * h + 2), scale), acc);
+        acc = __fmaf_rn(xv.w, __fmul_rn(qval<BITS>(wx, 4 * h + 3), scale), acc);
+    }
+    return acc;
+}
+
+// A quantized row's scales: the tensor's scale array, its length, log2 of
+// its group size (-1: one group), and the flat index of the row's first
+// element in the tensor.
+struct QRow {
+    const float* sc;
+    int64_t nsc;
+    int gshift;
+    int64_t f;
+};
+
+// Partial sums of two quantized rows (which may belong to different
+// tensors).  d0/d1: the rows' first words; words: words per row; steps
+// [s0, s1) of kQStep words (all by default; the partial last step goes to
+// whoever owns step words / kQStep).
+template <int BITS, bool XS = false>
+__device__ __forceinline__ void quant_dot2(const uint32_t* __restrict__ d0,
+                                           const uint32_t* __restrict__ d1, const QRow q0,
+                                           const QRow q1, int64_t words, const float4* x4,
+                                           int lane, float& a0, float& a1, int64_t s0 = 0,
+                                           int64_t s1 = -1) {
+    constexpr int kPer = 32 / BITS;
+    const int64_t full = words / kQStep;
+    if (s1 < 0) s1 = full + 1;
+    const int64_t send = s1 < full ? s1 : full;
+    for (int64_t s = s0; s < send; ++s) {
+        const int64_t w0 = s * kQStep + lane;
+        uint32_t r0[kQU], r1[kQU];
+#pragma unroll
+        for (int u = 0; u < kQU; ++u) {
+            r0[u] = __ldcs(d0 + w0 + 32 * u);
+            r1[u] = __ldcs(d1 + w0 + 32 * u);
+        }
+#pragma unroll
+        for (int u = 0; u < kQU; ++u) {
+            const int64_t w = w0 + 32 * u;
+            a0 = qword_dot<BITS, XS>(r0[u], qscale<BITS>(q0.sc, q0.nsc, q0.gshift, q0.f + w * kPer),
+                                     x4, w, a0);
+            a1 = qword_dot<BITS, XS>(r1[u], qscale<BITS>(q1.sc, q1.nsc, q1.gshift, q1.f + w * kPer),
+                                     x4, w, a1);
+        }
+    }
+    if (s1 <= full) return;
+    for (int u = 0; u < kQU; ++u) {  // the partial step
+        const int64_t w = full * kQStep + 32 * u + lane;
+        if (w >= words) break;
+        a0 = qword_dot<BITS, XS>(__ldcs(d0 + w),
+                                 qscale<BITS>(q0.sc, q0.nsc, q0.gshift, q0.f + w * kPer), x4, w, a0);
+        a1 = qword_dot<BITS, XS>(__ldcs(d1 + w),
+                                 qscale<BITS>(q1.sc, q1.nsc, q1.gshift, q1.f + w * kPer), x4, w, a1);
+    }
+}
+
 __device__ __forceinline__ void warp_sum2(float& a0, float& a1) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {

@@ -67,11 +67,21 @@ __device__ __forceinline__ bool unit_rows(const GemvArgs& a, int64_t u, int& s, 
     }
 }
 
+// Weight words per row of a quantized layout.
+template <int LAYOUT>
+__host__ __device__ constexpr int64_t qwords(int64_t cols) {
+    return LAYOUT == tbh::kInt8 ? cols / 4 : cols / 8;
+}
+
 template <int LAYOUT>
 __device__ __forceinline__ void row_ptrs(const tbh::GemvSeg& g, int64_t cols, int64_t r,
                                          const float4*& v, const uint8_t*& ib) {
     if (LAYOUT == tbh::kDense) {
         v = static_cast<const float4*>(g.w) + r * (cols / 4);
+        ib = nullptr;
+    } else if (LAYOUT == tbh::kInt8 || LAYOUT == tbh::kInt4) {  // v: the row's first word
+        v = reinterpret_cast<const float4*>(static_cast<const uint32_t*>(g.w) +
+                                            r * qwords<LAYOUT>(cols));
         ib = nullptr;
     } else {
         const int64_t pairs = cols / 8;
@@ -88,6 +98,13 @@ template <int LAYOUT>
 __device__ __forceinline__ void prefetch_row(int64_t cols, const float4* v, const uint8_t* ib,
                                              int64_t step) {
     constexpr int64_t kCap = 2048;
+    if (LAYOUT == tbh::kInt8 || LAYOUT == tbh::kInt4) {
+        const int64_t woff = step * tbk::kQStep;
+        const int64_t left = (qwords<LAYOUT>(cols) - woff) * 4;
+        if (left > 0)
+            tbk::prefetch_l2(reinterpret_cast<const uint32_t*>(v) + woff, (uint32_t)min(left, kCap));
+        return;
+    }
     const int64_t off = step * tbk::kGemvStep;  // float4s (dense) or pairs (packed)
     if (LAYOUT == tbh::kDense) {
         const int64_t left = (cols / 4 - off) * 16;
@@ -112,7 +129,9 @@ __global__ void __launch_bounds__(kThreads, 4) k_fgemv(const __grid_constant__ G
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     // a.ks warps share a unit, each over a contiguous range of its steps
     const int ks = a.ks, upc = kWarps / ks, slot = wid / ks, part = wid % ks;
-    const int64_t per_row = (LAYOUT == tbh::kDense ? a.cols / 4 : a.cols / 8) / tbk::kGemvStep + 1;
+    const int64_t per_row = (LAYOUT == tbh::kInt8 || LAYOUT == tbh::kInt4)
+                                ? qwords<LAYOUT>(a.cols) / tbk::kQStep + 1
+                                : (LAYOUT == tbh::kDense ? a.cols / 4 : a.cols / 8) / tbk::kGemvStep + 1;
     const int64_t s0 = part * per_row / ks, s1 = (part + 1) * per_row / ks;
     {  // weights do not depend on the previous kernel: start their stream
         int s;
@@ -184,8 +203,14 @@ __global__ void __launch_bounds__(kThreads, 4) k_fgemv(const __grid_constant__ G
             row_ptrs<LAYOUT>(g1, a.cols, r1, v1, i1);
             if (LAYOUT == tbh::kDense)
                 tbk::dense_dot2<NORM>(v0, v1, n4, xsrc, lane, a0, a1, s0, s1);
-            else
+            else if (LAYOUT == tbh::kPacked)
                 tbk::packed_dot2<NORM>(v0, i0, v1, i1, a.cols / 8, xsrc, lane, a0, a1, s0, s1);
+            else
+                tbk::quant_dot2<LAYOUT == tbh::kInt8 ? 8 : 4, NORM>(
+                    reinterpret_cast<const uint32_t*>(v0), reinterpret_cast<const uint32_t*>(v1),
+                    tbk::QRow{g0.scales, g0.n_scales, g0.gshift, r0 * a.cols},
+                    tbk::QRow{g1.scales, g1.n_scales, g1.gshift, r1 * a.cols},
+                    qwords<LAYOUT>(a.cols), xsrc, lane, a0, a1, s0, s1);
         }
         tbk::warp_sum2(a0, a1);
         if (ks > 1) {  // the unit's parts, added in part order
@@ -305,7 +330,10 @@ int fused_gemv(const GemvArgs& a, int layout, int epi, cudaStream_t s) {
     if (units == 0) return TB_OK;
     // split rows over more warps when there are few of them (two resident
     // CTAs of 8 warps per SM), at most one part per step of a row
-    const int64_t steps = (layout == kDense ? a.cols / 4 : a.cols / 8) / tbk::kGemvStep + 1;
+    const int64_t steps =
+        layout == kInt8   ? qwords<kInt8>(a.cols) / tbk::kQStep + 1
+        : layout == kInt4 ? qwords<kInt4>(a.cols) / tbk::kQStep + 1
+                          : (layout == kDense ? a.cols / 4 : a.cols / 8) / tbk::kGemvStep + 1;
     int ks = 1;
     while (ks < kWarps && units * ks < (int64_t)ds->sm_count * 2 * kWarps && 2 * ks <= steps) ks *= 2;
     b.units = units;
@@ -314,8 +342,13 @@ int fused_gemv(const GemvArgs& a, int layout, int epi, cudaStream_t s) {
     // one wave of resident CTAs (four per SM): each normalises x once and
     // loops over units (measured faster than two waves of 8 per SM)
     const int grid = ew_grid(units, upc, ds, 4);
-    return layout == kDense ? fgemv_layout<kDense>(b, epi, grid, s)
-                            : fgemv_layout<kPacked>(b, epi, grid, s);
+    switch (layout) {
+        case kDense: return fgemv_layout<kDense>(b, epi, grid, s);
+        case kPacked: return fgemv_layout<kPacked>(b, epi, grid, s);
+        case kInt8: return fgemv_layout<kInt8>(b, epi, grid, s);
+        case kInt4: return fgemv_layout<kInt4>(b, epi, grid, s);
+        default: return TB_ERR_INVALID_ARG;
+    }
 }
 
 int runner_norm(int64_t n, const float* x, const float* w, float* y, float eps, cudaStream_t s) {
@@ -334,7 +367,11 @@ int fused_gemv_setup(int64_t cols) {
     const cudaError_t r[] = {allow_smem<kDense, kPlain>(b),   allow_smem<kDense, kResidual>(b),
                              allow_smem<kDense, kRope>(b),    allow_smem<kDense, kSwiglu>(b),
                              allow_smem<kPacked, kPlain>(b),  allow_smem<kPacked, kResidual>(b),
-                             allow_smem<kPacked, kRope>(b),   allow_smem<kPacked, kSwiglu>(b)};
+                             allow_smem<kPacked, kRope>(b),   allow_smem<kPacked, kSwiglu>(b),
+                             allow_smem<kInt8, kPlain>(b),    allow_smem<kInt8, kResidual>(b),
+                             allow_smem<kInt8, kRope>(b),     allow_smem<kInt8, kSwiglu>(b),
+                             allow_smem<kInt4, kPlain>(b),    allow_smem<kInt4, kResidual>(b),
+                             allow_smem<kInt4, kRope>(b),     allow_smem<kInt4, kSwiglu>(b)};
     for (cudaError_t x : r)
         if (x != cudaSuccess) e = x;
     if (e != cudaSuccess) {

@@ -35,11 +35,15 @@ namespace {
 __global__ void k_advance(int32_t* pos) { *pos += 1; }
 
 struct Proj {
-    const float* w = nullptr;
+    const float* w = nullptr;    // f32 weights (INT8/INT4: the quantized bytes)
     const uint8_t* mask = nullptr;
     const void* vals = nullptr;  // packed 2:4 form, when the mask allows it
     const uint8_t* idx = nullptr;
     int64_t rows = 0, cols = 0;
+    int qbits = 0;               // 8 or 4: kept quantized, expanded inside the GEMV
+    const float* qscales = nullptr;
+    int64_t nsc = 0;
+    int gshift = -1;             // log2(group size), -1 for one group
 };
 
 struct Layer {
@@ -195,10 +199,68 @@ int pack(Runner* r, Proj* p) {
     return TB_OK;
 }
 
+// A device copy of `bytes` at p (borrowed when p already is device memory).
+int upload(Runner* r, const void* p, size_t bytes, const void** out) {
+    int on_dev = 0;
+    tb_b200_is_device_ptr(p, &on_dev);
+    if (on_dev) {
+        *out = p;
+        return TB_OK;
+    }
+    void* d = nullptr;
+    int rc = dev_alloc(r, bytes, &d);
+    if (rc) return rc;
+    TB_CUDA_TRY(cudaMemcpyAsync(d, p, bytes, cudaMemcpyHostToDevice, r->stream));
+    *out = d;
+    return TB_OK;
+}
+
+// An unmasked INT8/INT4 projection whose rows are whole words of 32 inputs
+// and whose scale groups are 0 (one group) or a power of two of at least 8
+// stays quantized: the fused GEMV expands each weight to the same
+// (float)q * scale that Model::get_weight_fp32 gives.
+int keep_quantized(Runner* r, const TbB200Weight& w, Proj* p) {
+    const int64_t gs = (int64_t)w.group_size;
+    const int64_t n = w.rows * w.cols;
+    const size_t qbytes = w.dtype == TB_DTYPE_INT4 ? (size_t)(n + 1) / 2 : (size_t)n;
+    const void *q = nullptr, *sc = nullptr;
+    int rc = upload(r, w.data, qbytes, &q);
+    if (rc) return rc;
+    if (!tbh::aligned16(q)) return TB_ERR_INVALID_ARG;  // caller falls back
+    if (w.n_scales > 0 && w.scales) {
+        if ((rc = upload(r, w.scales, (size_t)w.n_scales * 4, &sc))) return rc;
+    }
+    p->w = static_cast<const float*>(q);
+    p->qbits = w.dtype == TB_DTYPE_INT4 ? 4 : 8;
+    p->qscales = static_cast<const float*>(sc);
+    p->nsc = sc ? w.n_scales : 0;
+    p->gshift = -1;
+    if (gs > 0 && gs < n)
+        for (p->gshift = 0; ((int64_t)1 << p->gshift) < gs; ++p->gshift) {
+        }
+    return TB_OK;
+}
+
+bool quantized_fits(const TbB200Weight& w) {
+    if ((w.dtype != TB_DTYPE_INT8 && w.dtype != TB_DTYPE_INT4) || w.mask) return false;
+    const int64_t gs = (int64_t)w.group_size;
+    return w.cols % 32 == 0 && (gs == 0 || (gs >= 8 && (gs & (gs - 1)) == 0));
+}
+
 int make_proj(Runner* r, const TbB200Weight& w, int64_t rows, int64_t cols, Proj* p) {
     *p = Proj{};
     if (!w.data) return TB_OK;
     if (w.rows != rows || w.cols != cols) return TB_ERR_INVALID_SHAPE;
+    p->rows = rows;
+    p->cols = cols;
+    if (quantized_fits(w)) {
+        const int rq = keep_quantized(r, w, p);
+        if (rq == TB_OK) return TB_OK;
+        if (rq != TB_ERR_INVALID_ARG) return rq;
+        *p = Proj{};  // an unaligned borrowed tensor: dequantise it below
+        p->rows = rows;
+        p->cols = cols;
+    }
     int rc = materialize(r, w, &p->w);
     if (rc) return rc;
     rc = materialize_mask(r, w, &p->mask);
@@ -208,8 +270,14 @@ int make_proj(Runner* r, const TbB200Weight& w, int64_t rows, int64_t cols, Proj
     return pack(r, p);
 }
 
+int fused_layout(const Proj& p);
+tbh::GemvSeg seg_of(const Proj& p, float* y);
+struct Norm;
+int fused_one(Runner* r, int layout, const Proj& p, const float* x, const float* res, float* y);
+
 // y = W x, plus `res` (which may be y itself) when given.
 int project(Runner* r, const Proj& p, const float* x, const float* res, float* y) {
+    if (p.qbits) return fused_one(r, fused_layout(p), p, x, res, y);  // only the fused GEMV reads it
     r->launches++;
     if (p.vals)
         return tb_b200_sparse24_linear(p.rows, p.cols, x, p.vals, p.idx, res, y, r->stream);
@@ -221,6 +289,7 @@ int project(Runner* r, const Proj& p, const float* x, const float* res, float* y
 // The fused-GEMV layout a projection can take (k_runner.cu), or -1.
 int fused_layout(const Proj& p) {
     if (!p.w) return -1;
+    if (p.qbits) return p.qbits == 8 ? tbh::kInt8 : tbh::kInt4;
     if (p.vals) return p.cols % 8 == 0 ? tbh::kPacked : -1;
     if (p.mask) return -1;  // dense-with-mask: the library's sparse GEMV
     return p.cols % 4 == 0 && tbh::aligned16(p.w) ? tbh::kDense : -1;
@@ -238,6 +307,9 @@ tbh::GemvSeg seg_of(const Proj& p, float* y) {
     g.idx = p.idx;
     g.y = y;
     g.rows = p.rows;
+    g.scales = p.qscales;
+    g.n_scales = p.nsc;
+    g.gshift = p.gshift;
     return g;
 }
 
@@ -274,6 +346,11 @@ int fused(Runner* r, int layout, int epi, std::initializer_list<tbh::GemvSeg> se
     a.status = ds ? ds->status : nullptr;
     r->launches++;
     return tbh::fused_gemv(a, layout, epi, r->stream);
+}
+
+// A single projection through the fused GEMV (plain, or with the residual).
+int fused_one(Runner* r, int layout, const Proj& p, const float* x, const float* res, float* y) {
+    return fused(r, layout, res ? tbh::kResidual : tbh::kPlain, {seg_of(p, y)}, x, p.cols, res);
 }
 
 // The token's decoder step, queued on the runner's stream: 5 launches per

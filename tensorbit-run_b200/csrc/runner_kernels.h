@@ -7,13 +7,16 @@
 namespace tbh {
 
 struct GemvSeg {
-    const void* w;       // dense f32 [rows, cols], or the packed float4 values
+    const void* w;       // dense f32 [rows, cols], the packed float4 values, or INT8/INT4 bytes
     const uint8_t* idx;  // packed index bytes (packed layout only)
     float* y;            // output [rows]
     int64_t rows;
+    const float* scales; // INT8/INT4: per-group scales (1.0 past n_scales)
+    int64_t n_scales;
+    int gshift;          // INT8/INT4: log2(group size), -1 for one group
 };
 
-enum GemvLayout { kDense = 0, kPacked = 1 };
+enum GemvLayout { kDense = 0, kPacked = 1, kInt8 = 2, kInt4 = 3 };
 enum GemvEpi { kPlain = 0, kResidual = 1, kRope = 2, kSwiglu = 3 };
 
 struct GemvArgs {
@@ -39,7 +42,8 @@ struct GemvArgs {
 };
 
 // One fused GEMV launch over 1-3 segments sharing x (programmatic dependent
-// launch).  layout kDense needs cols % 4 == 0, kPacked cols % 8 == 0; x and
+// launch).  layout kDense needs cols % 4 == 0, kPacked cols % 8 == 0, kInt8 and
+// kInt4 cols % 32 == 0 and a group size of at least 8 (a power of two); x and
 // the weights 16-byte aligned.  kSwiglu takes two segments of equal rows.
 // With norm set, every CTA normalises x into shared memory first (cols * 4
 // bytes; fused_gemv_setup opts in to more than 48 KB).

@@ -217,3 +217,52 @@ def test_long_rows_split_over_ctas(dev):
     assert_logits(a, want)
     b = run_device(cfg, model, toks[:600], attention=T.ATTN_STANDARD, use_graph=False)
     assert np.array_equal(a[:600], b)
+
+
+def quantized_model(cfg, model, bits, group_size, names=("q", "k", "v", "o", "gate", "up", "down")):
+    """The model with the named projections quantized (.tbm INT8/INT4
+    layout), and the oracle's model over their dequantised weights."""
+    dt = T.INT8 if bits == 8 else T.INT4
+    qlayers, rlayers = [], []
+    for ly in model["layers"]:
+        ql, rl = dict(ly), dict(ly)
+        for n in names:
+            w, m = ly[n]
+            data, scales = quantize(w, bits, group_size)
+            ql[n] = (T.QuantWeight(data, dt, w.shape[0], w.shape[1], scales, group_size), m)
+            rl[n] = (O.dequant(dt, data, scales, group_size, w.size).reshape(w.shape), m)
+        qlayers.append(ql)
+        rlayers.append(rl)
+    return dict(model, layers=qlayers), dict(model, layers=rlayers)
+
+
+@pytest.mark.parametrize("bits,group_size", [(8, 64), (8, 0), (4, 128), (4, 32), (4, 0), (4, 96)])
+def test_unmasked_quantized_projections_stay_quantized(dev, bits, group_size):
+    """Unmasked INT8/INT4 projections are read as bytes by the fused GEMV,
+    each weight expanded to (float)q * scale in registers (group sizes 0 and
+    powers of two from 8); other group sizes (96) are dequantised at load."""
+    cfg, model = mock(seed=53, masks="none", norms="rand")
+    qmodel, rmodel = quantized_model(cfg, model, bits, group_size)
+    toks = tokens(24, cfg["vocab"])
+    a = run_device(cfg, qmodel, toks)
+    assert_logits(a, O.runner_run(cfg, rmodel, toks))
+    assert np.array_equal(a, run_device(cfg, qmodel, toks, use_graph=False))
+
+
+def test_quantized_and_f32_projections_mixed(dev):
+    """Only q and down quantized: the layer's groups no longer share one
+    layout, so each projection is its own launch."""
+    cfg, model = mock(seed=59, masks="none", layers=2)
+    qmodel, rmodel = quantized_model(cfg, model, 4, 64, names=("q", "down"))
+    toks = tokens(16, cfg["vocab"])
+    assert_logits(run_device(cfg, qmodel, toks), O.runner_run(cfg, rmodel, toks))
+
+
+def test_quantized_long_rows_split(dev):
+    """INT4 down projection of 128 rows over 8192 inputs: rows split over
+    several warps."""
+    cfg, model = mock(seed=61, hidden=128, heads=4, kv=4, inter=8192, layers=1, vocab=100,
+                      max_seq=16, masks="none", norms="rand")
+    qmodel, rmodel = quantized_model(cfg, model, 4, 128)
+    toks = tokens(10, cfg["vocab"])
+    assert_logits(run_device(cfg, qmodel, toks), O.runner_run(cfg, rmodel, toks))
