@@ -180,24 +180,40 @@ __device__ __forceinline__ float qval(uint32_t wx, int k) {  // wx: word with si
 }
 
 template <int BITS>
-__device__ __forceinline__ float qscale(const float* sc, int64_t nsc, int gshift, int64_t f) {
-    const int64_t g = gshift < 0 ? 0 : f >> gshift;
+__device__ __forceinline__ float qscale(const float* sc, uint32_t nsc, int gshift, uint32_t f) {
+    const uint32_t g = gshift < 0 ? 0u : f >> gshift;
     return g < nsc ? __ldg(sc + g) : 1.0f;
 }
 
-// One word of a row against x: acc += x[e] * ((float)q[e] * scale).
+// One word of a row against x: acc += x[e] * ((float)q[e] * scale).  INT4:
+// each byte's low nibble enters the mantissa as q + 8, its high nibble in
+// place as 16 (q + 8); the latter is scaled by scale / 16 (exact: a power of
+// two), so both products equal (float)q * scale.
 template <int BITS, bool XS>
 __device__ __forceinline__ float qword_dot(uint32_t w, float scale, const float4* x4, int64_t word,
                                            float acc) {
     const uint32_t wx = w ^ (BITS == 8 ? 0x80808080u : 0x88888888u);
-    constexpr int kPer = 32 / BITS;
+    if constexpr (BITS == 8) {
+        const float4 xv = ldx<XS>(x4 + word);
+        acc = __fmaf_rn(xv.x, __fmul_rn(qval<8>(wx, 0), scale), acc);
+        acc = __fmaf_rn(xv.y, __fmul_rn(qval<8>(wx, 1), scale), acc);
+        acc = __fmaf_rn(xv.z, __fmul_rn(qval<8>(wx, 2), scale), acc);
+        acc = __fmaf_rn(xv.w, __fmul_rn(qval<8>(wx, 3), scale), acc);
+    } else {
+        const float s16 = __fmul_rn(scale, 0.0625f);
 #pragma unroll
-    for (int h = 0; h < kPer / 4; ++h) {
-        const float4 xv = ldx<XS>(x4 + word * (kPer / 4) + h);
-        acc = __fmaf_rn(xv.x, __fmul_rn(qval<BITS>(wx, 4 * h + 0), scale), acc);
-        acc = __fmaf_rn(xv.y, __fmul_rn(qval<BITS>(wx, 4 * h + 1), scale), acc);
-        acc = __fmaf_rn(xv.z, __fmul_rn(qval<BITS>(wx, 4 * h + 2), scale), acc);
-        acc = __fmaf_rn(xv.w, __fmul_rn(qval<BITS>(wx, 4 * h + 3), scale), acc);
+        for (int h = 0; h < 2; ++h) {
+            const float4 xv = ldx<XS>(x4 + 2 * word + h);
+            const uint32_t b0 = wx >> (16 * h), b1 = wx >> (16 * h + 8);
+            const float q0 = __fsub_rn(__uint_as_float((b0 & 0xFu) | 0x4B000000u), 8388616.0f);
+            const float q1 = __fsub_rn(__uint_as_float((b0 & 0xF0u) | 0x4B000000u), 8388736.0f);
+            const float q2 = __fsub_rn(__uint_as_float((b1 & 0xFu) | 0x4B000000u), 8388616.0f);
+            const float q3 = __fsub_rn(__uint_as_float((b1 & 0xF0u) | 0x4B000000u), 8388736.0f);
+            acc = __fmaf_rn(xv.x, __fmul_rn(q0, scale), acc);
+            acc = __fmaf_rn(xv.y, __fmul_rn(q1, s16), acc);
+            acc = __fmaf_rn(xv.z, __fmul_rn(q2, scale), acc);
+            acc = __fmaf_rn(xv.w, __fmul_rn(q3, s16), acc);
+        }
     }
     return acc;
 }
@@ -207,9 +223,9 @@ __device__ __forceinline__ float qword_dot(uint32_t w, float scale, const float4
 // element in the tensor.
 struct QRow {
     const float* sc;
-    int64_t nsc;
+    uint32_t nsc;
     int gshift;
-    int64_t f;
+    uint32_t f;  // tensors of fewer than 2^31 weights
 };
 
 // Partial sums of two quantized rows (which may belong to different
@@ -237,20 +253,22 @@ __device__ __forceinline__ void quant_dot2(const uint32_t* __restrict__ d0,
 #pragma unroll
         for (int u = 0; u < kQU; ++u) {
             const int64_t w = w0 + 32 * u;
-            a0 = qword_dot<BITS, XS>(r0[u], qscale<BITS>(q0.sc, q0.nsc, q0.gshift, q0.f + w * kPer),
-                                     x4, w, a0);
-            a1 = qword_dot<BITS, XS>(r1[u], qscale<BITS>(q1.sc, q1.nsc, q1.gshift, q1.f + w * kPer),
-                                     x4, w, a1);
+            const uint32_t e = (uint32_t)w * kPer;
+            a0 = qword_dot<BITS, XS>(r0[u], qscale<BITS>(q0.sc, q0.nsc, q0.gshift, q0.f + e), x4, w,
+                                     a0);
+            a1 = qword_dot<BITS, XS>(r1[u], qscale<BITS>(q1.sc, q1.nsc, q1.gshift, q1.f + e), x4, w,
+                                     a1);
         }
     }
     if (s1 <= full) return;
     for (int u = 0; u < kQU; ++u) {  // the partial step
         const int64_t w = full * kQStep + 32 * u + lane;
         if (w >= words) break;
-        a0 = qword_dot<BITS, XS>(__ldcs(d0 + w),
-                                 qscale<BITS>(q0.sc, q0.nsc, q0.gshift, q0.f + w * kPer), x4, w, a0);
-        a1 = qword_dot<BITS, XS>(__ldcs(d1 + w),
-                                 qscale<BITS>(q1.sc, q1.nsc, q1.gshift, q1.f + w * kPer), x4, w, a1);
+        const uint32_t e = (uint32_t)w * kPer;
+        a0 = qword_dot<BITS, XS>(__ldcs(d0 + w), qscale<BITS>(q0.sc, q0.nsc, q0.gshift, q0.f + e),
+                                 x4, w, a0);
+        a1 = qword_dot<BITS, XS>(__ldcs(d1 + w), qscale<BITS>(q1.sc, q1.nsc, q1.gshift, q1.f + e),
+                                 x4, w, a1);
     }
 }
 

@@ -244,7 +244,8 @@ int keep_quantized(Runner* r, const TbB200Weight& w, Proj* p) {
 bool quantized_fits(const TbB200Weight& w) {
     if ((w.dtype != TB_DTYPE_INT8 && w.dtype != TB_DTYPE_INT4) || w.mask) return false;
     const int64_t gs = (int64_t)w.group_size;
-    return w.cols % 32 == 0 && (gs == 0 || (gs >= 8 && (gs & (gs - 1)) == 0));
+    return w.cols % 32 == 0 && w.rows * w.cols < ((int64_t)1 << 31) && w.n_scales < ((int64_t)1 << 31) &&
+           (gs == 0 || (gs >= 8 && (gs & (gs - 1)) == 0));
 }
 
 int make_proj(Runner* r, const TbB200Weight& w, int64_t rows, int64_t cols, Proj* p) {
