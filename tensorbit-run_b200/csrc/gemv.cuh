@@ -159,8 +159,9 @@ __device__ __forceinline__ void dense_dot2(const float4* __restrict__ w0,
 // include/tensorbit/run/model.hpp:181-225): element i of the tensor is byte
 // i (INT8) or the low (even i) / high (odd i) nibble of byte i / 2 (INT4),
 // two's complement, with an f32 scale per group of gs consecutive elements
-// (1.0 past the last scale).  The weight is (float)q * scale -- here too, so
-// each product is the reference's; only the summation order differs.
+// (1.0 past the last scale; the runner sends tensors with fewer scales than
+// groups to the dequantising path).  The weight is (float)q * scale -- here
+// too, so each product is the reference's; only the summation order differs.
 //
 // Lanes take consecutive 32-bit words (4 INT8 or 8 INT4 weights), so their
 // float4s of x are contiguous across the warp; eight words per lane and row
@@ -179,53 +180,58 @@ __device__ __forceinline__ float qval(uint32_t wx, int k) {  // wx: word with si
         return __fsub_rn(__uint_as_float(0x4B000000u | ((wx >> (4 * k)) & 0xFu)), 8388616.0f);
 }
 
-template <int BITS>
-__device__ __forceinline__ float qscale(const float* sc, uint32_t nsc, int gshift, uint32_t f) {
-    const uint32_t g = gshift < 0 ? 0u : f >> gshift;
-    return g < nsc ? __ldg(sc + g) : 1.0f;
+// The scale of element f: the caller guarantees every group has one (a
+// tensor of one group has gshift 31).
+__device__ __forceinline__ float qscale(const float* sc, int gshift, uint32_t f) {
+    return __ldg(sc + (f >> gshift));
 }
 
-// One word of a row against x: acc += x[e] * ((float)q[e] * scale).  INT4:
-// each byte's low nibble enters the mantissa as q + 8, its high nibble in
-// place as 16 (q + 8); the latter is scaled by scale / 16 (exact: a power of
-// two), so both products equal (float)q * scale.
+// One word of a row against x: acc += x[e] * ((float)q[e] * scale).
+// INT4: nibble k (k <= 4) enters the float in place, as 16^k (q + 8) in the
+// low mantissa of 2^23, with no shift; subtracting 2^23 + 8 * 16^k leaves
+// 16^k q, scaled by scale / 16^k (exact: a power of two), so the product is
+// (float)q * scale.  Nibbles 5-7 are the same after one 16-bit shift.
 template <int BITS, bool XS>
 __device__ __forceinline__ float qword_dot(uint32_t w, float scale, const float4* x4, int64_t word,
                                            float acc) {
-    const uint32_t wx = w ^ (BITS == 8 ? 0x80808080u : 0x88888888u);
     if constexpr (BITS == 8) {
+        const uint32_t wx = w ^ 0x80808080u;
         const float4 xv = ldx<XS>(x4 + word);
         acc = __fmaf_rn(xv.x, __fmul_rn(qval<8>(wx, 0), scale), acc);
         acc = __fmaf_rn(xv.y, __fmul_rn(qval<8>(wx, 1), scale), acc);
         acc = __fmaf_rn(xv.z, __fmul_rn(qval<8>(wx, 2), scale), acc);
         acc = __fmaf_rn(xv.w, __fmul_rn(qval<8>(wx, 3), scale), acc);
     } else {
-        const float s16 = __fmul_rn(scale, 0.0625f);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const float4 xv = ldx<XS>(x4 + 2 * word + h);
-            const uint32_t b0 = wx >> (16 * h), b1 = wx >> (16 * h + 8);
-            const float q0 = __fsub_rn(__uint_as_float((b0 & 0xFu) | 0x4B000000u), 8388616.0f);
-            const float q1 = __fsub_rn(__uint_as_float((b0 & 0xF0u) | 0x4B000000u), 8388736.0f);
-            const float q2 = __fsub_rn(__uint_as_float((b1 & 0xFu) | 0x4B000000u), 8388616.0f);
-            const float q3 = __fsub_rn(__uint_as_float((b1 & 0xF0u) | 0x4B000000u), 8388736.0f);
-            acc = __fmaf_rn(xv.x, __fmul_rn(q0, scale), acc);
-            acc = __fmaf_rn(xv.y, __fmul_rn(q1, s16), acc);
-            acc = __fmaf_rn(xv.z, __fmul_rn(q2, scale), acc);
-            acc = __fmaf_rn(xv.w, __fmul_rn(q3, s16), acc);
-        }
+        const uint32_t wx = w ^ 0x88888888u, hi = wx >> 16;
+        const float s1 = __fmul_rn(scale, 0.0625f), s2 = __fmul_rn(scale, 0.00390625f);
+        const float s3 = __fmul_rn(scale, 0.000244140625f), s4 = __fmul_rn(scale, 1.52587890625e-05f);
+        const float4 xa = ldx<XS>(x4 + 2 * word), xb = ldx<XS>(x4 + 2 * word + 1);
+        const float q0 = __fsub_rn(__uint_as_float((wx & 0xFu) | 0x4B000000u), 8388616.0f);
+        const float q1 = __fsub_rn(__uint_as_float((wx & 0xF0u) | 0x4B000000u), 8388736.0f);
+        const float q2 = __fsub_rn(__uint_as_float((wx & 0xF00u) | 0x4B000000u), 8390656.0f);
+        const float q3 = __fsub_rn(__uint_as_float((wx & 0xF000u) | 0x4B000000u), 8421376.0f);
+        const float q4 = __fsub_rn(__uint_as_float((wx & 0xF0000u) | 0x4B000000u), 8912896.0f);
+        const float q5 = __fsub_rn(__uint_as_float((hi & 0xF0u) | 0x4B000000u), 8388736.0f);
+        const float q6 = __fsub_rn(__uint_as_float((hi & 0xF00u) | 0x4B000000u), 8390656.0f);
+        const float q7 = __fsub_rn(__uint_as_float((hi & 0xF000u) | 0x4B000000u), 8421376.0f);
+        acc = __fmaf_rn(xa.x, __fmul_rn(q0, scale), acc);
+        acc = __fmaf_rn(xa.y, __fmul_rn(q1, s1), acc);
+        acc = __fmaf_rn(xa.z, __fmul_rn(q2, s2), acc);
+        acc = __fmaf_rn(xa.w, __fmul_rn(q3, s3), acc);
+        acc = __fmaf_rn(xb.x, __fmul_rn(q4, s4), acc);
+        acc = __fmaf_rn(xb.y, __fmul_rn(q5, s1), acc);
+        acc = __fmaf_rn(xb.z, __fmul_rn(q6, s2), acc);
+        acc = __fmaf_rn(xb.w, __fmul_rn(q7, s3), acc);
     }
     return acc;
 }
 
-// A quantized row's scales: the tensor's scale array, its length, log2 of
-// its group size (-1: one group), and the flat index of the row's first
-// element in the tensor.
+// A quantized row's scales: the tensor's scale array, log2 of its group
+// size, and the flat index of the row's first element in the tensor.
 struct QRow {
-    const float* sc;
-    uint32_t nsc;
-    int gshift;
-    uint32_t f;  // tensors of fewer than 2^31 weights
+    const float* sc;  // one scale per group, every group present
+    int gshift;       // 31 for a tensor of one group
+    uint32_t f;       // tensors of fewer than 2^31 weights
 };
 
 // Partial sums of two quantized rows (which may belong to different
@@ -254,9 +260,9 @@ __device__ __forceinline__ void quant_dot2(const uint32_t* __restrict__ d0,
         for (int u = 0; u < kQU; ++u) {
             const int64_t w = w0 + 32 * u;
             const uint32_t e = (uint32_t)w * kPer;
-            a0 = qword_dot<BITS, XS>(r0[u], qscale<BITS>(q0.sc, q0.nsc, q0.gshift, q0.f + e), x4, w,
+            a0 = qword_dot<BITS, XS>(r0[u], qscale(q0.sc, q0.gshift, q0.f + e), x4, w,
                                      a0);
-            a1 = qword_dot<BITS, XS>(r1[u], qscale<BITS>(q1.sc, q1.nsc, q1.gshift, q1.f + e), x4, w,
+            a1 = qword_dot<BITS, XS>(r1[u], qscale(q1.sc, q1.gshift, q1.f + e), x4, w,
                                      a1);
         }
     }
@@ -265,9 +271,9 @@ __device__ __forceinline__ void quant_dot2(const uint32_t* __restrict__ d0,
         const int64_t w = full * kQStep + 32 * u + lane;
         if (w >= words) break;
         const uint32_t e = (uint32_t)w * kPer;
-        a0 = qword_dot<BITS, XS>(__ldcs(d0 + w), qscale<BITS>(q0.sc, q0.nsc, q0.gshift, q0.f + e),
+        a0 = qword_dot<BITS, XS>(__ldcs(d0 + w), qscale(q0.sc, q0.gshift, q0.f + e),
                                  x4, w, a0);
-        a1 = qword_dot<BITS, XS>(__ldcs(d1 + w), qscale<BITS>(q1.sc, q1.nsc, q1.gshift, q1.f + e),
+        a1 = qword_dot<BITS, XS>(__ldcs(d1 + w), qscale(q1.sc, q1.gshift, q1.f + e),
                                  x4, w, a1);
     }
 }

@@ -208,8 +208,8 @@ __global__ void __launch_bounds__(kThreads, 4) k_fgemv(const __grid_constant__ G
             else
                 tbk::quant_dot2<LAYOUT == tbh::kInt8 ? 8 : 4, NORM>(
                     reinterpret_cast<const uint32_t*>(v0), reinterpret_cast<const uint32_t*>(v1),
-                    tbk::QRow{g0.scales, (uint32_t)g0.n_scales, g0.gshift, (uint32_t)(r0 * a.cols)},
-                    tbk::QRow{g1.scales, (uint32_t)g1.n_scales, g1.gshift, (uint32_t)(r1 * a.cols)},
+                    tbk::QRow{g0.scales, g0.gshift, (uint32_t)(r0 * a.cols)},
+                    tbk::QRow{g1.scales, g1.gshift, (uint32_t)(r1 * a.cols)},
                     qwords<LAYOUT>(a.cols), xsrc, lane, a0, a1, s0, s1);
         }
         tbk::warp_sum2(a0, a1);

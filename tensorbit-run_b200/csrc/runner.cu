@@ -43,7 +43,7 @@ struct Proj {
     int qbits = 0;               // 8 or 4: kept quantized, expanded inside the GEMV
     const float* qscales = nullptr;
     int64_t nsc = 0;
-    int gshift = -1;             // log2(group size), -1 for one group
+    int gshift = 31;             // log2(group size), 31 for one group
 };
 
 struct Layer {
@@ -234,7 +234,7 @@ int keep_quantized(Runner* r, const TbB200Weight& w, Proj* p) {
     p->qbits = w.dtype == TB_DTYPE_INT4 ? 4 : 8;
     p->qscales = static_cast<const float*>(sc);
     p->nsc = sc ? w.n_scales : 0;
-    p->gshift = -1;
+    p->gshift = 31;  // one group
     if (gs > 0 && gs < n)
         for (p->gshift = 0; ((int64_t)1 << p->gshift) < gs; ++p->gshift) {
         }
@@ -244,7 +244,10 @@ int keep_quantized(Runner* r, const TbB200Weight& w, Proj* p) {
 bool quantized_fits(const TbB200Weight& w) {
     if ((w.dtype != TB_DTYPE_INT8 && w.dtype != TB_DTYPE_INT4) || w.mask) return false;
     const int64_t gs = (int64_t)w.group_size;
-    return w.cols % 32 == 0 && w.rows * w.cols < ((int64_t)1 << 31) && w.n_scales < ((int64_t)1 << 31) &&
+    const int64_t n = w.rows * w.cols;
+    const int64_t groups = gs == 0 || gs >= n ? 1 : (n + gs - 1) / gs;
+    // every group has its scale (the kernel reads one per group, unchecked)
+    return w.cols % 32 == 0 && n < ((int64_t)1 << 31) && w.scales && w.n_scales >= groups &&
            (gs == 0 || (gs >= 8 && (gs & (gs - 1)) == 0));
 }
 

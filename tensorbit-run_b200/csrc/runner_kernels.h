@@ -11,9 +11,9 @@ struct GemvSeg {
     const uint8_t* idx;  // packed index bytes (packed layout only)
     float* y;            // output [rows]
     int64_t rows;
-    const float* scales; // INT8/INT4: per-group scales (1.0 past n_scales)
+    const float* scales; // INT8/INT4: one scale per group, every group present
     int64_t n_scales;
-    int gshift;          // INT8/INT4: log2(group size), -1 for one group
+    int gshift;          // INT8/INT4: log2(group size), 31 for one group
 };
 
 enum GemvLayout { kDense = 0, kPacked = 1, kInt8 = 2, kInt4 = 3 };
