@@ -56,7 +56,11 @@ CONFIGS = {
     "runner": (W.CONFIGS["7b"], None, "TransformerRunner decode of one sequence at the llama7b "
                                       "shape (32 layers, f32 weights, 2:4-pruned projections), "
                                       "one CUDA graph per token"),
+    "runner_int4": (W.CONFIGS["7b"], None, "TransformerRunner decode of one sequence at the llama7b "
+                                           "shape (32 layers, INT4 projections in groups of 128, "
+                                           "f32 embedding and lm head), one CUDA graph per token"),
 }
+RUNNER_GROUP = 128  # INT4 scale group of --config runner_int4
 RUNNER_LAYERS = 32
 RUNNER_MAX_SEQ = 2048
 RUNNER_CONTEXT = 1024  # tokens fed (untimed) before the timed ones: decode at context 1024+
@@ -468,24 +472,29 @@ def runner_shapes(cfg):
                 down=(H, I))
 
 
-def runner_token_bytes(cfg, pos):
+def runner_token_bytes(cfg, pos, int4=False):
     """Algorithmic bytes of one token at position `pos` in the runner's
-    layout: packed 2:4 projections (kept f32 values + index bytes), the
-    dense f32 lm head, the embedding row, the norm weights, and the KV cache
-    (rows 0..pos-1 read for every layer, row pos written)."""
+    layout: packed 2:4 projections (kept f32 values + index bytes) or INT4
+    projections (bytes + scales), the dense f32 lm head, the embedding row,
+    the norm weights, and the KV cache (rows 0..pos-1 read for every layer,
+    row pos written)."""
     H, L = cfg["hidden"], cfg["layers"]
     kvd = cfg["n_kv_heads"] * cfg["head_dim"]
     proj = 0
     for rows, cols in runner_shapes(cfg).values():
+        if int4:  # half a byte per weight, a 4-byte scale per group
+            proj += rows * cols // 2 + rows * cols // RUNNER_GROUP * 4
+            continue
         pairs = cols // 8
         proj += rows * pairs * 16 + rows * ((pairs + 127) // 128 * 128)
     return (L * proj + cfg["vocab"] * H * 4 + H * 4 + (2 * L + 1) * H * 4
             + L * 2 * kvd * 4 * (pos + 1))
 
 
-def runner_model_torch(torch, dev, cfg, seed):
+def runner_model_torch(torch, dev, cfg, seed, int4=False):
     """Weights U(-0.01, 0.01) (the engine's mock initialisation), random 2:4
-    masks, norm weights 1 + N(0, 0.1); all f32 on the device."""
+    masks, norm weights 1 + N(0, 0.1); all f32 on the device.  int4: the
+    projections are random INT4 bytes with scales per 128 weights."""
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
     pats = torch.tensor(PATTERNS_2_4, dtype=torch.uint8, device=dev)
@@ -496,11 +505,20 @@ def runner_model_torch(torch, dev, cfg, seed):
     def nv():
         return 1 + 0.1 * torch.randn(cfg["hidden"], generator=g, device=dev)
 
+    def q4(r, c):  # random INT4 bytes, scales U(0, 0.002)
+        import tb_b200 as T
+        data = torch.randint(0, 256, (r * c // 2,), dtype=torch.uint8, generator=g, device=dev)
+        scales = torch.rand(r * c // RUNNER_GROUP, generator=g, device=dev) * 0.002
+        return (T.QuantWeight(data, T.INT4, r, c, scales, RUNNER_GROUP), None)
+
     layers = []
     for _ in range(cfg["layers"]):
-        ly = {n: (w(r, c), pats[torch.randint(0, len(PATTERNS_2_4), (r, c // 4), generator=g,
-                                              device=dev)].contiguous())
-              for n, (r, c) in runner_shapes(cfg).items()}
+        if int4:
+            ly = {n: q4(r, c) for n, (r, c) in runner_shapes(cfg).items()}
+        else:
+            ly = {n: (w(r, c), pats[torch.randint(0, len(PATTERNS_2_4), (r, c // 4), generator=g,
+                                                  device=dev)].contiguous())
+                  for n, (r, c) in runner_shapes(cfg).items()}
         ly["in_norm"], ly["post_norm"] = nv(), nv()
         layers.append(ly)
     return dict(embed=w(cfg["vocab"], cfg["hidden"]), final_norm=nv(),
@@ -560,7 +578,8 @@ def run_runner(args, rank, world, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     cfg = runner_cfg(RUNNER_LAYERS)
-    model = runner_model_torch(torch, dev, cfg, 777 + rank)
+    int4 = args.config == "runner_int4"
+    model = runner_model_torch(torch, dev, cfg, 777 + rank, int4=int4)
     runner = T.Runner(cfg, model, attention=T.ATTN_STANDARD, use_graph=True)
     stream = torch.cuda.ExternalStream(runner.stream.value)
     n_tok = RUNNER_CONTEXT + args.warmup + args.steps + max(3, min(args.steps, 20)) + 8
@@ -613,16 +632,19 @@ def run_runner(args, rank, world, local):
     runner.close()
 
     mean_pos = pos0 + (args.steps - 1) / 2
-    tb = runner_token_bytes(cfg, mean_pos)
+    tb = runner_token_bytes(cfg, mean_pos, int4=int4)
     peak, peak_kind = peaks()
     achieved = tb / (ms / 1e3) / 1e9
     tok_s = world * 1e3 / ms
     return {
         "metric": RUNNER_METRIC, "value": round(tok_s, 2), "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded; weights U(-0.01, 0.01) as the engine's mock model, "
-                "random 2:4 masks, norm weights 1 + N(0, 0.1))",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int4 weights, f32 arithmetic" if int4 else "f32",
+        "data": ("synthetic (seeded; random INT4 projections, scales per 128 weights, "
+                 "norm weights 1 + N(0, 0.1))" if int4 else
+                 "synthetic (seeded; weights U(-0.01, 0.01) as the engine's mock model, "
+                 "random 2:4 masks, norm weights 1 + N(0, 0.1))"),
         "config": {"workload": WORKLOAD, "layers": RUNNER_LAYERS, "hidden": cfg["hidden"],
                    "heads": [cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"]],
                    "intermediate": cfg["intermediate"], "vocab": cfg["vocab"],
@@ -905,7 +927,8 @@ def main():
                     help="7b (default): the Llama-7B prefill step; 70b: the Llama-70B prefill's "
                          "layer ops and the sweep's 4096 x 128256 softmax/argmax; decode: the "
                          "32-layer chain over a 256-sequence decode batch; runner: single-"
-                         "sequence decode through the device TransformerRunner")
+                         "sequence decode through the device TransformerRunner (f32, 2:4); "
+                         "runner_int4: the same with INT4 projections")
     ap.add_argument("--rows", type=int, default=None, help="layer-op rows per GPU (config's)")
     args = ap.parse_args()
     global CFG, LOGIT_ROWS, WORKLOAD
@@ -919,7 +942,8 @@ def main():
 
     if args.impl == "reference":
         if rank == 0:
-            print(json.dumps(run_reference_runner(args, world) if args.config == "runner"
+            print(json.dumps(run_reference_runner(args, world)
+                             if args.config in ("runner", "runner_int4")
                              else run_reference(args, world)))
         return
 
@@ -931,12 +955,13 @@ def main():
                                 device_id=torch.device("cuda", local))
     try:
         decode = args.config == "decode"
-        run = {"decode": run_decode, "runner": run_runner}.get(args.config, run_gpu)
+        run = {"decode": run_decode, "runner": run_runner,
+               "runner_int4": run_runner}.get(args.config, run_gpu)
         line = run(args, rank, world, local)
         if line is None:
             return
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
-            if args.config == "runner":
+            if args.config in ("runner", "runner_int4"):
                 per_token, sample = cpu_sample_runner()
                 line["cpu_baseline"] = {"value": round(1.0 / per_token, 4), "unit": "tokens/s",
                                         "cores": 1, "kind": "port", "sample": sample}
