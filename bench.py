@@ -577,7 +577,7 @@ def run_runner(args, rank, world, local):
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    cfg = runner_cfg(RUNNER_LAYERS)
+    cfg = runner_cfg(args.runner_layers)
     int4 = args.config == "runner_int4"
     model = runner_model_torch(torch, dev, cfg, 777 + rank, int4=int4)
     runner = T.Runner(cfg, model, attention=T.ATTN_STANDARD, use_graph=True)
@@ -645,7 +645,7 @@ def run_runner(args, rank, world, local):
                  "norm weights 1 + N(0, 0.1))" if int4 else
                  "synthetic (seeded; weights U(-0.01, 0.01) as the engine's mock model, "
                  "random 2:4 masks, norm weights 1 + N(0, 0.1))"),
-        "config": {"workload": WORKLOAD, "layers": RUNNER_LAYERS, "hidden": cfg["hidden"],
+        "config": {"workload": WORKLOAD, "layers": cfg["layers"], "hidden": cfg["hidden"],
                    "heads": [cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"]],
                    "intermediate": cfg["intermediate"], "vocab": cfg["vocab"],
                    "max_seq": RUNNER_MAX_SEQ, "attention": "standard (every key of the row)",
@@ -930,6 +930,8 @@ def main():
                          "sequence decode through the device TransformerRunner (f32, 2:4); "
                          "runner_int4: the same with INT4 projections")
     ap.add_argument("--rows", type=int, default=None, help="layer-op rows per GPU (config's)")
+    ap.add_argument("--runner-layers", type=int, default=RUNNER_LAYERS,
+                    help="layers of the runner configs' model (32; fewer for small ncu captures)")
     args = ap.parse_args()
     global CFG, LOGIT_ROWS, WORKLOAD
     CFG, LOGIT_ROWS, WORKLOAD = CONFIGS[args.config]
