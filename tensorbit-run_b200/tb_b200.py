@@ -592,10 +592,10 @@ class Runner:
             if w is None:
                 return Weight()
             if isinstance(w, QuantWeight):
-                sc = addr(w.scales, np.float32)
+                sc = w.scales
+                n_sc = 0 if sc is None else int(sc.numel() if hasattr(sc, "numel") else np.size(sc))
                 return Weight(addr(w.data, np.uint8), w.dtype, w.rows, w.cols, addr(mask, np.uint8),
-                              sc, 0 if w.scales is None else int(np.size(w.scales) if not hasattr(
-                                  w.scales, "numel") else w.scales.numel()), w.group_size)
+                              addr(sc, np.float32), n_sc, w.group_size)
             return Weight(addr(w, np.float32), F32, w.shape[0], w.shape[1], addr(mask, np.uint8),
                           None, 0, 0)
 
