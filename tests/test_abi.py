@@ -64,6 +64,32 @@ def test_no_device_is_not_an_error():
     assert n.value >= 0
 
 
+def test_decoder_entry_points_check_arguments_before_device_work():
+    """The decoder's entry points reject bad arguments before they touch a
+    device (so these run without a GPU): TB_ERR_INVALID_ARG (8) and
+    TB_ERR_INVALID_SHAPE (9)."""
+    L = T.lib()
+    h = C.c_void_p()
+    assert L.tb_b200_runner_create(None, C.byref(h)) == 8
+    d = T.RunnerDesc()  # hidden 0
+    assert L.tb_b200_runner_create(C.byref(d), C.byref(h)) == 9 and not h.value
+    assert L.tb_b200_runner_forward(None, 0, None) == 8
+    assert L.tb_b200_runner_logits(None, None) == 8
+    assert L.tb_b200_runner_reset(None) == 8
+    assert L.tb_b200_runner_destroy(None) == 0
+    buf = (C.c_float * 64)()
+    p = C.cast(buf, C.c_void_p)
+    args = [p] * 7 + [None]
+    assert L.tb_b200_decode_attention(7, 8, 8, 64, 16, *args) == 8     # no such layout
+    assert L.tb_b200_decode_attention(0, 8, 8, 512, 16, *args) == 9    # head_dim > 256
+    assert L.tb_b200_decode_attention(0, 8, 3, 64, 16, *args) == 9     # heads not a multiple
+    assert L.tb_b200_decode_attention(1, 8, 8, 64, 16, None, *args[1:]) == 8
+    assert L.tb_b200_sparse24_linear(4, 12, p, p, p, None, p, None) == 9  # 3 groups: no pairs
+    assert L.tb_b200_sparse24_linear(4, 16, None, p, p, None, p, None) == 8
+    assert L.tb_b200_sparse24_linear(-1, 16, p, p, p, None, p, None) == 9
+    assert L.tb_b200_sparse24_pack(4, 16, None, p, p, p, p, None) == 8
+
+
 def test_partition_rule():
     lo, hi = C.c_int64(), C.c_int64()
     for total, parts in [(16384, 8), (10, 3), (5, 8), (128256, 7)]:
