@@ -427,6 +427,33 @@ int tb_b200_embedding_sharded(int dtype, int64_t n_tokens, int64_t dim, int64_t 
                               const int32_t* ids_host, const void* table_shard, void* y_local,
                               void* stream);
 
+/* Peer memory of the other GPUs of one box, through CUDA IPC, for the
+ * one-kernel sharded gather below.  The owner of a device buffer exports a
+ * handle (TB_B200_P2P_HANDLE_BYTES bytes) and the buffer's offset within its
+ * allocation; the handle and offset go to the other processes out of band;
+ * each opens them into a device pointer valid in its own context until it
+ * closes it (tb_b200_p2p_close, with the same offset).  The owner must keep
+ * the buffer alive until every importer has closed it. */
+#define TB_B200_P2P_HANDLE_BYTES 64
+int tb_b200_p2p_export(const void* dev_ptr, void* handle_out, int64_t* offset_out);
+int tb_b200_p2p_import(const void* handle, int64_t offset, void** dev_ptr_out);
+int tb_b200_p2p_close(void* dev_ptr, int64_t offset);
+
+/* Vocab-sharded embedding gather as one kernel, no collective.  The same
+ * computation as tb_b200_embedding_sharded (the reference's per-token row
+ * copy, src/ops/embedding.c:4-14, over a table split by vocabulary rows):
+ * shards[r] (rank order, nranks <= 8) is rank r's table part
+ * (tb_b200_partition(vocab, nranks, r)) -- this rank's own pointer for its
+ * own part, imported pointers for the others' -- and ids (n_tokens DEVICE
+ * int32) are the tokens whose rows this call writes to y [n_tokens, dim].
+ * Each row is read from its owner's memory (a peer load over NVLink when
+ * the owner is another GPU) and written once: bit-exact with
+ * tb_cpu_embedding_f32 over the full table.  Ids outside [0, vocab) give a
+ * zero row and raise TB_B200_FLAG_TOKEN_RANGE (tb_b200_check_status). */
+int tb_b200_embedding_sharded_p2p(int dtype, int64_t n_tokens, int64_t dim, int64_t vocab,
+                                  const int32_t* ids, const void* const* shards, int nranks,
+                                  void* y, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -154,6 +154,10 @@ SIGNATURES = {
     "tb_b200_comm_destroy": (i32, []),
     "tb_b200_comm_info": (i32, [P(i32), P(i32)]),
     "tb_b200_embedding_sharded": (i32, [i32, i64, i64, i64, vp, vp, vp, vp]),
+    "tb_b200_embedding_sharded_p2p": (i32, [i32, i64, i64, i64, vp, P(vp), i32, vp, vp]),
+    "tb_b200_p2p_export": (i32, [vp, vp, P(i64)]),
+    "tb_b200_p2p_import": (i32, [vp, i64, P(vp)]),
+    "tb_b200_p2p_close": (i32, [vp, i64]),
     # registry (include/tb_backend.h)
     "tb_backend_register": (i32, [vp]),
     "tb_backend_register_device": (i32, [vp, i32]),
@@ -534,6 +538,49 @@ def embedding_sharded(ids_host, table_shard, vocab: int, y_local=None, stream=No
                                           vocab, ids.ctypes.data, ptr(table_shard), ptr(y_local),
                                           stream or cur_stream()), "embedding_sharded")
     return y_local
+
+
+P2P_HANDLE_BYTES = 64
+
+
+def p2p_export(t):
+    """(handle bytes, offset) of CUDA tensor t's allocation, for the other
+    processes of the box to import (tb_b200_p2p_export)."""
+    _dev(t)
+    h = C.create_string_buffer(P2P_HANDLE_BYTES)
+    off = C.c_int64()
+    check(lib().tb_b200_p2p_export(ptr(t), h, C.byref(off)), "p2p_export")
+    return h.raw, off.value
+
+
+def p2p_import(handle: bytes, offset: int) -> int:
+    """Device address, in this process, of a buffer another process exported."""
+    p = vp()
+    check(lib().tb_b200_p2p_import(C.create_string_buffer(bytes(handle), P2P_HANDLE_BYTES),
+                                   offset, C.byref(p)), "p2p_import")
+    return p.value
+
+
+def p2p_close(addr: int, offset: int) -> None:
+    check(lib().tb_b200_p2p_close(vp(addr), offset), "p2p_close")
+
+
+def embedding_sharded_p2p(ids, shard_addrs, vocab: int, dim: int, dtype, y=None, stream=None):
+    """The rows of `ids` (int32 CUDA tensor) gathered in one kernel from the
+    vocab shards at `shard_addrs` (device addresses, rank order)
+    (tb_b200_embedding_sharded_p2p)."""
+    torch = _torch()
+    _dev(ids)
+    if ids.dtype != torch.int32:
+        raise TypeError("ids must be int32")
+    if y is None:
+        y = torch.empty((ids.numel(), dim), dtype=dtype, device=ids.device)
+    _dev(y)
+    arr = (vp * len(shard_addrs))(*shard_addrs)
+    check(lib().tb_b200_embedding_sharded_p2p(dtype_code(y), ids.numel(), dim, vocab, ptr(ids),
+                                              arr, len(shard_addrs), ptr(y),
+                                              stream or cur_stream()), "embedding_sharded_p2p")
+    return y
 
 
 # ------------------------------------------------ decoder forward (runner)

@@ -90,6 +90,35 @@ def test_decoder_entry_points_check_arguments_before_device_work():
     assert L.tb_b200_sparse24_pack(4, 16, None, p, p, p, p, None) == 8
 
 
+def test_p2p_entry_points_check_arguments_before_device_work():
+    """The peer-memory gather and its IPC set-up reject bad arguments before
+    any CUDA call: TB_ERR_INVALID_ARG (8), TB_ERR_INVALID_SHAPE (9),
+    TB_ERR_UNSUPPORTED_DTYPE (10)."""
+    L = T.lib()
+    buf = (C.c_float * 64)()
+    p = C.cast(buf, C.c_void_p)
+    shards = (C.c_void_p * 8)(*([p.value] * 8))
+    off, out = C.c_int64(), C.c_void_p()
+    assert L.tb_b200_p2p_export(None, p, C.byref(off)) == 8
+    assert L.tb_b200_p2p_export(p, None, C.byref(off)) == 8
+    assert L.tb_b200_p2p_import(None, 0, C.byref(out)) == 8
+    assert L.tb_b200_p2p_import(p, -1, C.byref(out)) == 8
+    assert L.tb_b200_p2p_close(None, 0) == 8
+    assert L.tb_b200_p2p_close(p, -16) == 8
+    f = L.tb_b200_embedding_sharded_p2p
+    assert f(0, -1, 16, 100, p, shards, 2, p, None) == 9
+    assert f(4, 8, 16, 100, p, shards, 2, p, None) == 10     # int32 rows: not a table type
+    assert f(0, 8, 16, 100, p, shards, 0, p, None) == 8      # no ranks
+    assert f(0, 8, 16, 100, p, shards, 9, p, None) == 8      # more than 8 ranks
+    assert f(0, 8, 16, 1, p, shards, 2, p, None) == 8        # fewer rows than ranks
+    assert f(0, 8, 16, 100, None, shards, 2, p, None) == 8
+    assert f(0, 8, 16, 100, p, None, 2, p, None) == 8
+    assert f(0, 8, 16, 100, p, shards, 2, None, None) == 8
+    shards[1] = None
+    assert f(0, 8, 16, 100, p, shards, 2, p, None) == 8      # a missing shard
+    assert f(0, 0, 16, 100, None, None, 2, None, None) == 0  # no tokens: nothing to do
+
+
 def test_partition_rule():
     lo, hi = C.c_int64(), C.c_int64()
     for total, parts in [(16384, 8), (10, 3), (5, 8), (128256, 7)]:

@@ -7,8 +7,10 @@ send/recv in the order the NCCL path groups them; the assembled token part
 must equal the full-table gather (tb_cpu_embedding_f32,
 src/ops/embedding.c:4-14) -- the plan is consistent across processes.
 
-GPU (2 GPUs, skipped on fewer): the library's NCCL exchange itself,
-bit-exact against the oracle for f32 and bf16 tables.
+GPU (2 GPUs, skipped on fewer): the library's NCCL exchange itself, and
+the one-kernel gather over peer memory (tb_b200_embedding_sharded_p2p,
+shards mapped through CUDA IPC), both bit-exact against the oracle for f32
+and bf16 tables.
 """
 import os
 import socket
@@ -147,3 +149,67 @@ def test_sharded_embedding_nccl_two_gpus():
     assert len(res) == 2
     for rank, ok, err in res:
         assert ok, f"rank {rank}: {err or 'sharded gather differs from the full-table gather'}"
+
+
+def _p2p_rank(rank, world, port, n, vocab, dim, q):
+    """One kernel, no collective: this rank's rows read straight from the
+    owners' shards through CUDA IPC mappings (peer loads over NVLink)."""
+    import torch
+    import torch.distributed as dist
+    import tb_b200 as T
+    from oracle import oracle as O
+    try:
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=world)
+        ids, table = problem(n, vocab, dim, 98)
+        vlo, vhi = T.partition(vocab, world, rank)
+        tlo, thi = T.partition(n, world, rank)
+        oks = []
+        for host in (table, O.f32_to_bf16(table)):  # f32, then bf16 bits
+            shard = torch.from_numpy(np.ascontiguousarray(host[vlo:vhi]))
+            if host.dtype == np.uint16:
+                shard = shard.view(torch.int16).view(torch.bfloat16)
+            shard = shard.cuda()
+            handles = [None] * world
+            dist.all_gather_object(handles, T.p2p_export(shard))
+            addrs = [shard.data_ptr() if r == rank else T.p2p_import(*handles[r])
+                     for r in range(world)]
+            my_ids = torch.from_numpy(ids[tlo:thi].astype(np.int32)).cuda()
+            for _ in range(2):  # twice: the mappings stay valid
+                y = T.embedding_sharded_p2p(my_ids, addrs, vocab, dim, shard.dtype)
+                torch.cuda.synchronize()
+                got = y.cpu()
+                if host.dtype == np.uint16:
+                    got = got.view(torch.int16)
+                oks.append(np.array_equal(got.numpy().view(host.dtype),
+                                          O.embedding(ids[tlo:thi], host)))
+            oks.append(T.check_status() == (0, 0))
+            # ids outside [0, vocab): zero rows and the token-range flag, no read
+            bad = torch.tensor([-1, vocab, 0], dtype=torch.int32, device="cuda")
+            y = T.embedding_sharded_p2p(bad, addrs, vocab, dim, shard.dtype)
+            rc, flags = T.check_status()
+            got = y.cpu().view(torch.int16 if host.dtype == np.uint16 else torch.int32).numpy()
+            oks.append(rc != 0 and flags == 1 and not got[:2].any()
+                       and np.array_equal(got[2].view(host.dtype), host[0]))
+            for r in range(world):
+                if r != rank:
+                    T.p2p_close(addrs[r], handles[r][1])
+            dist.barrier()  # every importer closed before the owner frees its shard
+            del shard
+        dist.destroy_process_group()
+        q.put((rank, all(oks), "" if all(oks) else f"checks {oks}"))
+    except Exception as e:
+        q.put((rank, False, repr(e)))
+
+
+@pytest.mark.gpu
+def test_sharded_embedding_p2p_two_gpus():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    # an odd vocabulary: rank 0 holds one row more (the uneven partition rule)
+    res = run_ranks(_p2p_rank, 2, 4096, 32003, 4096)
+    assert len(res) == 2
+    for rank, ok, err in res:
+        assert ok, f"rank {rank}: {err or 'p2p gather differs from the full-table gather'}"
