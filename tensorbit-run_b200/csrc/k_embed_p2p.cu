@@ -29,6 +29,7 @@ namespace {
 
 constexpr int kMaxRanks = 8;
 constexpr int kThreads = 256;
+constexpr int kBatch = 4;
 
 struct Shards {
     const void* p[kMaxRanks];
@@ -62,7 +63,18 @@ k_embed_p2p(const int32_t* __restrict__ ids, int64_t n, int64_t vocab, int nrank
     int64_t lo;
     const int r = owner_of(id, vocab, nranks, lo);
     const W* s = static_cast<const W*>(sh.p[r]) + (id - lo) * words;
-    for (int64_t i = lane; i < words; i += 32) d[i] = s[i];
+    // kBatch loads in flight per lane before their stores.  Measured level
+    // with one at a time on 2 GPUs (0.1166 vs 0.1175 ms at 8192 rows of
+    // 16 KB): the gather is bound by NVLink read bandwidth, not latency.
+    int64_t i = lane;
+    for (; i + 32 * (kBatch - 1) < words; i += 32 * kBatch) {
+        W v[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) v[u] = s[i + 32 * u];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) d[i + 32 * u] = v[u];
+    }
+    for (; i < words; i += 32) d[i] = s[i];
 }
 
 using GetRange = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);

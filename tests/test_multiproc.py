@@ -204,12 +204,15 @@ def _p2p_rank(rank, world, port, n, vocab, dim, q):
 
 
 @pytest.mark.gpu
-def test_sharded_embedding_p2p_two_gpus():
+@pytest.mark.parametrize("n,vocab,dim", [(4096, 32003, 4096), (333, 1001, 1000), (333, 1001, 100)])
+def test_sharded_embedding_p2p_two_gpus(n, vocab, dim):
+    """Odd vocabularies (rank 0 holds one row more: the uneven partition
+    rule); rows of 16 KB, of 4000 / 2000 bytes (16-byte words, a ragged last
+    batch) and of 400 / 200 bytes (the bf16 rows move as 4-byte words)."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    # an odd vocabulary: rank 0 holds one row more (the uneven partition rule)
-    res = run_ranks(_p2p_rank, 2, 4096, 32003, 4096)
+    res = run_ranks(_p2p_rank, 2, n, vocab, dim)
     assert len(res) == 2
     for rank, ok, err in res:
         assert ok, f"rank {rank}: {err or 'p2p gather differs from the full-table gather'}"
