@@ -85,6 +85,15 @@ int tb_b200_check_status(void* stream, unsigned int* flags_out);
 #define TB_B200_FLAG_WAIT_TIMEOUT 0x2u  /* a kernel's bounded wait gave up (its output is invalid) */
 #define TB_B200_FLAG_POSITION_RANGE 0x4u /* decode attention: position outside [0, max_seq) */
 
+/* Runs, in a one-warp kernel, the bounded mbarrier wait the staged kernels
+ * use for their bulk copies.  supply != 0: one 16-byte copy completes the
+ * wait, no flag.  supply == 0: the wait expects bytes no copy brings and
+ * gives up after limit_us microseconds (1 .. 1000000, else
+ * TB_ERR_INVALID_ARG), raising TB_B200_FLAG_WAIT_TIMEOUT; the kernel returns
+ * and the context stays usable.  Read the outcome with
+ * tb_b200_check_status.  No counterpart in the reference. */
+int tb_b200_selftest_wait(int supply, uint32_t limit_us, void* stream);
+
 /* ======================================================================
  * Row kernels
  * ====================================================================== */
@@ -218,8 +227,13 @@ int tb_b200_embedding_host_ids(int dtype, int64_t n_tokens, int64_t dim, int64_t
  * first call on a device looks up the array's device address once (make it
  * before any stream capture on that device).  All calls share the array and
  * each starts by clearing the status word: calls whose work can overlap on
- * the GPU (different streams, no ordering between them) race on it.  No
- * counterpart in the reference (its embedding is a host memcpy). */
+ * the GPU (different streams, no ordering between them) race on it.  The ids
+ * are copied from ids_host on `stream`: from pageable memory the copy has
+ * taken them when the call returns; from page-locked memory it reads them
+ * when the stream reaches it, so the caller must not overwrite them before
+ * then.  The array's device address is cached per device for the life of
+ * the process; the library assumes no cudaDeviceReset while it is loaded.
+ * No counterpart in the reference (its embedding is a host memcpy). */
 #define TB_B200_STATIC_MAX_TOKENS 65536
 int tb_b200_embedding_host_ids_static(int dtype, int64_t n_tokens, int64_t dim, int64_t vocab,
                                       const int32_t* ids_host, const void* table, void* y,
@@ -415,6 +429,17 @@ int tb_b200_comm_init(int nranks, int rank, const void* unique_id, int device);
 int tb_b200_comm_destroy(void);
 int tb_b200_comm_info(int* rank, int* nranks);
 
+/* Bounded wait for the work queued on `stream` so far -- the exchanges of
+ * tb_b200_embedding_sharded among it.  Polls the stream and the
+ * communicator's error state every few microseconds.  TB_OK once the work
+ * is done.  If the communicator reports an error, or the work is not done
+ * after TB_B200_COMM_TIMEOUT_S seconds (environment, default 120; a peer
+ * that never posts its side of an exchange), the communicator is aborted
+ * (its kernels still waiting for peers end, with their output invalid),
+ * released, and TB_ERR_DEVICE is returned; tb_b200_comm_init may then make
+ * a new one.  The reference has no communication layer: no counterpart. */
+int tb_b200_comm_wait(void* stream);
+
 /* Vocab-sharded embedding gather over the communicator.  Every rank holds
  * the same n_tokens ids (host int32), the table rows of its vocab part
  * (tb_b200_partition(vocab, nranks, rank)) in table_shard, and receives the
@@ -422,7 +447,10 @@ int tb_b200_comm_info(int* rank, int* nranks);
  * y_local.  Owned rows are copied locally; the rest arrive from their
  * owners through one grouped NCCL send/recv exchange.  Bit-exact with
  * tb_cpu_embedding_f32 over the full table.  Ids outside [0, vocab) return
- * TB_ERR_INVALID_ARG before any work is queued. */
+ * TB_ERR_INVALID_ARG before any work is queued.  Returns once the exchange
+ * is queued on `stream` (that host-side enqueue is bounded by
+ * TB_B200_COMM_TIMEOUT_S); the exchange runs asynchronously, and
+ * tb_b200_comm_wait bounds the wait for it. */
 int tb_b200_embedding_sharded(int dtype, int64_t n_tokens, int64_t dim, int64_t vocab,
                               const int32_t* ids_host, const void* table_shard, void* y_local,
                               void* stream);

@@ -14,10 +14,14 @@
 //      send/recv (NVLink/NVSwitch), only rows that are needed;
 //   4. scatters the received rows into its output (one kernel).
 // Every step is a byte copy, so the result is bit-exact with the
-// full-table gather.  The communicator is created non-blocking and every
-// wait on it is bounded (TB_B200_COMM_TIMEOUT_S seconds, default 120): a
-// rank that never arrives makes the others return TB_ERR_DEVICE after
-// aborting the communicator, instead of hanging.
+// full-table gather.  The communicator is created non-blocking, and every
+// host-side wait on it is bounded (TB_B200_COMM_TIMEOUT_S seconds, default
+// 120): creation, and the enqueue of the grouped exchange.  The exchange
+// itself runs later on the stream, where an NCCL kernel waits for its peers;
+// tb_b200_comm_wait bounds that wait too: it polls the stream's progress and
+// the communicator's error state, and on timeout aborts the communicator
+// (which ends its kernels) and returns TB_ERR_DEVICE.  A rank that never
+// arrives thus makes the others fail instead of hanging.
 //
 // NCCL is not linked: its entry points are resolved with dlopen/dlsym on
 // first use.  A process that also loads PyTorch then shares torch's NCCL
@@ -277,6 +281,62 @@ int tb_b200_comm_destroy(void) {
     g_comm = nullptr;
     g_rank = 0;
     g_nranks = 0;
+    return rc;
+}
+
+int tb_b200_comm_wait(void* stream) {
+    if (!g_comm) {
+        tbh::set_error_text("tb_b200_comm_wait: no communicator (tb_b200_comm_init)");
+        return TB_ERR_INVALID_ARG;
+    }
+    cudaStream_t s = tbh::stream_of(stream);
+    cudaEvent_t ev = nullptr;
+    TB_CUDA_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    cudaError_t e = cudaEventRecord(ev, s);
+    if (e != cudaSuccess) {
+        cudaEventDestroy(ev);
+        tbh::set_error("tb_b200_comm_wait: event record", e);
+        return TB_ERR_DEVICE;
+    }
+    const double limit = timeout_s();
+    const auto t0 = std::chrono::steady_clock::now();
+    auto elapsed = [&]() {
+        return std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    };
+    int rc = TB_OK;
+    for (;;) {
+        e = cudaEventQuery(ev);
+        if (e == cudaSuccess) break;
+        if (e != cudaErrorNotReady) {
+            tbh::set_error("tb_b200_comm_wait", e);
+            rc = TB_ERR_DEVICE;
+            break;
+        }
+        ncclResult_t st = ncclSuccess;
+        const ncclResult_t r = g_nccl.CommGetAsyncError(g_comm, &st);
+        const bool failed = r != ncclSuccess || (st != ncclSuccess && st != ncclInProgress);
+        if (failed || elapsed() > limit) {
+            if (failed)
+                nccl_error("tb_b200_comm_wait", r != ncclSuccess ? r : st);
+            else
+                tbh::set_error_text("tb_b200_comm_wait: exchange timed out; communicator aborted");
+            // Aborting ends the communicator's kernels still waiting for
+            // peers, so the stream drains; wait for that, bounded again.
+            g_nccl.CommAbort(g_comm);
+            g_comm = nullptr;
+            g_rank = 0;
+            g_nranks = 0;
+            const auto t1 = std::chrono::steady_clock::now();
+            while (cudaEventQuery(ev) == cudaErrorNotReady &&
+                   std::chrono::duration<double>(std::chrono::steady_clock::now() - t1).count() <
+                       limit)
+                std::this_thread::sleep_for(std::chrono::microseconds(200));
+            rc = TB_ERR_DEVICE;
+            break;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+    cudaEventDestroy(ev);
     return rc;
 }
 

@@ -368,7 +368,11 @@ int tbh::decode_attention_launch(int mode, int n_heads, int n_kv_heads, int head
         if (rc != TB_OK) return rc;
     }
     const float scale = 1.f / sqrtf((float)head_dim);  // ops.hpp:175
-    const bool vec = head_dim % 4 == 0 && tbh::aligned16(k) && tbh::aligned16(k_cache);
+    // The float4 path reads k, v and both caches as float4 (the new token's
+    // k and v too): every one of them must start on a 16-byte boundary --
+    // slices of a packed qkv buffer may not.
+    const bool vec = head_dim % 4 == 0 && tbh::aligned16(k) && tbh::aligned16(k_cache) &&
+                     tbh::aligned16(v) && tbh::aligned16(v_cache);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)n_heads, (unsigned)splits);
     cfg.blockDim = dim3(kT);

@@ -553,6 +553,15 @@ int create(const TbB200RunnerDesc* d, Runner* r) {
                         ? tbh::decode_attention_splits(c.n_heads, c.max_seq)
                         : 1;  // the reference's rows attend at most n_heads keys
     if (r->att_splits > 1) {
+        // One partials buffer and one set of arrival counters serve every
+        // layer's attention launch.  That is safe only while consecutive
+        // attention launches are fully ordered: every kernel between two of
+        // them (o-projection, gate/up, down, the next layer's QKV) executes
+        // griddepcontrol.wait before its first memory access, so under
+        // programmatic dependent launch a layer's attention cannot start
+        // before the previous layer's has finished and reset its counters.
+        // A kernel added to the step without that wait would let two
+        // attention launches overlap on these buffers.
         if ((rc = dev_alloc(r, (size_t)c.n_heads * r->att_splits * (c.head_dim + 2) * f, &p)))
             return rc;
         r->att_part = (float*)p;

@@ -21,6 +21,7 @@ LIB_PATH = os.path.join(HERE, "lib", "libtb_b200.so")
 F32, F16, BF16, I32 = 0, 1, 2, 4
 DEVICE_CPU, DEVICE_CUDA = 0, 1
 FLAG_TOKEN_RANGE = 0x1
+FLAG_WAIT_TIMEOUT = 0x2
 
 # TbOpType values (include/tb_backend.h)
 OP = dict(SPARSE_LINEAR=0, DENSE_LINEAR=1, RMS_NORM=2, LAYER_NORM=3, GELU=4, SILU=5, SOFTMAX=6,
@@ -153,6 +154,8 @@ SIGNATURES = {
     "tb_b200_comm_init": (i32, [i32, i32, vp, i32]),
     "tb_b200_comm_destroy": (i32, []),
     "tb_b200_comm_info": (i32, [P(i32), P(i32)]),
+    "tb_b200_comm_wait": (i32, [vp]),
+    "tb_b200_selftest_wait": (i32, [i32, C.c_uint32, vp]),
     "tb_b200_embedding_sharded": (i32, [i32, i64, i64, i64, vp, vp, vp, vp]),
     "tb_b200_embedding_sharded_p2p": (i32, [i32, i64, i64, i64, vp, P(vp), i32, vp, vp]),
     "tb_b200_p2p_export": (i32, [vp, vp, P(i64)]),
@@ -520,6 +523,20 @@ def comm_init(nranks: int, rank: int, unique_id: bytes, device: int) -> None:
 
 def comm_destroy() -> None:
     check(lib().tb_b200_comm_destroy(), "comm_destroy")
+
+
+def comm_wait(stream=None) -> int:
+    """Bounded wait for the stream's queued work, exchanges included
+    (tb_b200_comm_wait): TB_OK, or TB_ERR_DEVICE after aborting the
+    communicator on an error or a timeout.  Returns the code."""
+    return lib().tb_b200_comm_wait(stream or cur_stream())
+
+
+def comm_info():
+    """(rank, nranks) of this process's communicator; (0, 0) without one."""
+    rank, nranks = C.c_int(), C.c_int()
+    check(lib().tb_b200_comm_info(C.byref(rank), C.byref(nranks)), "comm_info")
+    return rank.value, nranks.value
 
 
 def embedding_sharded(ids_host, table_shard, vocab: int, y_local=None, stream=None):

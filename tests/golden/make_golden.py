@@ -11,6 +11,9 @@ sampled rows.  Inputs are regenerated from the seeds in workloads.py, so only
 outputs are stored.
 
     python tests/golden/make_golden.py [REF_ROOT]
+
+REF_ROOT defaults to $TB_REFERENCE_ROOT, else a checkout named `reference`
+beside this repository.
 """
 from __future__ import annotations
 
@@ -82,7 +85,9 @@ def cases():
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref_root = (sys.argv[1] if len(sys.argv) > 1 else
+                os.environ.get("TB_REFERENCE_ROOT",
+                               os.path.join(os.path.dirname(ROOT), "reference")))
     subprocess.run(["make", "-C", os.path.join(ROOT, "oracle"), "all", f"REF_ROOT={ref_root}"],
                    check=True, capture_output=True)
     O.lib()

@@ -191,6 +191,42 @@ def test_decode_attention_kernel(dev, mode, heads, kv, d, pos):
     assert np.array_equal(g["vc"][pos].cpu().numpy(), v)
 
 
+@pytest.mark.parametrize("which", ["v", "v_cache", "k"])
+def test_decode_attention_unaligned_operand(dev, which):
+    """k, v and the caches are read as float4 only when every one of them is
+    16-byte aligned: a slice of a packed buffer one float off (for example v
+    inside a fused qkv vector) takes the scalar path and gives the same
+    attention as aligned copies of the same values."""
+    import torch
+    rng = np.random.default_rng(43)
+    heads, kv, d, pos = 8, 2, 64, 37
+    max_seq, kvd = 64, kv * d
+    vals = {n: rng.standard_normal(s).astype(np.float32)
+            for n, s in dict(q=heads * d, k=kvd, v=kvd, k_cache=max_seq * kvd,
+                             v_cache=max_seq * kvd).items()}
+
+    def run(off):
+        g = {}
+        for n, a in vals.items():
+            pad = 1 if n == off else 0
+            buf = torch.zeros(a.size + pad, dtype=torch.float32, device=dev)
+            buf[pad:] = torch.from_numpy(a).to(dev)
+            g[n] = buf[pad:]
+        g["k_cache"] = g["k_cache"].view(max_seq, kvd)
+        g["v_cache"] = g["v_cache"].view(max_seq, kvd)
+        p = torch.tensor([pos], dtype=torch.int32, device=dev)
+        out = T.decode_attention(g["q"], g["k"], g["v"], g["k_cache"], g["v_cache"], p, heads, kv,
+                                 T.ATTN_STANDARD)
+        torch.cuda.synchronize()
+        return out.cpu().numpy(), g
+
+    want, _ = run(None)
+    got, g = run(which)
+    assert T.check_status() == (0, 0)
+    np.testing.assert_allclose(got, want, rtol=0, atol=2e-6 * np.abs(want).max())
+    assert np.array_equal(g["v_cache"][pos].cpu().numpy(), vals["v"])
+
+
 @pytest.mark.parametrize("inter,masks", [(16384, "rand"), (8192, "none"), (8192, "rand")])
 def test_rows_split_over_warps(dev, inter, masks):
     """Few output rows with long rows (a down projection of 128 rows over
