@@ -1,23 +1,30 @@
 #!/usr/bin/env python
 """Benchmark of the B200 row-op hot path (libtb_b200.so), one JSON line.
 
-Workload: one pass of the per-token row ops of a Llama-7B-shape prefill of
-4096 tokens -- the reference engine's layer ops batched over rows:
-  embedding gather          ids [4096] -> rows of a [32000, 4096] table
-  residual + RMSNorm        [4096, 4096]                    } one fused
-  RoPE on Q and K           [4096, 32, 128] x 2, pos 0..4095 } layer-chain
-  SwiGLU silu(gate)*up      [4096, 11008]                    } launch
-  row softmax               logits [4096, 32000] f32
-  greedy argmax             logits [4096, 32000] f32 (own buffer)
-Activations bf16 (f32 arithmetic), logits f32; synthetic seeded inputs with
-the reference config's distributions.  Every op reads distinct buffers and a
-step moves ~2.2 GB, far more than the 126 MB L2, so nothing is served from
-L2 across steps.
+Default workload (--config 70b): one pass of the per-token row ops of a
+Llama-3-70B-shape prefill of 16384 tokens (8 sequences x 2048), strong-
+scaled: the token rows, the logit rows and the embedding table's vocabulary
+rows are split over the N ranks (tb_b200_partition).
+  embedding gather          16384 ids -> rows of a [128256, 8192] bf16 table,
+                            vocab-sharded: each rank holds 128256/N table
+                            rows and gathers its token part with the NCCL
+                            exchange (tb_b200_embedding_sharded); the one-
+                            kernel peer-memory gather (..._sharded_p2p) is
+                            timed beside the step
+  residual + RMSNorm        [16384/N, 8192]                   } one fused
+  RoPE on Q and K           [16384/N, 64 | 8, 128], pos % 2048 } layer-chain
+  SwiGLU silu(gate)*up      [16384/N, 28672]                   } launch
+  row softmax               logits [4096/N, 128256] f32
+  greedy argmax             logits [4096/N, 128256] f32 (own buffer)
+--config 7b is the Llama-7B prefill of 4096 tokens (embedding from a
+[32000, 4096] table, chain, softmax/argmax over [4096, 32000]) run whole on
+every rank (weak scaling).  Activations bf16 (f32 arithmetic), logits f32;
+synthetic seeded inputs with the reference configs' distributions.  Every
+op reads distinct buffers and a step moves GBs, far more than the 126 MB L2.
 
 metric: algorithmic HBM bytes of the step (each input read once, each
-output written once) / device time, in GB/s, over all ranks; rows/s beside
-it.  --gpus N (torchrun) runs the same per-GPU workload on every rank (weak
-scaling, no collective in the data path) and takes the max time over ranks.
+output written once) over all ranks / device time (max over ranks), in
+GB/s; rows/s beside it.
 
 --impl reference times the reference's own CPU kernels (oracle/_ref, the
 reference's src/ops/*.c) on the host's cores over a bounded row sample of
@@ -48,8 +55,14 @@ import workloads as W  # noqa: E402
 CONFIGS = {
     "7b": (W.CONFIGS["7b"], None, "llama7b-prefill-4096 row ops (embedding, residual+RMSNorm, "
                                   "RoPE, SwiGLU, softmax, argmax)"),
-    "70b": (W.CONFIGS["70b"], 4096, "llama70b-prefill-16384 layer ops (embedding, residual+RMSNorm, "
-                                    "RoPE, SwiGLU) + softmax/argmax over 4096 x 128256 logits"),
+    "70b": (W.CONFIGS["70b"], 4096, "llama70b-prefill-16384 (8 x 2048) row ops strong-scaled "
+                                    "over the ranks: vocab-sharded 128256 x 8192 embedding "
+                                    "gather (NCCL exchange), residual+RMSNorm, RoPE, SwiGLU, "
+                                    "softmax/argmax over 4096 x 128256 logits"),
+    "sweep": (W.CONFIGS["7b"], None, "bandwidth sweep: residual+RMSNorm and SwiGLU over rows "
+                                     "2^10..2^20 x hidden {2048, 4096, 8192, 16384} in f32 and "
+                                     "bf16; softmax and argmax over rows {1, 16, 256, 4096} x "
+                                     "128256 f32 logits; rows split over the ranks"),
     "decode": (W.CONFIGS["decode"], None, "decode 256 sequences x 1 token at the llama7b shape: the "
                                           "fused layer chain (residual+RMSNorm, RoPE, SwiGLU) over "
                                           "32 layers, one CUDA graph"),
@@ -66,7 +79,10 @@ RUNNER_MAX_SEQ = 2048
 RUNNER_CONTEXT = 1024  # tokens fed (untimed) before the timed ones: decode at context 1024+
 RUNNER_METRIC = "decode tokens/s"
 DECODE_LAYERS = 32
-CFG, LOGIT_ROWS, WORKLOAD = CONFIGS["7b"]
+DEFAULT_CONFIG = "70b"
+CFG, LOGIT_ROWS, WORKLOAD = CONFIGS[DEFAULT_CONFIG]
+SEQ_LEN_70B = 2048  # the 70b prefill's 16384 tokens are 8 sequences of 2048
+TABLE_CHUNK = 4096  # embedding-table rows drawn per seed (rank-count independent)
 E2E_BLOCKS = 8    # row blocks of the end-to-end step
 E2E_STREAMS = 3   # streams they are spread over
 METRIC = "fused layer-op HBM GB/s"
@@ -78,19 +94,25 @@ def logit_rows(rows):
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per row of each
-# kernel, from one ncu capture each (profiles/*.md), for roofline.traffic.
-# Writes still dirty in L2 when a kernel ends are not in the write count.
+# kernel, from one ncu capture of that kernel at the config's row shape, for
+# roofline.traffic.  Writes still dirty in L2 when a kernel ends are not in
+# the write count.
 TRAFFIC_PER_ROW = {
-    "embedding": (32137856 / 4096, "profiles/k_embed_llama7b-prefill-4096.md"),
-    "layer_chain": (485573888 / 4096, "profiles/k_chain_llama7b-prefill-4096.md"),
-    "softmax": ((192851456 + 74482944) / 1024, "profiles/k_softmax_staged_logits-1024x32000.md"),
-    "argmax": (530358016 / 4096, "profiles/k_argmax_llama7b-prefill-4096.md"),
+    "7b": {
+        "embedding": 32137856 / 4096,
+        "layer_chain": 485573888 / 4096,
+        "softmax": (192851456 + 74482944) / 1024,
+        "argmax": 530358016 / 4096,
+    },
+    "70b": {},
 }
+TRAFFIC_SOURCE = "ncu capture of the kernel (DRAM bytes read + written per row, scaled to the " \
+                 "launch's rows)"
 
 
-def step_bytes(rows, act_s):
+def step_bytes(rows, act_s, lr=None):
     c = CFG
-    lr = logit_rows(rows)
+    lr = logit_rows(rows) if lr is None else lr
     parts = {
         "embedding": W.bytes_embedding(rows, c.hidden, act_s),
         "layer_chain": (W.bytes_res_rms(rows, c.hidden, act_s)
@@ -440,10 +462,9 @@ def run_decode(args, rank, world, local):
         "roofline": {"bound": "hbm", "kernel": "layer_chain", "achieved": round(achieved, 1),
                      "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
                      "frac": round(achieved / peak, 3),
-                     "traffic": round(TRAFFIC_PER_ROW["layer_chain"][0] * R),
+                     "traffic": round(TRAFFIC_PER_ROW["7b"]["layer_chain"] * R),
                      "algorithmic_bytes": lb,
-                     "traffic_source": TRAFFIC_PER_ROW["layer_chain"][1]
-                                       + " (ncu, same row shape, scaled to the launch's rows)",
+                     "traffic_source": TRAFFIC_SOURCE + "; captured at the same row shape",
                      "duration": "graph step time / layers (launch gaps included)"},
         "e2e": {"value": round(total / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": bi,
@@ -896,11 +917,10 @@ def run_gpu(args, rank, world, local):
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1),
                      "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
                      "frac": round(achieved / peak, 3),
-                     "traffic": (round(TRAFFIC_PER_ROW[dom][0] * (LR if dom in ("softmax", "argmax") else R))
+                     "traffic": (round(TRAFFIC_PER_ROW["7b"][dom] * (LR if dom in ("softmax", "argmax") else R))
                                  if CFG is CONFIGS["7b"][0] else None),
                      "algorithmic_bytes": parts[dom],
-                     "traffic_source": (TRAFFIC_PER_ROW[dom][1] + " (ncu, scaled to the launch's rows)"
-                                        if CFG is CONFIGS["7b"][0] else
+                     "traffic_source": (TRAFFIC_SOURCE if CFG is CONFIGS["7b"][0] else
                                         "no ncu capture of this configuration")},
         "e2e": {"value": round(total_bytes / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": bi,
@@ -913,6 +933,499 @@ def run_gpu(args, rank, world, local):
     return line
 
 
+# ----------------------------------------------- 70b prefill, strong-scaled
+def table_shard(torch, dev, c, lo, hi, seed):
+    """Rows [lo, hi) of the [vocab, hidden] bf16 embedding table ~N(0, 0.02).
+    The table is drawn TABLE_CHUNK rows at a time, chunk j from seed + j, so
+    a rank's shard is a slice of the same table whatever the rank count."""
+    out = torch.empty((hi - lo, c.hidden), dtype=torch.bfloat16, device=dev)
+    g = torch.Generator(device=dev)
+    if hi <= lo:
+        return out
+    for j in range(lo // TABLE_CHUNK, (hi - 1) // TABLE_CHUNK + 1):
+        a, b = j * TABLE_CHUNK, min((j + 1) * TABLE_CHUNK, c.vocab)
+        g.manual_seed(seed + j)
+        blk = (torch.randn((b - a, c.hidden), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        lo2, hi2 = max(a, lo), min(b, hi)
+        out[lo2 - lo:hi2 - lo] = blk[lo2 - a:hi2 - a]
+    return out
+
+
+def run_sharded(args, rank, world, local):
+    """The 70b step strong-scaled over `world` ranks: rank r takes token
+    rows tb_b200_partition(16384, world, r), logit rows
+    tb_b200_partition(4096, world, r) and table rows
+    tb_b200_partition(128256, world, r).  The embedding gather is the
+    library's NCCL exchange over its own communicator (one grouped
+    send/recv per step); every other op is local to the rank."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import tb_b200 as T
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    L = T.lib()
+    c = CFG
+    NT, NLG = args.rows, LOGIT_ROWS
+    tlo, thi = T.partition(NT, world, rank)
+    llo, lhi = T.partition(NLG, world, rank)
+    vlo, vhi = T.partition(c.vocab, world, rank)
+    R, LR = thi - tlo, lhi - llo
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v, op=None):
+        if world == 1:
+            return v
+        x = torch.tensor([float(v)], dtype=torch.float64, device=dev)
+        dist.all_reduce(x, op=op or dist.ReduceOp.MAX)
+        return float(x.item())
+
+    # the library's NCCL communicator over the same ranks
+    if world > 1:
+        uid = [T.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        uid = uid[0]
+    else:
+        uid = T.comm_unique_id()
+    T.comm_init(world, rank, uid, local)
+
+    ids = np.random.default_rng(c.seed + 8).integers(0, c.vocab, NT).astype(np.int32)
+    table_seed = c.seed + 700
+    shard = table_shard(torch, dev, c, vlo, vhi, table_seed)
+    g = torch.Generator(device=dev)
+    base = 12345 + 1000 * rank
+
+    def randn(shape, std=1.0, mean=0.0, dtype=torch.bfloat16, k=0):
+        g.manual_seed(base + k)
+        return (torch.randn(shape, generator=g, device=dev) * std + mean).to(dtype)
+
+    t = {
+        "x": randn((R, c.hidden), k=0), "res": randn((R, c.hidden), k=1),
+        "gamma": randn((c.hidden,), 0.1, 1.0, k=2),
+        "q": randn((R, c.n_q_heads, c.head_dim), k=3),
+        "k": randn((R, c.n_kv_heads, c.head_dim), k=4),
+        "gate": randn((R, c.intermediate), k=5), "up": randn((R, c.intermediate), k=6),
+        "pos": (torch.arange(tlo, thi, dtype=torch.int32, device=dev) % SEQ_LEN_70B),
+        "logits_s": randn((LR, c.vocab), c.logit_std, dtype=torch.float32, k=9),
+        "logits_a": randn((LR, c.vocab), c.logit_std, dtype=torch.float32, k=10),
+    }
+    o = {
+        "emb": torch.empty((R, c.hidden), dtype=torch.bfloat16, device=dev),
+        "h": torch.empty_like(t["x"]), "y": torch.empty_like(t["x"]),
+        "act": torch.empty_like(t["gate"]), "probs": torch.empty_like(t["logits_s"]),
+        "tok": torch.empty(LR, dtype=torch.int32, device=dev),
+    }
+    rope = T.rope_table(c.theta, c.head_dim, SEQ_LEN_70B)
+    stream = torch.cuda.current_stream()
+    sp = C.c_void_p(stream.cuda_stream)
+    chain = T.make_chain(t["x"], t["res"], t["gamma"], o["h"], o["y"], c.eps, t["q"], t["k"],
+                         t["pos"], c.theta, rope, t["gate"], t["up"], o["act"])
+    ids_p = ids.ctypes.data
+    ops = {
+        "embedding": lambda: T.check(L.tb_b200_embedding_sharded(
+            T.BF16, NT, c.hidden, c.vocab, ids_p, T.ptr(shard), T.ptr(o["emb"]), sp),
+            "embedding_sharded"),
+        "layer_chain": lambda: T.check(L.tb_b200_layer_chain(C.byref(chain), sp), "layer_chain"),
+        "softmax": lambda: T.check(L.tb_b200_softmax(T.F32, LR, c.vocab, T.ptr(t["logits_s"]),
+                                                     None, T.ptr(o["probs"]), sp), "softmax"),
+        "argmax": lambda: T.check(L.tb_b200_argmax(T.F32, LR, c.vocab, T.ptr(t["logits_a"]),
+                                                   T.ptr(o["tok"]), sp), "argmax"),
+    }
+
+    def step():
+        for f in ops.values():
+            f()
+
+    if args.profile_op:
+        for _ in range(args.warmup + args.steps):
+            ops[args.profile_op]()
+        torch.cuda.synchronize()
+        T.comm_destroy()
+        return None
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = L.tb_b200_launch_count()
+    uuid = getattr(torch.cuda.get_device_properties(dev), "uuid", None)
+    uuid = f"GPU-{uuid}" if uuid is not None else None
+    with ClockSampler(local, uuid) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        e1.synchronize()
+    launches = L.tb_b200_launch_count() - l0
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+
+    # per-op device time inside full steps (for the roofline and the shares)
+    names = list(ops)
+    evs = {n: [] for n in names}
+    for _ in range(max(3, min(args.steps, 20))):
+        for n in names:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            ops[n]()
+            b.record(stream)
+            evs[n].append((a, b))
+    torch.cuda.synchronize()
+    per_op_ms = {n: max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in evs[n]))
+                 for n in names}
+    barrier()
+
+    # the same gather as one kernel over peer memory (no collective), timed
+    # alone: this rank's rows read straight from the owners' shards
+    if world > 1:
+        handles = [None] * world
+        dist.all_gather_object(handles, T.p2p_export(shard))
+        addrs = [shard.data_ptr() if r == rank else T.p2p_import(*handles[r])
+                 for r in range(world)]
+    else:
+        handles, addrs = None, [shard.data_ptr()]
+    my_ids = torch.from_numpy(ids[tlo:thi]).to(dev)
+    y_p2p = torch.empty_like(o["emb"])
+    darr = (C.c_void_p * world)(*addrs)
+
+    def p2p():
+        T.check(L.tb_b200_embedding_sharded_p2p(T.BF16, R, c.hidden, c.vocab, T.ptr(my_ids), darr,
+                                                world, T.ptr(y_p2p), sp), "embedding_sharded_p2p")
+
+    for _ in range(3):
+        p2p()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    n_p2p = max(5, min(args.steps, 20))
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(n_p2p):
+        p2p()
+    b.record(stream)
+    b.synchronize()
+    p2p_ms = max_over_ranks(a.elapsed_time(b)) / n_p2p
+    # both gathers against each other and against the table itself: a sample
+    # of token rows regenerated from their chunk's seed
+    ops["embedding"]()
+    torch.cuda.synchronize()
+    same = bool(torch.equal(o["emb"].view(torch.int16), y_p2p.view(torch.int16)))
+    rs = np.random.default_rng(11 + rank)
+    sample = sorted(set(rs.integers(0, R, 8).tolist()) | {0, R - 1}) if R else []
+    by_chunk = {}
+    for r_ in sample:
+        by_chunk.setdefault(int(ids[tlo + r_]) // TABLE_CHUNK, []).append(r_)
+    for j, rows_ in by_chunk.items():
+        lo_, hi_ = j * TABLE_CHUNK, min((j + 1) * TABLE_CHUNK, c.vocab)
+        chunk = table_shard(torch, dev, c, lo_, hi_, table_seed)
+        for r_ in rows_:
+            same = same and bool(torch.equal(o["emb"][r_].view(torch.int16),
+                                             chunk[int(ids[tlo + r_]) - lo_].view(torch.int16)))
+        del chunk
+    verified = max_over_ranks(0.0 if same else 1.0) == 0.0
+    if world > 1:
+        torch.cuda.synchronize()
+        for r in range(world):
+            if r != rank:
+                T.p2p_close(addrs[r], handles[r][1])
+        barrier()  # every importer closed before an owner may free its shard
+    owner = np.searchsorted(np.array([T.partition(c.vocab, world, r)[1] for r in range(world)]),
+                            ids[tlo:thi], side="right")
+    n_remote = int((owner != rank).sum())
+    nvlink_bytes = max_over_ranks(n_remote * c.hidden * 2)
+
+    # End to end through the C ABI: pinned host inputs in, outputs back out,
+    # every step.  The gather takes its host ids as the engine passes them;
+    # the other ops run as row blocks spread over streams, each block copying
+    # its own inputs in and its outputs out, so copies overlap kernels.
+    ins = ["x", "res", "q", "k", "gate", "up", "logits_s", "logits_a"]
+    outs = ["emb", "h", "y", "q", "k", "act", "probs", "tok"]
+    host_in = {n: torch.empty_like(t[n], device="cpu").pin_memory() for n in ins}
+    for n in ins:
+        host_in[n].copy_(t[n])
+    host_out = {n: torch.empty_like((o.get(n) if n in o else t[n]), device="cpu").pin_memory()
+                for n in outs}
+    bi = sum(host_in[n].numel() * host_in[n].element_size() for n in ins) + ids.nbytes
+    bo = sum(host_out[n].numel() * host_out[n].element_size() for n in outs)
+    nb = E2E_BLOCKS if R % E2E_BLOCKS == 0 and LR % E2E_BLOCKS == 0 else 1
+    rb, lrb = R // nb, LR // nb
+    logit_names = {"logits_s", "logits_a", "probs", "tok"}
+    streams = [torch.cuda.Stream(device=dev) for _ in range(E2E_STREAMS)]
+
+    def dev_of(n):
+        return o[n] if n in o else t[n]
+
+    blocks = []
+    for j in range(nb):
+        span = {n: ((j * lrb, (j + 1) * lrb) if n in logit_names else (j * rb, (j + 1) * rb))
+                for n in set(ins) | set(outs)}
+        sl = {n: dev_of(n)[a_:b_] for n, (a_, b_) in span.items()}
+        sl["pos"] = t["pos"][j * rb:(j + 1) * rb]
+        ch = T.make_chain(sl["x"], sl["res"], t["gamma"], sl["h"], sl["y"], c.eps, sl["q"],
+                          sl["k"], sl["pos"], c.theta, rope, sl["gate"], sl["up"], sl["act"])
+        blocks.append((span, sl, ch))
+
+    def e2e_step():
+        main = torch.cuda.current_stream()
+        for st in streams:
+            st.wait_stream(main)
+        ops["embedding"]()  # host ids in, on the main stream
+        gathered = torch.cuda.Event()
+        gathered.record(main)
+        for j, (span, sl, ch) in enumerate(blocks):
+            st = streams[j % len(streams)]
+            ss = C.c_void_p(st.cuda_stream)
+            for n in ins:
+                hb = host_in[n][span[n][0]:span[n][1]]
+                T.check(L.tb_b200_memcpy_h2d(T.ptr(sl[n]), C.c_void_p(hb.data_ptr()),
+                                             hb.numel() * hb.element_size(), ss), "h2d")
+            T.check(L.tb_b200_layer_chain(C.byref(ch), ss), "layer_chain")
+            T.check(L.tb_b200_softmax(T.F32, lrb, c.vocab, T.ptr(sl["logits_s"]), None,
+                                      T.ptr(sl["probs"]), ss), "softmax")
+            T.check(L.tb_b200_argmax(T.F32, lrb, c.vocab, T.ptr(sl["logits_a"]),
+                                     T.ptr(sl["tok"]), ss), "argmax")
+            st.wait_event(gathered)
+            for n in outs:
+                hb = host_out[n][span[n][0]:span[n][1]]
+                T.check(L.tb_b200_memcpy_d2h(C.c_void_p(hb.data_ptr()), T.ptr(sl[n]),
+                                             hb.numel() * hb.element_size(), ss), "d2h")
+        for st in streams:
+            main.wait_stream(st)
+
+    e2e_steps = max(3, min(args.steps, 5))
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    b.record(stream)
+    b.synchronize()
+    e2e_ms = max_over_ranks(a.elapsed_time(b)) / e2e_steps
+    barrier()
+    T.comm_destroy()
+
+    parts = step_bytes(NT, 2, NLG)  # the whole job's algorithmic bytes
+    total_bytes = sum(parts.values())
+    mine = step_bytes(R, 2, LR)    # this rank's share
+    peak, peak_kind = peaks()
+    dom = max(per_op_ms, key=per_op_ms.get)
+    achieved = mine[dom] / (per_op_ms[dom] / 1e3) / 1e9
+    step_sum = sum(per_op_ms.values())
+    per_op = {n: {"ms": round(per_op_ms[n], 4), "GB/s": round(mine[n] / per_op_ms[n] / 1e6, 1),
+                  "frac": round(mine[n] / per_op_ms[n] / 1e6 / peak, 3), "bytes": mine[n],
+                  "share": round(per_op_ms[n] / step_sum, 3)} for n in names}
+    traffic = TRAFFIC_PER_ROW["70b"].get(dom)
+    line = {
+        "metric": METRIC, "value": round(total_bytes / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded, reference config distributions)",
+        "config": {"workload": WORKLOAD, "tokens": NT, "seq_len": SEQ_LEN_70B,
+                   "rows_per_gpu": R, "logit_rows_per_gpu": LR, "hidden": c.hidden,
+                   "heads": [c.n_q_heads, c.n_kv_heads, c.head_dim],
+                   "intermediate": c.intermediate, "vocab": c.vocab,
+                   "table_rows_per_gpu": vhi - vlo, "activations": "bf16 (f32 arithmetic)",
+                   "logits": "f32", "bytes_per_step": total_bytes,
+                   "l2": f"inputs larger than L2: {sum(mine.values()) / 1e9:.2f} GB of distinct "
+                         "buffers per step per GPU",
+                   "parallelism": f"rows and vocab sharded x{world}; NCCL exchange in the "
+                                  "embedding gather only"},
+        "rows_per_s": round(NT / (ms / 1e3), 1),
+        "per_op": per_op,
+        "largest_share": dom,
+        "gather": {"nccl_ms": round(per_op_ms["embedding"], 4), "p2p_ms": round(p2p_ms, 4),
+                   "rows_per_gpu": R, "row_bytes": c.hidden * 2,
+                   "algorithmic_bytes_per_gpu": mine["embedding"],
+                   "nvlink_read_bytes_per_gpu_max": int(nvlink_bytes),
+                   "nccl_nvlink_GBps": (round(nvlink_bytes / per_op_ms["embedding"] / 1e6, 1)
+                                        if world > 1 else None),
+                   "p2p_nvlink_GBps": (round(nvlink_bytes / p2p_ms / 1e6, 1)
+                                       if world > 1 else None),
+                   "bit_exact": verified,
+                   "check": "NCCL and P2P outputs equal; sampled rows equal the table rows"},
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1),
+                     "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
+                     "frac": round(achieved / peak, 3),
+                     "traffic": round(traffic * (LR if dom in ("softmax", "argmax") else R))
+                     if traffic else None,
+                     "algorithmic_bytes": mine[dom],
+                     "traffic_source": TRAFFIC_SOURCE if traffic else
+                     "no ncu capture of this kernel at this shape"},
+        "e2e": {"value": round(total_bytes / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": int(bi),
+                "d2h_bytes_per_step": int(bo),
+                "api": f"tb_b200_* C ABI: sharded gather from host ids, then {nb} row blocks "
+                       f"on {len(streams)} streams with pinned host copies in and out"},
+        "gpu_launches": int(launches),
+        "clocks": clocks.summary(),
+    }
+    return line
+
+
+# ------------------------------------------------------- bandwidth sweep
+SWEEP_ROWS = [1 << k for k in range(10, 21)]
+SWEEP_WIDTHS = [2048, 4096, 8192, 16384]
+SWEEP_LOGIT_ROWS = [1, 16, 256, 4096]
+SWEEP_VOCAB = 128256
+SWEEP_REPS = 5
+
+
+def run_sweep(args, rank, world, local):
+    """Each point launched alone: residual+RMSNorm [rows, w] and SwiGLU over
+    [rows, w] elements for the sweep's rows and widths, f32 and bf16, then
+    softmax and argmax over [rows, 128256] f32 logits.  A point's rows are
+    split over the ranks (tb_b200_partition); its time is the median over
+    SWEEP_REPS launches of the max over ranks.  L2 is flushed (a 512 MB
+    write) before every timed launch whose buffers would fit in 4x L2.
+    Points whose buffers exceed the memory budget are listed as skipped."""
+    import torch
+    import torch.distributed as dist
+    import tb_b200 as T
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    L = T.lib()
+    props = torch.cuda.get_device_properties(dev)
+    budget = min(int(0.75 * props.total_memory), 136 * 10**9)
+    l2 = getattr(props, "L2_cache_size", 126 * 2**20)
+    flush = torch.empty(512 * 2**20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    sp = C.c_void_p(stream.cuda_stream)
+    peak, peak_kind = peaks()
+    g = torch.Generator(device=dev)
+    g.manual_seed(777 + rank)
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        x = torch.tensor([float(v)], dtype=torch.float64, device=dev)
+        dist.all_reduce(x, op=dist.ReduceOp.MAX)
+        return float(x.item())
+
+    def time_point(launch, footprint):
+        for _ in range(2):
+            launch()
+        times = []
+        for _ in range(SWEEP_REPS):
+            if footprint < 4 * l2:
+                flush.fill_(1)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            launch()
+            b.record(stream)
+            b.synchronize()
+            times.append(max_over_ranks(a.elapsed_time(b)))
+        return statistics.median(times)
+
+    points, total_b, total_ms = [], 0, 0.0
+    l0 = L.tb_b200_launch_count()
+    uuid = getattr(props, "uuid", None)
+    uuid = f"GPU-{uuid}" if uuid is not None else None
+    with ClockSampler(local, uuid) as clocks:
+        for dt, s_, tdt in ((T.F32, 4, torch.float32), (T.BF16, 2, torch.bfloat16)):
+            for op in ("residual_rms_norm", "swiglu"):
+                for w in SWEEP_WIDTHS:
+                    for rows in SWEEP_ROWS:
+                        lo, hi = T.partition(rows, world, rank)
+                        big = -(-rows // world)  # the largest rank's rows
+                        nt = 4 if op == "residual_rms_norm" else 3
+                        pt = {"op": op, "dtype": "f32" if s_ == 4 else "bf16", "rows": rows,
+                              "width": w}
+                        if nt * big * w * s_ > budget:
+                            pt["skipped"] = "buffers exceed the memory budget"
+                            points.append(pt)
+                            continue
+                        r = hi - lo
+                        buf = [torch.randn((r, w), generator=g, device=dev).to(tdt)
+                               for _ in range(nt)]
+                        if op == "residual_rms_norm":
+                            gam = torch.randn((w,), generator=g, device=dev).to(tdt) * 0.1 + 1
+                            x, res, h, y = buf
+
+                            def launch():
+                                T.check(L.tb_b200_residual_rms_norm(
+                                    dt, r, w, T.ptr(x), T.ptr(res), T.ptr(gam), T.ptr(h),
+                                    T.ptr(y), C.c_float(1e-5), sp), "residual_rms_norm")
+                            nbytes = W.bytes_res_rms(rows, w, s_)
+                        else:
+                            gate, up, out = buf
+
+                            def launch():
+                                T.check(L.tb_b200_swiglu(dt, r * w, T.ptr(gate), T.ptr(up),
+                                                         T.ptr(out), sp), "swiglu")
+                            nbytes = W.bytes_swiglu(rows, w, s_)
+                        ms = time_point(launch, nt * r * w * s_)
+                        del buf
+                        pt.update({"ms": round(ms, 5), "GB/s": round(nbytes / ms / 1e6, 1),
+                                   "frac": round(nbytes / ms / 1e6 / peak, 3)})
+                        points.append(pt)
+                        total_b += nbytes
+                        total_ms += ms
+        for op in ("softmax", "argmax"):
+            for rows in SWEEP_LOGIT_ROWS:
+                lo, hi = T.partition(rows, world, rank)
+                r = hi - lo
+                x = torch.randn((r, SWEEP_VOCAB), generator=g, device=dev) * 3.0
+                if op == "softmax":
+                    y = torch.empty_like(x)
+
+                    def launch():
+                        T.check(L.tb_b200_softmax(T.F32, r, SWEEP_VOCAB, T.ptr(x), None,
+                                                  T.ptr(y), sp), "softmax")
+                    nbytes, fp = W.bytes_softmax(rows, SWEEP_VOCAB, 4), 2 * r * SWEEP_VOCAB * 4
+                else:
+                    y = torch.empty(max(r, 1), dtype=torch.int32, device=dev)
+
+                    def launch():
+                        T.check(L.tb_b200_argmax(T.F32, r, SWEEP_VOCAB, T.ptr(x), T.ptr(y), sp),
+                                "argmax")
+                    nbytes, fp = W.bytes_argmax(rows, SWEEP_VOCAB, 4), r * SWEEP_VOCAB * 4
+                ms = time_point(launch, fp)
+                del x, y
+                points.append({"op": op, "dtype": "f32", "rows": rows, "width": SWEEP_VOCAB,
+                               "ms": round(ms, 5), "GB/s": round(nbytes / ms / 1e6, 1),
+                               "frac": round(nbytes / ms / 1e6 / peak, 3)})
+                total_b += nbytes
+                total_ms += ms
+    launches = L.tb_b200_launch_count() - l0
+    done = [p_ for p_ in points if "ms" in p_]
+    biggest = max(done, key=lambda p_: p_["ms"])
+    below = [f'{p_["op"]} {p_["dtype"]} {p_["rows"]}x{p_["width"]}: {p_["frac"]}'
+             for p_ in done if p_["frac"] < 0.8]
+    return {
+        "metric": METRIC, "value": round(total_b / total_ms / 1e6, 1), "unit": "GB/s",
+        "n_gpus": world, "steps": SWEEP_REPS, "warmup": 2,
+        "ms_per_step": round(total_ms, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32 and bf16 (f32 arithmetic)",
+        "data": "synthetic (N(0,1) activations, N(0,3) logits)",
+        "config": {"workload": WORKLOAD, "rows": SWEEP_ROWS, "widths": SWEEP_WIDTHS,
+                   "logit_rows": SWEEP_LOGIT_ROWS, "vocab": SWEEP_VOCAB,
+                   "memory_budget_bytes": budget,
+                   "l2": "points smaller than 4x L2 flushed with a 512 MB write before each "
+                         "timed launch; the rest exceed L2",
+                   "parallelism": f"each point's rows split x{world}"},
+        "points": points, "below_0.8": below,
+        "roofline": {"bound": "hbm", "kernel": f'{biggest["op"]} {biggest["dtype"]} '
+                                              f'{biggest["rows"]}x{biggest["width"]}',
+                     "achieved": biggest["GB/s"], "peak": peak, "peak_source": peak_kind,
+                     "unit": "GB/s", "frac": biggest["frac"], "traffic": None,
+                     "traffic_source": "no ncu capture of the sweep"},
+        "e2e": None,
+        "gpu_launches": int(launches),
+        "clocks": clocks.summary(),
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -923,13 +1436,16 @@ def main():
     ap.add_argument("--profile-op", choices=["embedding", "layer_chain", "softmax", "argmax"],
                     help="only launch this op (warmup + steps times) on --rows rows: a small "
                          "case for ncu captures")
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="7b",
-                    help="7b (default): the Llama-7B prefill step; 70b: the Llama-70B prefill's "
-                         "layer ops and the sweep's 4096 x 128256 softmax/argmax; decode: the "
-                         "32-layer chain over a 256-sequence decode batch; runner: single-"
-                         "sequence decode through the device TransformerRunner (f32, 2:4); "
-                         "runner_int4: the same with INT4 projections")
-    ap.add_argument("--rows", type=int, default=None, help="layer-op rows per GPU (config's)")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default=DEFAULT_CONFIG,
+                    help="70b (default): the Llama-70B prefill of 16384 tokens strong-scaled "
+                         "over the ranks, with the vocab-sharded embedding gather and the "
+                         "4096 x 128256 softmax/argmax; 7b: the Llama-7B prefill step on every "
+                         "rank; decode: the 32-layer chain over a 256-sequence decode batch; "
+                         "runner: single-sequence decode through the device TransformerRunner "
+                         "(f32, 2:4); runner_int4: the same with INT4 projections; sweep: the "
+                         "bandwidth sweep")
+    ap.add_argument("--rows", type=int, default=None,
+                    help="layer-op rows (70b: of the whole job; else per GPU; config's)")
     ap.add_argument("--runner-layers", type=int, default=RUNNER_LAYERS,
                     help="layers of the runner configs' model (32; fewer for small ncu captures)")
     args = ap.parse_args()
@@ -957,12 +1473,12 @@ def main():
                                 device_id=torch.device("cuda", local))
     try:
         decode = args.config == "decode"
-        run = {"decode": run_decode, "runner": run_runner,
-               "runner_int4": run_runner}.get(args.config, run_gpu)
+        run = {"decode": run_decode, "runner": run_runner, "runner_int4": run_runner,
+               "70b": run_sharded, "sweep": run_sweep}.get(args.config, run_gpu)
         line = run(args, rank, world, local)
         if line is None:
             return
-        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config != "sweep":
             if args.config in ("runner", "runner_int4"):
                 per_token, sample = cpu_sample_runner()
                 line["cpu_baseline"] = {"value": round(1.0 / per_token, 4), "unit": "tokens/s",
