@@ -1346,10 +1346,11 @@ def run_sweep(args, rank, world, local):
                             points.append(pt)
                             continue
                         r = hi - lo
-                        buf = [torch.randn((r, w), generator=g, device=dev).to(tdt)
+                        buf = [torch.empty((r, w), dtype=tdt, device=dev).normal_(generator=g)
                                for _ in range(nt)]
                         if op == "residual_rms_norm":
-                            gam = torch.randn((w,), generator=g, device=dev).to(tdt) * 0.1 + 1
+                            gam = torch.empty((w,), dtype=tdt, device=dev).normal_(
+                                1.0, 0.1, generator=g)
                             x, res, h, y = buf
 
                             def launch():
@@ -1365,7 +1366,12 @@ def run_sweep(args, rank, world, local):
                                                          T.ptr(out), sp), "swiglu")
                             nbytes = W.bytes_swiglu(rows, w, s_)
                         ms = time_point(launch, nt * r * w * s_)
-                        del buf
+                        del buf, launch
+                        if op == "residual_rms_norm":
+                            del x, res, h, y
+                        else:
+                            del gate, up, out
+                        torch.cuda.empty_cache()
                         pt.update({"ms": round(ms, 5), "GB/s": round(nbytes / ms / 1e6, 1),
                                    "frac": round(nbytes / ms / 1e6 / peak, 3)})
                         points.append(pt)
@@ -1375,7 +1381,7 @@ def run_sweep(args, rank, world, local):
             for rows in SWEEP_LOGIT_ROWS:
                 lo, hi = T.partition(rows, world, rank)
                 r = hi - lo
-                x = torch.randn((r, SWEEP_VOCAB), generator=g, device=dev) * 3.0
+                x = torch.empty((r, SWEEP_VOCAB), device=dev).normal_(0.0, 3.0, generator=g)
                 if op == "softmax":
                     y = torch.empty_like(x)
 
@@ -1391,7 +1397,8 @@ def run_sweep(args, rank, world, local):
                                 "argmax")
                     nbytes, fp = W.bytes_argmax(rows, SWEEP_VOCAB, 4), r * SWEEP_VOCAB * 4
                 ms = time_point(launch, fp)
-                del x, y
+                del x, y, launch
+                torch.cuda.empty_cache()
                 points.append({"op": op, "dtype": "f32", "rows": rows, "width": SWEEP_VOCAB,
                                "ms": round(ms, 5), "GB/s": round(nbytes / ms / 1e6, 1),
                                "frac": round(nbytes / ms / 1e6 / peak, 3)})

@@ -130,23 +130,35 @@ int wait_comm(const char* what) {
             g_comm = nullptr;
             return TB_ERR_DEVICE;
         }
-        std::this_thread::sleep_for(std::chrono::microseconds(50));
+        if (el > 1e-3)
+            std::this_thread::sleep_for(std::chrono::microseconds(50));
+        else
+            std::this_thread::yield();
     }
 }
 
 // Copy n rows of `words` W-words: dst[drow(j)] = src[srow(j)], where a NULL
-// index list means the identity.
+// index list means the identity.  64 threads per row, four loads in flight
+// per thread before their stores.
 template <typename W>
 __global__ void __launch_bounds__(256)
 k_rows(W* __restrict__ dst, const int32_t* __restrict__ drow, const W* __restrict__ src,
        const int32_t* __restrict__ srow, int64_t n, int64_t words) {
-    constexpr int kGroup = 64;
+    constexpr int kGroup = 64, kU = 4;
     const int64_t j = (int64_t)blockIdx.x * (blockDim.x / kGroup) + threadIdx.x / kGroup;
     if (j >= n) return;
     const int64_t di = drow ? drow[j] : j, si = srow ? srow[j] : j;
     const W* s = src + si * words;
     W* d = dst + di * words;
-    for (int64_t i = threadIdx.x % kGroup; i < words; i += kGroup) d[i] = s[i];
+    int64_t i = threadIdx.x % kGroup;
+    for (; i + (kU - 1) * kGroup < words; i += kU * kGroup) {
+        W v[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) v[u] = s[i + u * kGroup];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) d[i + u * kGroup] = v[u];
+    }
+    for (; i < words; i += kGroup) d[i] = s[i];
 }
 
 int copy_rows(void* dst, const int32_t* drow, const void* src, const int32_t* srow, int64_t n,
@@ -169,11 +181,64 @@ int copy_rows(void* dst, const int32_t* drow, const void* src, const int32_t* sr
     return TB_OK;
 }
 
-int owner_of(int64_t id, int64_t vocab, int nranks) {
-    const int64_t base = vocab / nranks, extra = vocab % nranks;
-    const int64_t big = extra * (base + 1);
-    if (id < big) return (int)(id / (base + 1));
-    return (int)(extra + (id - big) / base);
+// Rank owning table row `id` under tb_b200_partition(vocab, nranks, .):
+// ends[r] is rank r's end row; a short linear search (nranks <= 8 on a box).
+inline int owner_of(int64_t id, const int64_t* ends, int nranks) {
+    int r = 0;
+    while (r < nranks - 1 && id >= ends[r]) ++r;
+    return r;
+}
+
+// Per-communicator buffers of the sharded gather, kept across calls: the
+// device block [plan indices | send rows | receive rows], grown on demand,
+// and a ring of two page-locked plan buffers for the host-to-device copy.
+struct GatherBufs {
+    void* dev = nullptr;
+    size_t dev_cap = 0;
+    int32_t* host[2] = {nullptr, nullptr};
+    size_t host_cap[2] = {0, 0};
+    cudaEvent_t host_free[2] = {nullptr, nullptr};  // the copy out of host[k] is done
+    cudaEvent_t dev_free = nullptr;                 // the last call is done with `dev`
+    int k = 0;
+};
+GatherBufs g_bufs;
+
+// Wait for `ev` at most TB_B200_COMM_TIMEOUT_S; false on timeout or error.
+bool wait_event(cudaEvent_t ev) {
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        const cudaError_t e = cudaEventQuery(ev);
+        if (e == cudaSuccess) return true;
+        if (e != cudaErrorNotReady) return false;
+        if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() >
+            timeout_s())
+            return false;
+        std::this_thread::yield();
+    }
+}
+
+void release_bufs() {
+    // The buffers may still be used by queued work: wait for it, bounded.
+    // Work that never finishes (an exchange with a peer that is gone, not
+    // ended by an abort) keeps its buffers: they are left allocated.
+    bool idle = true;
+    if (g_bufs.dev_free) idle = wait_event(g_bufs.dev_free);
+    for (int k = 0; k < 2; ++k)
+        if (g_bufs.host_free[k]) idle = wait_event(g_bufs.host_free[k]) && idle;
+    if (!idle) {
+        g_bufs = GatherBufs();
+        return;
+    }
+    for (int k = 0; k < 2; ++k) {
+        if (g_bufs.host[k]) cudaFreeHost(g_bufs.host[k]);
+        if (g_bufs.host_free[k]) cudaEventDestroy(g_bufs.host_free[k]);
+        g_bufs.host[k] = nullptr;
+        g_bufs.host_cap[k] = 0;
+        g_bufs.host_free[k] = nullptr;
+    }
+    if (g_bufs.dev) cudaFree(g_bufs.dev);
+    if (g_bufs.dev_free) cudaEventDestroy(g_bufs.dev_free);
+    g_bufs = GatherBufs();
 }
 
 }  // namespace
@@ -191,41 +256,47 @@ int tb_b200_shard_plan(int64_t n_tokens, int64_t vocab, int nranks, int rank,
         return TB_ERR_INVALID_ARG;
     for (int64_t t = 0; t < n_tokens; ++t)
         if (ids[t] < 0 || ids[t] >= vocab) return TB_ERR_INVALID_ARG;
-    int64_t my_vlo, my_vhi, my_tlo, my_thi;
-    tb_b200_partition(vocab, nranks, rank, &my_vlo, &my_vhi);
-    tb_b200_partition(n_tokens, nranks, rank, &my_tlo, &my_thi);
-    int64_t ns = 0, nl = 0;
-    // Rows this rank sends: destination-major, token order within a destination.
-    for (int d = 0; d < nranks; ++d) {
-        int64_t lo, hi;
-        tb_b200_partition(n_tokens, nranks, d, &lo, &hi);
-        int64_t c = 0;
-        for (int64_t t = lo; t < hi; ++t) {
-            if (owner_of(ids[t], vocab, nranks) != rank) continue;
-            if (d == rank) {
-                local_dst[nl] = (int32_t)(t - my_tlo);
-                local_src[nl] = (int32_t)(ids[t] - my_vlo);
-                ++nl;
-            } else {
-                send_rows[ns++] = (int32_t)(ids[t] - my_vlo);
-                ++c;
-            }
-        }
-        send_counts[d] = c;
+    // One pass over the tokens: each token's owner from the vocab parts'
+    // boundaries (no division per token).
+    int64_t vend[64], tend[64];
+    if (nranks > 64) return TB_ERR_INVALID_ARG;
+    for (int r = 0; r < nranks; ++r) {
+        int64_t lo;
+        tb_b200_partition(vocab, nranks, r, &lo, &vend[r]);
+        tb_b200_partition(n_tokens, nranks, r, &lo, &tend[r]);
     }
-    // Rows this rank receives: source-major, token order within a source.
-    int64_t nr = 0;
-    for (int s = 0; s < nranks; ++s) {
-        int64_t c = 0;
-        if (s != rank) {
-            for (int64_t t = my_tlo; t < my_thi; ++t) {
-                if (owner_of(ids[t], vocab, nranks) == s) {
-                    recv_rows[nr++] = (int32_t)(t - my_tlo);
-                    ++c;
-                }
-            }
+    const int64_t my_vlo = rank ? vend[rank - 1] : 0;
+    const int64_t my_tlo = rank ? tend[rank - 1] : 0, my_thi = tend[rank];
+    int64_t ns = 0, nl = 0;
+    // Rows this rank sends: destination-major (destinations own consecutive
+    // token parts), token order within a destination.
+    int d = 0;
+    for (int r = 0; r < nranks; ++r) send_counts[r] = recv_counts[r] = 0;
+    for (int64_t t = 0; t < n_tokens; ++t) {
+        while (t >= tend[d]) ++d;
+        const int64_t id = ids[t];
+        if (owner_of(id, vend, nranks) != rank) continue;
+        if (d == rank) {
+            local_dst[nl] = (int32_t)(t - my_tlo);
+            local_src[nl] = (int32_t)(id - my_vlo);
+            ++nl;
+        } else {
+            send_rows[ns++] = (int32_t)(id - my_vlo);
+            ++send_counts[d];
         }
-        recv_counts[s] = c;
+    }
+    // Rows this rank receives: source-major, token order within a source
+    // (a counting sort of this rank's tokens by owner).
+    int64_t start[65];
+    for (int64_t t = my_tlo; t < my_thi; ++t) {
+        const int o = owner_of(ids[t], vend, nranks);
+        if (o != rank) ++recv_counts[o];
+    }
+    start[0] = 0;
+    for (int r = 0; r < nranks; ++r) start[r + 1] = start[r] + recv_counts[r];
+    for (int64_t t = my_tlo; t < my_thi; ++t) {
+        const int o = owner_of(ids[t], vend, nranks);
+        if (o != rank) recv_rows[start[o]++] = (int32_t)(t - my_tlo);
     }
     *n_local = nl;
     return TB_OK;
@@ -264,10 +335,15 @@ int tb_b200_comm_init(int nranks, int rank, const void* unique_id, int device) {
     if (rc) return rc;
     g_rank = rank;
     g_nranks = nranks;
+    release_bufs();  // left from an aborted communicator, if any
+    TB_CUDA_TRY(cudaEventCreateWithFlags(&g_bufs.dev_free, cudaEventDisableTiming));
+    for (int k = 0; k < 2; ++k)
+        TB_CUDA_TRY(cudaEventCreateWithFlags(&g_bufs.host_free[k], cudaEventDisableTiming));
     return TB_OK;
 }
 
 int tb_b200_comm_destroy(void) {
+    release_bufs();
     if (!g_comm) return TB_OK;
     ncclResult_t r = g_nccl.CommFinalize(g_comm);
     int rc = TB_OK;
@@ -364,13 +440,30 @@ int tb_b200_embedding_sharded(int dtype, int64_t n_tokens, int64_t dim, int64_t 
     tb_b200_partition(n_tokens, N, me, &tlo, &thi);
     if (thi > tlo && !y_local) return TB_ERR_INVALID_ARG;
 
-    // Plan on the host; one int32 block [send | recv | local dst | local src].
+    // Plan on the host, straight into a page-locked buffer of the ring:
+    // [send rows | recv rows | local dst | local src], each of capacity
+    // n_tokens, copied to the device block in one transfer.
+    GatherBufs& B = g_bufs;
+    const int k = B.k;
+    B.k ^= 1;
+    const size_t idx_ints = 4 * (size_t)n_tokens + 4;
+    cudaError_t e = wait_event(B.host_free[k]) ? cudaSuccess : cudaErrorNotReady;  // its copy two calls ago
+    if (e == cudaSuccess && B.host_cap[k] < idx_ints) {
+        if (B.host[k]) cudaFreeHost(B.host[k]);
+        B.host[k] = nullptr;
+        B.host_cap[k] = 0;
+        e = cudaMallocHost(reinterpret_cast<void**>(&B.host[k]), idx_ints * sizeof(int32_t));
+        if (e == cudaSuccess) B.host_cap[k] = idx_ints;
+    }
+    if (e != cudaSuccess) {
+        tbh::set_error("sharded embedding plan buffer", e);
+        return TB_ERR_DEVICE;
+    }
     std::vector<int64_t> sc(N), rcnt(N);
-    std::vector<int32_t> idx(4 * (size_t)(n_tokens + 1));
-    int32_t* send_rows = idx.data();
-    int32_t* recv_rows = send_rows + n_tokens + 1;
-    int32_t* ldst = recv_rows + n_tokens + 1;
-    int32_t* lsrc = ldst + n_tokens + 1;
+    int32_t* send_rows = B.host[k];
+    int32_t* recv_rows = send_rows + n_tokens;
+    int32_t* ldst = recv_rows + n_tokens;
+    int32_t* lsrc = ldst + n_tokens;
     int64_t nl = 0;
     int rc = tb_b200_shard_plan(n_tokens, vocab, N, me, ids, sc.data(), rcnt.data(), send_rows,
                                 recv_rows, ldst, lsrc, &nl);
@@ -380,72 +473,72 @@ int tb_b200_embedding_sharded(int dtype, int64_t n_tokens, int64_t dim, int64_t 
         ns += sc[p];
         nr += rcnt[p];
     }
-    // Compact: [send_rows(ns) | recv_rows(nr) | ldst(nl) | lsrc(nl)].
-    std::vector<int32_t> packed((size_t)(ns + nr + 2 * nl) + 1);
-    memcpy(packed.data(), send_rows, ns * sizeof(int32_t));
-    memcpy(packed.data() + ns, recv_rows, nr * sizeof(int32_t));
-    memcpy(packed.data() + ns + nr, ldst, nl * sizeof(int32_t));
-    memcpy(packed.data() + ns + nr + nl, lsrc, nl * sizeof(int32_t));
-
+    // Device block: the four index lists at their fixed offsets, then the
+    // send rows and the received rows (16-byte aligned).
+    const size_t idx_bytes = (idx_ints * sizeof(int32_t) + 255) / 256 * 256;
+    const size_t send_bytes = ((size_t)(ns * row_bytes) + 255) / 256 * 256;
+    const size_t need = idx_bytes + send_bytes + (size_t)(nr * row_bytes);
     cudaStream_t s = tbh::stream_of(stream);
-    void* didx = nullptr;
-    void* sendbuf = nullptr;
-    void* recvbuf = nullptr;
-    auto release = [&]() {
-        if (didx) cudaFreeAsync(didx, s);
-        if (sendbuf) cudaFreeAsync(sendbuf, s);
-        if (recvbuf) cudaFreeAsync(recvbuf, s);
-    };
-    rc = tb_b200_stage_h2d(packed.data(), packed.size() * sizeof(int32_t), &didx, s);
-    if (rc) return rc;
-    const int32_t* d_send = static_cast<const int32_t*>(didx);
-    const int32_t* d_recv = d_send + ns;
-    const int32_t* d_ldst = d_recv + nr;
-    const int32_t* d_lsrc = d_ldst + nl;
-    cudaError_t e = cudaSuccess;
-    if (ns) e = cudaMallocAsync(&sendbuf, (size_t)(ns * row_bytes), s);
-    if (e == cudaSuccess && nr) e = cudaMallocAsync(&recvbuf, (size_t)(nr * row_bytes), s);
-    if (e != cudaSuccess) {
-        tbh::set_error("sharded embedding buffers", e);
-        release();
-        return TB_ERR_DEVICE;
+    if (B.dev_cap < need) {  // grow: the previous call must be done with the block
+        e = wait_event(B.dev_free) ? cudaSuccess : cudaErrorNotReady;
+        if (e == cudaSuccess) {
+            if (B.dev) cudaFree(B.dev);
+            B.dev = nullptr;
+            B.dev_cap = 0;
+            e = cudaMalloc(&B.dev, need + need / 4);
+            if (e == cudaSuccess) B.dev_cap = need + need / 4;
+        }
+        if (e != cudaSuccess) {
+            tbh::set_error("sharded embedding buffers", e);
+            return TB_ERR_DEVICE;
+        }
     }
+    // A call on another stream may still be using the block.
+    TB_CUDA_TRY(cudaStreamWaitEvent(s, B.dev_free, 0));
+    int32_t* d_idx = static_cast<int32_t*>(B.dev);
+    TB_CUDA_TRY(cudaMemcpyAsync(d_idx, B.host[k], idx_ints * sizeof(int32_t),
+                                cudaMemcpyHostToDevice, s));
+    TB_CUDA_TRY(cudaEventRecord(B.host_free[k], s));
+    const int32_t* d_send = d_idx;
+    const int32_t* d_recv = d_idx + n_tokens;
+    const int32_t* d_ldst = d_recv + n_tokens;
+    const int32_t* d_lsrc = d_ldst + n_tokens;
+    char* sendbuf = static_cast<char*>(B.dev) + idx_bytes;
+    char* recvbuf = sendbuf + send_bytes;
     // Own rows: local tokens straight to the output, others packed.
     if ((rc = copy_rows(y_local, d_ldst, table_shard, d_lsrc, nl, row_bytes, s)) ||
-        (rc = copy_rows(sendbuf, nullptr, table_shard, d_send, ns, row_bytes, s))) {
-        release();
+        (rc = copy_rows(sendbuf, nullptr, table_shard, d_send, ns, row_bytes, s)))
         return rc;
-    }
     // One grouped exchange with every peer.
-    ncclResult_t r = g_nccl.GroupStart();
-    int64_t so = 0, ro = 0;
-    for (int p = 0; p < N && r == ncclSuccess; ++p) {
-        if (p == me) continue;
-        if (sc[p])
-            r = g_nccl.Send(static_cast<char*>(sendbuf) + so * row_bytes, (size_t)(sc[p] * row_bytes),
-                         ncclUint8, p, g_comm, s);
-        if ((r == ncclSuccess || r == ncclInProgress) && rcnt[p])
-            r = g_nccl.Recv(static_cast<char*>(recvbuf) + ro * row_bytes,
-                         (size_t)(rcnt[p] * row_bytes), ncclUint8, p, g_comm, s);
-        if (r == ncclInProgress) r = ncclSuccess;
-        so += sc[p];
-        ro += rcnt[p];
-    }
-    ncclResult_t r2 = g_nccl.GroupEnd();
-    if (r == ncclSuccess && r2 != ncclSuccess && r2 != ncclInProgress) r = r2;
-    if (r != ncclSuccess) {
-        nccl_error("sharded embedding exchange", r);
-        release();
-        return TB_ERR_DEVICE;
-    }
-    rc = wait_comm("sharded embedding exchange");
-    if (rc) {
-        release();
-        return rc;
+    ncclResult_t r = ncclSuccess;
+    if (N > 1) {
+        r = g_nccl.GroupStart();
+        int64_t so = 0, ro = 0;
+        for (int p = 0; p < N && r == ncclSuccess; ++p) {
+            if (p == me) continue;
+            if (sc[p])
+                r = g_nccl.Send(sendbuf + so * row_bytes, (size_t)(sc[p] * row_bytes), ncclUint8, p,
+                                g_comm, s);
+            if ((r == ncclSuccess || r == ncclInProgress) && rcnt[p])
+                r = g_nccl.Recv(recvbuf + ro * row_bytes, (size_t)(rcnt[p] * row_bytes), ncclUint8,
+                                p, g_comm, s);
+            if (r == ncclInProgress) r = ncclSuccess;
+            so += sc[p];
+            ro += rcnt[p];
+        }
+        ncclResult_t r2 = g_nccl.GroupEnd();
+        if (r == ncclSuccess && r2 != ncclSuccess && r2 != ncclInProgress) r = r2;
+        if (r != ncclSuccess) {
+            nccl_error("sharded embedding exchange", r);
+            return TB_ERR_DEVICE;
+        }
+        rc = wait_comm("sharded embedding exchange");
+        if (rc) return rc;
     }
     rc = copy_rows(y_local, d_recv, recvbuf, nullptr, nr, row_bytes, s);
-    release();
-    return rc;
+    if (rc) return rc;
+    TB_CUDA_TRY(cudaEventRecord(B.dev_free, s));
+    return TB_OK;
 }
 
 }  // extern "C"

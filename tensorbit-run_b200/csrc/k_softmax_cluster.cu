@@ -1,0 +1,710 @@
+// k_softmax_cluster.cu -- f32 row softmax, each row split over the CTAs of
+// one thread-block cluster, the reference's in-order sum reproduced exactly.
+//
+// Reference arithmetic (tb_cpu_softmax_f32, src/ops/softmax.c:4-32):
+//   m = max x (strict '>', from -inf);  e_i = expf(x_i - m);
+//   sum = ((e_0 + e_1) + e_2) + ...  (f32, in order);  y_i = e_i * (1.0f/sum) if sum > 0.
+// Here e_i = 2^fma(x_i, log2(e), -m*log2(e)) on the MUFU pipe (one expression
+// everywhere, so every pass sees the same bits; within a few ulp of expf).
+// The sum is the in-order f32 sum of those e_i, bit for bit: the integer-
+// grid argument of ordered_sum.cuh, applied per 256-term tile.
+//
+// Layout.  A row of `cols` terms is cut into 256-term tiles; a cluster of C
+// CTAs (C = ceil(tiles / 64), at most 8) takes a row, CTA c owning a segment
+// of T = ceil(tiles / C) consecutive tiles (at most 64 KB).  The clusters are
+// persistent: cluster q takes rows q, q + Q, ...  Each CTA has three segment
+// buffers, filled by bulk asynchronous copies (cp.async.bulk, one mbarrier
+// each): a segment is read from HBM once, two rows ahead of its use.
+//
+// Roles (16 warps per CTA):
+//   workers (9 warps), per row j, three phases interleaved with the next row
+//     A(j)  max over the segment; the segment max goes to every CTA of the
+//           cluster (st.shared::cluster + a remote mbarrier arrive);
+//     B(j)  with the row max: e in place, a sum estimate per tile, the
+//           segment's estimate to every CTA;
+//     A(j+1)
+//     C(j)  with the estimates of the segments before this one: the running-
+//           sum estimate at each tile start -> the binade the exact running
+//           sum is predicted to be in -> per tile the integer sum of
+//           rne(e / u) on that binade's grid u, as (D0, D1) for an even / odd
+//           running sum at the tile start (they differ only when a term is an
+//           exact tie); the summaries go to the row's scanner (remote
+//           stores); the buffer is released and the row three ahead is
+//           copied into it.
+//     So each cluster exchange has a whole phase of work to land in.
+//   scanners (2 warps; row j's scanner is warp (j / C) % 2 of CTA j % C):
+//     tile 0 summed in order by one lane; then 32 tiles per step: an ordered
+//     composition scan of the (D0, D1) functions gives each tile's start;
+//     the first tile that is not on its predicted grid, crosses the binade
+//     or is flagged is summed term by term (ordered_sum_tile, its terms
+//     recomputed from x in L2).  The row's sum and max go to every CTA.
+//   finalizers (5 warps): y = e * (1/sum) of the CTA's segment of each row,
+//     in row order, e recomputed from x (still in L2: the copies keep it
+//     there), streaming stores.
+// Every wait is bounded (%globaltimer, 2 s): a timeout raises
+// TB_B200_FLAG_WAIT_TIMEOUT and the CTA skips its remaining waits; every
+// thread of every CTA still reaches the final cluster barrier, so no CTA
+// leaves while a peer may write its shared memory, and no copy is in flight
+// when a CTA exits.  Only this GPU's memory is read; no multicast.
+#include <math.h>
+
+#include "ordered_sum.cuh"
+#include "tb_device.cuh"
+#include "tb_internal.h"
+#include "tma.cuh"
+
+namespace {
+
+constexpr int kTileN = 256;
+constexpr int kSegTiles = 64;  // tiles per CTA segment, at most
+constexpr int kMaxC = 8;       // CTAs per cluster (portable limit)
+constexpr int kMaxTiles = kSegTiles * kMaxC;
+constexpr int kNB = 3;         // segment buffers per CTA
+constexpr int kScanW = 2;      // scanner warps per CTA
+constexpr int kFinW = 5;       // finalizer warps
+constexpr int kWorkW = 9;      // worker warps
+constexpr int kNT = 512;
+constexpr int kKeys = kMaxC * kScanW;  // one per scanner warp of the cluster
+constexpr uint32_t kSat = 1u << 30;
+constexpr uint32_t kLimit = 1u << 24;
+constexpr uint32_t kExact = 1u << 16;  // meta flag: sum the tile term by term
+constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+constexpr float kLog2e = 1.44269504f;
+static_assert(kScanW + kFinW + kWorkW == kNT / 32, "warp roles");
+
+// Warp roles: scanners on warps 0 and 4 and finalizers on 8 and 12 share
+// warp scheduler 0 (warp id mod 4), so the scanners' latency-bound chains
+// never compete with the throughput-bound workers for issue slots.
+__device__ __forceinline__ int scanner_of(int w) { return w == 0 ? 0 : w == 4 ? 1 : -1; }
+__device__ __forceinline__ int finalizer_of(int w) { return w == 8 ? 0 : w >= 12 ? w - 11 : -1; }
+__device__ __forceinline__ int worker_of(int w) { return w - 1 - (w > 4) - (w > 8); }
+
+struct Ctl {
+    uint2 D[kScanW][kMaxTiles];          // summaries pushed by every CTA (row of scanner s)
+    uint32_t meta[kScanW][kMaxTiles];    // predicted binade (int8) | kExact
+    float row_m[kScanW];                 // the row max, pushed by CTA 0
+    float tsum[kSegTiles];               // this CTA's tile sum estimates
+    uint32_t lmeta[kSegTiles];           // this CTA's predicted binades
+    float xmax[2][kMaxC];                // segment maxima of rows of parity p
+    float xtot[2][kMaxC];                // segment sum estimates
+    float res_sum[kKeys];                // row results, by key j % (C * kScanW)
+    float res_m[kKeys];
+    float red[kWorkW];
+    float scratch[kScanW][kTileN];       // tile 0 of a scanner's row
+    uint64_t bar_x[kNB];                 // segment landed
+    uint64_t bar_max[2], bar_tot[2];     // C arrivals
+    uint64_t bar_sfree[kKeys];           // scanner of that key released its summaries
+    uint64_t bar_ready[kScanW];          // C arrivals: summaries of the row pushed
+    uint64_t bar_res[kKeys];             // the row's result is here
+    uint64_t bar_fcred[kScanW];          // C * kFinW arrivals: result slot read everywhere
+    int abort_flag;
+};
+
+// ------------------------------------------------------------- cluster PTX
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_id() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_count() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
+// Address of this CTA's shared variable p in CTA `cta`'s shared memory.
+__device__ __forceinline__ uint32_t remote(const void* p, uint32_t cta) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+                 : "=r"(r)
+                 : "r"(tbk::smem_addr(p)), "r"(cta));
+    return r;
+}
+__device__ __forceinline__ void st_remote(uint32_t a, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_remote(uint32_t a, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_remote(uint32_t a, uint2 v) {
+    asm volatile("st.shared::cluster.v2.u32 [%0], {%1, %2};" ::"r"(a), "r"(v.x), "r"(v.y)
+                 : "memory");
+}
+// One arrival on an mbarrier of any CTA of the cluster, ordered after this
+// thread's earlier shared-memory stores (release at cluster scope).
+__device__ __forceinline__ void arrive_remote(uint32_t bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ bool try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(tbk::smem_addr(bar)), "r"(parity), "r"(tbk::kSuspendHintNs)
+        : "memory");
+    return done != 0;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n"
+                 "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Bounded wait on a barrier that remote CTAs arrive on; false (and the CTA
+// gives up waiting from then on) after a timeout or an earlier one.
+__device__ __forceinline__ bool wait_c(uint64_t* bar, uint32_t parity, unsigned* status,
+                                       volatile int* abort_flag) {
+    if (*abort_flag) return false;
+    if (try_wait_cluster(bar, parity)) return true;
+    const uint64_t t0 = tbk::global_ns();
+    while (!try_wait_cluster(bar, parity)) {
+        if (tbk::global_ns() - t0 > 2000000000ull) {
+            atomicOr(status, tbk::kFlagTimeout);
+            *abort_flag = 1;
+            return false;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void work_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kWorkW * 32) : "memory");
+}
+
+// ---------------------------------------------------------------- e and D
+// e = 2^(x*log2(e) - m*log2(e)): c = -m*log2(e).  When m*log2(e) is not
+// finite (|m| > 2.3e38) the row uses 2^((x - m)*log2(e)) instead.
+struct Expo {
+    float c, m;
+    bool slow;
+    __device__ __forceinline__ explicit Expo(float mx) : m(mx) {
+        c = __fmul_rn(-mx, kLog2e);
+        slow = !(fabsf(c) <= 3.0e38f) && (mx == mx);
+    }
+    __device__ __forceinline__ float operator()(float x) const {
+        const float a = slow ? __fmul_rn(__fsub_rn(x, m), kLog2e) : __fmaf_rn(x, kLog2e, c);
+        float r;
+        asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+        return r;
+    }
+};
+
+// Units added by one term given the parity of the partial sum before it.
+struct Fn {
+    uint32_t a0, a1;  // total for an even / odd running sum at the start
+};
+__device__ __forceinline__ Fn compose(Fn f, Fn g) {  // f, then g
+    Fn r;
+    r.a0 = min(f.a0 + ((f.a0 & 1u) ? g.a1 : g.a0), kSat);
+    r.a1 = min(f.a1 + (((f.a1 + 1u) & 1u) ? g.a1 : g.a0), kSat);
+    return r;
+}
+__device__ __forceinline__ Fn term_fn(float e, float inv_u) {
+    const float a = __fmaf_rn(e, inv_u, kMagic);
+    const float r = __fsub_rn(a, kMagic);
+    const float d = __fmaf_rn(e, inv_u, -r);
+    const uint32_t ri = __float_as_uint(a) - 0x4B400000u;
+    if (fabsf(d) != 0.5f) return Fn{ri, ri};
+    const uint32_t base = d < 0.0f ? ri - 1u : ri;  // floor(t)
+    return Fn{base + (base & 1u), base + ((base + 1u) & 1u)};
+}
+__device__ __forceinline__ Fn warp_compose(Fn f) {  // lane 0 first; valid in lane 0
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        Fn g;
+        g.a0 = __shfl_down_sync(tbk::kFull, f.a0, o);
+        g.a1 = __shfl_down_sync(tbk::kFull, f.a1, o);
+        if ((lane & (2 * o - 1)) == 0) f = compose(f, g);
+    }
+    return f;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(tbk::kFull, v, o);
+    return v;
+}
+
+// ------------------------------------------------------------------ scanner
+// Tile `tile` of the row, term by term from x (lane l: terms 8l .. 8l+7).
+__device__ void resolve_tile(tbk::RunSum& st, const float* xr, const Expo& ex, int tile,
+                             int cols) {
+    const int lane = threadIdx.x & 31;
+    const int n = min(kTileN, cols - tile * kTileN);
+    float e[8];
+    const float* p = xr + (int64_t)tile * kTileN + 8 * lane;
+    if (8 * lane + 8 <= n) {
+        const float4 a = __ldcg(reinterpret_cast<const float4*>(p));
+        const float4 b = __ldcg(reinterpret_cast<const float4*>(p + 4));
+        e[0] = ex(a.x); e[1] = ex(a.y); e[2] = ex(a.z); e[3] = ex(a.w);
+        e[4] = ex(b.x); e[5] = ex(b.y); e[6] = ex(b.z); e[7] = ex(b.w);
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) e[k] = 8 * lane + k < n ? ex(__ldcg(p + k)) : 0.0f;
+    }
+    tbk::ordered_sum_tile<8>(st, e, n, 0);
+}
+
+// The in-order sum of the row from its summaries (lane-uniform result).
+__device__ float scan_row(const uint2* D, const uint32_t* meta, float* scratch, const float* xr,
+                          const Expo& ex, int cols) {
+    const int lane = threadIdx.x & 31;
+    const int ntiles = (cols + kTileN - 1) / kTileN;
+    // tile 0: strictly in order, one lane
+    const int n0 = min(cols, kTileN);
+    for (int k = lane; k < n0; k += 32) scratch[k] = ex(__ldcg(xr + k));
+    __syncwarp();
+    float acc = 0.0f;
+    if (lane == 0)
+        for (int k = 0; k < n0; ++k) acc = __fadd_rn(acc, scratch[k]);
+    acc = __shfl_sync(tbk::kFull, acc, 0);
+    __syncwarp();
+    tbk::RunSum st;
+    st.set(acc);
+    for (int t0 = 1; t0 < ntiles && !st.nan; t0 += 32) {
+            const int cnt = min(32, ntiles - t0);
+            uint2 dl = make_uint2(0u, 0u);
+            uint32_t mt = 0;
+            if (lane < cnt) {
+                dl = D[t0 + lane];
+                mt = meta[t0 + lane];
+            }
+            const int tb = (int)(int8_t)(mt & 0xffu);
+            int pos = 0;
+            while (pos < cnt && !st.nan) {
+                const bool valid = lane >= pos && lane < cnt;
+                const bool ok = valid && st.fast && !(mt & kExact) && tb == st.b;
+                const Fn f = ok ? Fn{dl.x, dl.y} : Fn{0u, 0u};
+                Fn inc = f;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    Fn g;
+                    g.a0 = __shfl_up_sync(tbk::kFull, inc.a0, o);
+                    g.a1 = __shfl_up_sync(tbk::kFull, inc.a1, o);
+                    if (lane >= o) inc = compose(g, inc);
+                }
+                Fn exc;
+                exc.a0 = __shfl_up_sync(tbk::kFull, inc.a0, 1);
+                exc.a1 = __shfl_up_sync(tbk::kFull, inc.a1, 1);
+                if (lane == 0) exc = Fn{0u, 0u};
+                const uint32_t p = st.S & 1u;
+                const uint32_t exs = p ? exc.a1 : exc.a0;
+                const uint32_t mine = ((p + exs) & 1u) ? f.a1 : f.a0;
+                const bool ev = valid && (!ok || st.S + exs + mine >= kLimit);
+                const unsigned bal = __ballot_sync(tbk::kFull, ev);
+                if (bal == 0) {
+                    st.S += __shfl_sync(tbk::kFull, p ? inc.a1 : inc.a0, 31);
+                    st.s = __fmul_rn((float)st.S, st.u);
+                    break;
+                }
+                const int fl = __ffs(bal) - 1;
+                const uint32_t pre = __shfl_sync(tbk::kFull, exs, fl);
+                if (st.fast && pre) {
+                    st.S += pre;
+                    st.s = __fmul_rn((float)st.S, st.u);
+                }
+                resolve_tile(st, xr, ex, t0 + fl, cols);
+                pos = fl + 1;
+            }
+    }
+    return st.s;
+}
+
+// ------------------------------------------------------------------ kernel
+__global__ void __launch_bounds__(kNT, 1)
+k_softmax_cluster(const float* __restrict__ x, float* y, int rows, int cols, int seg_tiles,
+                  unsigned* status) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ __align__(16) Ctl ctl;
+    float* xbuf = reinterpret_cast<float*>(smem);  // [kNB][seg_tiles * 256]
+
+    uint32_t nc;
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(nc));
+    const uint32_t me = cluster_rank();
+    const int Q = (int)cluster_count(), q = (int)cluster_id();
+    const int ncl = (int)nc;
+    const int keys = ncl * kScanW;
+    const int ntiles = (cols + kTileN - 1) / kTileN;
+    const int t0 = (int)me * seg_tiles;                       // first tile of the segment
+    const int nt = max(0, min(seg_tiles, ntiles - t0));       // tiles in it
+    const int col0 = t0 * kTileN, col1 = min(cols, (t0 + nt) * kTileN);
+    const uint32_t seg_bytes = (uint32_t)(col1 - col0) * 4u;
+    const int seg_floats = seg_tiles * kTileN;
+    const int nloc = rows > q ? (rows - 1 - q) / Q + 1 : 0;   // rows of this cluster
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    volatile int* abort_v = &ctl.abort_flag;
+
+    if (threadIdx.x == 0) {
+        for (int b = 0; b < kNB; ++b) tbk::mbar_init(&ctl.bar_x[b], 1);
+        for (int p = 0; p < 2; ++p) {
+            tbk::mbar_init(&ctl.bar_max[p], nc);
+            tbk::mbar_init(&ctl.bar_tot[p], nc);
+        }
+        for (int k = 0; k < kKeys; ++k) {
+            tbk::mbar_init(&ctl.bar_sfree[k], 1);
+            tbk::mbar_init(&ctl.bar_res[k], 1);
+        }
+        for (int s = 0; s < kScanW; ++s) {
+            tbk::mbar_init(&ctl.bar_ready[s], nc);
+            tbk::mbar_init(&ctl.bar_fcred[s], nc * kFinW);
+        }
+        ctl.abort_flag = 0;
+        tbk::fence_mbar_init();
+    }
+    __syncthreads();
+    cluster_sync_all();  // every CTA's barriers exist before any remote arrive
+
+    const int sw = scanner_of(warp), fw = finalizer_of(warp);
+    const int64_t row_stride = cols;
+    auto row_of = [&](int j) -> int64_t { return (int64_t)q + (int64_t)j * Q; };
+
+    if (sw >= 0) {
+        // ------------------------------------------------------ scanner
+        const int key = (int)me + ncl * sw;
+        for (int k = 0;; ++k) {
+            const int j = key + keys * k;
+            if (j >= nloc) break;
+            if (!wait_c(&ctl.bar_ready[sw], (uint32_t)k & 1u, status, abort_v)) break;
+            const float m = ctl.row_m[sw];
+            const Expo ex(m);
+            const float* xr = x + row_of(j) * row_stride;
+            const float sum = scan_row(ctl.D[sw], ctl.meta[sw], ctl.scratch[sw], xr, ex, cols);
+            // the summaries are consumed: every CTA may push its next row
+            __syncwarp();
+            if (lane < ncl) arrive_remote(remote(&ctl.bar_sfree[key], (uint32_t)lane));
+            // the result slot is free once every finalizer read row j - keys
+            if (k >= 1 && !wait_c(&ctl.bar_fcred[sw], (uint32_t)(k - 1) & 1u, status, abort_v))
+                break;
+            if (lane < ncl) {
+                st_remote(remote(&ctl.res_sum[key], (uint32_t)lane), sum);
+                st_remote(remote(&ctl.res_m[key], (uint32_t)lane), m);
+                arrive_remote(remote(&ctl.bar_res[key], (uint32_t)lane));
+            }
+        }
+    } else if (fw >= 0) {
+        // ------------------------------------------------------ finalizers
+        const int ft = fw * 32 + lane;
+        constexpr int kFin = kFinW * 32;
+        const uint64_t pol = tbk::policy_evict_first();  // last use of x
+        const int nv = (col1 - col0) / 4;
+        for (int j = 0; j < nloc; ++j) {
+            const int key = j % keys;
+            if (!wait_c(&ctl.bar_res[key], (uint32_t)(j / keys) & 1u, status, abort_v)) break;
+            const float sum = ctl.res_sum[key];
+            const float m = ctl.res_m[key];
+            __syncwarp();
+            if (lane == 0)
+                arrive_remote(remote(&ctl.bar_fcred[key / ncl], (uint32_t)(key % ncl)));
+            const Expo ex(m);
+            const bool norm = sum > 0.0f;
+            const float inv = __fdiv_rn(1.0f, sum);
+            const int64_t base = row_of(j) * row_stride + col0;
+            const float4* xr = reinterpret_cast<const float4*>(x + base);
+            float4* yr = reinterpret_cast<float4*>(y + base);
+            constexpr int kU = 8;
+            int v = ft;
+            for (; v + (kU - 1) * kFin < nv; v += kU * kFin) {
+                float4 a[kU];
+#pragma unroll
+                for (int u = 0; u < kU; ++u) a[u] = tbk::ld_f4_hint(xr + v + u * kFin, pol);
+#pragma unroll
+                for (int u = 0; u < kU; ++u) {
+                    float4 o;
+                    o.x = ex(a[u].x); o.y = ex(a[u].y); o.z = ex(a[u].z); o.w = ex(a[u].w);
+                    if (norm) {
+                        o.x = __fmul_rn(o.x, inv); o.y = __fmul_rn(o.y, inv);
+                        o.z = __fmul_rn(o.z, inv); o.w = __fmul_rn(o.w, inv);
+                    }
+                    __stcs(yr + v + u * kFin, o);
+                }
+            }
+            for (; v < nv; v += kFin) {
+                const float4 a = tbk::ld_f4_hint(xr + v, pol);
+                float4 o;
+                o.x = ex(a.x); o.y = ex(a.y); o.z = ex(a.z); o.w = ex(a.w);
+                if (norm) {
+                    o.x = __fmul_rn(o.x, inv); o.y = __fmul_rn(o.y, inv);
+                    o.z = __fmul_rn(o.z, inv); o.w = __fmul_rn(o.w, inv);
+                }
+                __stcs(yr + v, o);
+            }
+        }
+    } else {
+        // ------------------------------------------------------ workers
+        const int wi = worker_of(warp);
+        const bool producer = wi == 0 && lane == 0;
+        const uint64_t pol_keep = tbk::policy_evict_last();  // the finalizers read x again
+        auto seg = [&](int b) { return xbuf + (size_t)b * seg_floats; };
+        auto issue = [&](int j) {  // one thread: row j's segment into buffer j % kNB
+            const int b = j % kNB;
+            tbk::mbar_expect_tx(&ctl.bar_x[b], seg_bytes);
+            if (seg_bytes)
+                tbk::bulk_g2s_hint(seg(b), x + row_of(j) * row_stride + col0, seg_bytes,
+                                   &ctl.bar_x[b], pol_keep);
+        };
+        int issued = 0;  // rows whose copy was issued
+        if (producer)
+            for (; issued < min(kNB, nloc); ++issued) issue(issued);
+
+        // Phase A: segment max -> every CTA.
+        auto phase_a = [&](int j) {
+            const int b = j % kNB;
+            wait_c(&ctl.bar_x[b], (uint32_t)(j / kNB) & 1u, status, abort_v);
+            const float* s = seg(b);
+            float mx = -INFINITY;
+            for (int t = wi; t < nt; t += kWorkW) {
+                const float* xt = s + t * kTileN;
+                const int n = min(kTileN, (col1 - col0) - t * kTileN);
+                if (n == kTileN) {
+                    const float4 a = *reinterpret_cast<const float4*>(xt + 4 * lane);
+                    const float4 c = *reinterpret_cast<const float4*>(xt + 128 + 4 * lane);
+                    mx = fmaxf(mx, fmaxf(fmaxf(fmaxf(a.x, a.y), fmaxf(a.z, a.w)),
+                                         fmaxf(fmaxf(c.x, c.y), fmaxf(c.z, c.w))));
+                } else {
+                    for (int k = lane; k < n; k += 32) mx = fmaxf(mx, xt[k]);
+                }
+            }
+            mx = tbk::warp_max(mx);
+            if (lane == 0) ctl.red[wi] = mx;
+            work_sync();
+            if (wi == 0) {
+                float mc = ctl.red[0];
+#pragma unroll
+                for (int w = 1; w < kWorkW; ++w) mc = fmaxf(mc, ctl.red[w]);
+                if (lane < ncl) {
+                    st_remote(remote(&ctl.xmax[j & 1][me], (uint32_t)lane), mc);
+                    arrive_remote(remote(&ctl.bar_max[j & 1], (uint32_t)lane));
+                }
+            }
+        };
+        // Phase B: e in place, tile estimates, segment estimate -> every CTA.
+        auto phase_b = [&](int j) -> float {
+            wait_c(&ctl.bar_max[j & 1], (uint32_t)(j >> 1) & 1u, status, abort_v);
+            float m = ctl.xmax[j & 1][0];
+            for (int c = 1; c < ncl; ++c) m = fmaxf(m, ctl.xmax[j & 1][c]);
+            const Expo ex(m);
+            float* s = seg(j % kNB);
+            for (int t = wi; t < nt; t += kWorkW) {
+                float* xt = s + t * kTileN;
+                const int n = min(kTileN, (col1 - col0) - t * kTileN);
+                float acc = 0.0f;
+                if (n == kTileN) {
+                    float4 a = *reinterpret_cast<float4*>(xt + 4 * lane);
+                    float4 c = *reinterpret_cast<float4*>(xt + 128 + 4 * lane);
+                    a.x = ex(a.x); a.y = ex(a.y); a.z = ex(a.z); a.w = ex(a.w);
+                    c.x = ex(c.x); c.y = ex(c.y); c.z = ex(c.z); c.w = ex(c.w);
+                    *reinterpret_cast<float4*>(xt + 4 * lane) = a;
+                    *reinterpret_cast<float4*>(xt + 128 + 4 * lane) = c;
+                    acc = ((a.x + a.y) + (a.z + a.w)) + ((c.x + c.y) + (c.z + c.w));
+                } else {
+                    for (int k = lane; k < n; k += 32) {
+                        const float e = ex(xt[k]);
+                        xt[k] = e;
+                        acc += e;
+                    }
+                }
+                acc = warp_sum(acc);
+                if (lane == 0) ctl.tsum[t] = acc;
+            }
+            work_sync();
+            if (wi == 0) {
+                float v = 0.0f;
+                for (int t = lane; t < nt; t += 32) v += ctl.tsum[t];
+                v = warp_sum(v);
+                if (lane < ncl) {
+                    st_remote(remote(&ctl.xtot[j & 1][me], (uint32_t)lane), v);
+                    arrive_remote(remote(&ctl.bar_tot[j & 1], (uint32_t)lane));
+                }
+            }
+            return m;
+        };
+        // Phase C: predicted binades, (D0, D1) per tile -> the row's scanner.
+        auto phase_c = [&](int j, float m) {
+            wait_c(&ctl.bar_tot[j & 1], (uint32_t)(j >> 1) & 1u, status, abort_v);
+            const int key = j % keys;
+            const uint32_t tgt = (uint32_t)(key % ncl);
+            const int slot = key / ncl;
+            if (wi == 0) {
+                float run = 0.0f;  // estimate of the running sum at the segment start
+                for (int c = 0; c < (int)me; ++c) run += ctl.xtot[j & 1][c];
+                // warp scan of the segment's tile estimates (two per lane)
+                const float v0 = 2 * lane < nt ? ctl.tsum[2 * lane] : 0.0f;
+                const float v1 = 2 * lane + 1 < nt ? ctl.tsum[2 * lane + 1] : 0.0f;
+                float inc = v0 + v1;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const float nb = __shfl_up_sync(tbk::kFull, inc, o);
+                    if (lane >= o) inc += nb;
+                }
+                float ex0 = __shfl_up_sync(tbk::kFull, inc, 1);
+                if (lane == 0) ex0 = 0.0f;
+                const float p0 = run + ex0, p1 = p0 + v0;
+                const int b0 = tbk::binade_of(p0), b1 = tbk::binade_of(p1);
+                if (2 * lane < nt)
+                    ctl.lmeta[2 * lane] = ((uint32_t)b0 & 0xffu) | (b0 == tbk::kNoBinade ? kExact : 0u);
+                if (2 * lane + 1 < nt)
+                    ctl.lmeta[2 * lane + 1] =
+                        ((uint32_t)b1 & 0xffu) | (b1 == tbk::kNoBinade ? kExact : 0u);
+            }
+            // the scanner of this key must be done with row j - keys
+            if (j >= keys)
+                wait_c(&ctl.bar_sfree[key], (uint32_t)(j / keys - 1) & 1u, status, abort_v);
+            work_sync();
+            const float* s = seg(j % kNB);
+            const uint32_t rD = remote(&ctl.D[slot][0], tgt);
+            const uint32_t rM = remote(&ctl.meta[slot][0], tgt);
+            for (int t = wi; t < nt; t += kWorkW) {
+                const float* xt = s + t * kTileN;
+                const int n = min(kTileN, (col1 - col0) - t * kTileN);
+                const uint32_t mt = ctl.lmeta[t];
+                const int b = (int)(int8_t)(mt & 0xffu);
+                uint2 D = make_uint2(0u, 0u);
+                if (!(mt & kExact)) {
+                    const float iu = tbk::inv_grid(b);
+                    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), c = a;
+                    if (n == kTileN) {
+                        a = *reinterpret_cast<const float4*>(xt + 4 * lane);
+                        c = *reinterpret_cast<const float4*>(xt + 128 + 4 * lane);
+                    } else {
+                        if (4 * lane < n) a = *reinterpret_cast<const float4*>(xt + 4 * lane);
+                        if (128 + 4 * lane < n)
+                            c = *reinterpret_cast<const float4*>(xt + 128 + 4 * lane);
+                        // (n is a multiple of 4: a float4 is wholly in or out)
+                    }
+                    const float e[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+                    // Every term below 2^22 grid units makes the magic
+                    // rounding exact: certain when the tile's estimate is
+                    // below 2^21 units, checked term by term otherwise.
+                    const bool small = __fmul_rn(ctl.tsum[t], iu) < 2097152.0f;
+                    uint32_t acc = 0;
+                    float dm = 0.0f;
+                    bool bad = false;
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const float fa = __fmaf_rn(e[k], iu, kMagic);
+                        acc += __float_as_uint(fa);
+                        const float r = __fsub_rn(fa, kMagic);
+                        dm = fmaxf(dm, fabsf(__fmaf_rn(e[k], iu, -r)));
+                        if (!small) bad |= !(fa < 16777216.0f);  // t >= 2^22, or NaN
+                    }
+                    acc -= 8u * 0x4B400000u;  // sum of the eight rne(t), mod 2^32
+                    const bool big = !small && __any_sync(tbk::kFull, bad);
+                    const bool tie = __any_sync(tbk::kFull, dm == 0.5f);
+                    const uint32_t sum_u = __reduce_add_sync(tbk::kFull, acc);
+                    D = make_uint2(sum_u, sum_u);
+                    if (big) {
+                        D = make_uint2(kSat, kSat);
+                    } else if (tie) {
+                        Fn fa{0u, 0u}, fb{0u, 0u};
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) fa = compose(fa, term_fn(e[k], iu));
+#pragma unroll
+                        for (int k = 4; k < 8; ++k) fb = compose(fb, term_fn(e[k], iu));
+                        fa = warp_compose(fa);
+                        fb = warp_compose(fb);
+                        const Fn ft = compose(fa, fb);
+                        D = make_uint2(ft.a0, ft.a1);
+                    }
+                }
+                if (lane == 0) {
+                    st_remote(rD + 8u * (uint32_t)(t0 + t), D);
+                    st_remote(rM + 4u * (uint32_t)(t0 + t), mt);
+                }
+            }
+            // this warp's summary stores, ordered before the arrive below
+            if (lane == 0) asm volatile("fence.acq_rel.cluster;" ::: "memory");
+            work_sync();
+            if (wi == 0 && lane == 0) {
+                if (me == 0) st_remote(remote(&ctl.row_m[slot], tgt), m);
+                arrive_remote(remote(&ctl.bar_ready[slot], tgt));
+            }
+            // the buffer is free: the row kNB ahead is copied into it
+            if (producer && issued < nloc && !*abort_v) {
+                tbk::fence_proxy_async_shared();
+                issue(issued);
+                ++issued;
+            }
+        };
+
+        if (nloc > 0) phase_a(0);
+        for (int j = 0; j < nloc; ++j) {
+            const float m = phase_b(j);
+            if (j + 1 < nloc) phase_a(j + 1);
+            phase_c(j, m);
+        }
+        // No copy may still be writing this CTA's shared memory at exit
+        // (possible only after a timeout): a last bounded wait on each.
+        if (producer)
+            for (int r = max(0, issued - kNB); r < issued; ++r)
+                tbk::mbar_wait(&ctl.bar_x[r % kNB], (uint32_t)(r / kNB) & 1u, status, 200000000ull);
+    }
+    __syncwarp();
+    __syncthreads();
+    cluster_sync_all();  // no CTA leaves while a peer may still write its shared memory
+}
+
+}  // namespace
+
+namespace tbh {
+
+// f32 softmax through k_softmax_cluster.  Returns 1 (nothing launched) when
+// the shape is not one it handles: fewer than 1024 or more than 131072
+// columns, a column count that is not a multiple of 4, or unaligned rows.
+int softmax_cluster_f32(int64_t rows, int64_t cols, const float* x, float* y, cudaStream_t s) {
+    if (cols < 1024 || cols > (int64_t)kMaxTiles * kTileN || cols % 4 || !aligned16(x) ||
+        !aligned16(y) || rows > INT32_MAX)
+        return 1;
+    DeviceState* ds = current_device_state();
+    if (!ds) return TB_ERR_DEVICE;
+    const int ntiles = (int)((cols + kTileN - 1) / kTileN);
+    const int C = (ntiles + kSegTiles - 1) / kSegTiles;
+    const int seg_tiles = (ntiles + C - 1) / C;
+    const size_t smem = (size_t)kNB * seg_tiles * kTileN * sizeof(float);
+    static thread_local size_t attr_set[64];
+    static thread_local int clusters_cache[64][kMaxC + 1];
+    const int dv = ds->device;
+    if (dv < 0 || dv >= 64) return 1;
+    if (attr_set[dv] < smem) {
+        TB_CUDA_TRY(cudaFuncSetAttribute(k_softmax_cluster,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        attr_set[dv] = smem;
+        for (int c = 0; c <= kMaxC; ++c) clusters_cache[dv][c] = 0;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)C;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.blockDim = dim3(kNT);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    int& Q = clusters_cache[dv][C];
+    if (Q == 0) {
+        cfg.gridDim = dim3((unsigned)(C * ds->sm_count));
+        int n = 0;
+        TB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, k_softmax_cluster, &cfg));
+        if (n < 1) return 1;
+        Q = n;
+    }
+    const int nclu = (int)(rows < Q ? rows : Q);
+    cfg.gridDim = dim3((unsigned)(nclu * C));
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, k_softmax_cluster, static_cast<const float*>(x),
+                                             y, (int)rows, (int)cols, seg_tiles, ds->status);
+    count_launch();
+    if (e != cudaSuccess) {
+        set_error("softmax kernel (cluster)", e);
+        return TB_ERR_DEVICE;
+    }
+    return TB_OK;
+}
+
+}  // namespace tbh

@@ -62,6 +62,9 @@ inline NormCfg norm_cfg(int64_t nvec, int max_group) {
 // f32 softmax staged through shared memory (k_softmax_staged.cu): TB_OK
 // after launching, 1 when the shape is not one it handles, else an error.
 int softmax_staged_f32(int64_t rows, int64_t cols, const float* x, float* y, cudaStream_t s);
+// f32 softmax with each row split over a thread-block cluster
+// (k_softmax_cluster.cu): same return convention.
+int softmax_cluster_f32(int64_t rows, int64_t cols, const float* x, float* y, cudaStream_t s);
 
 }  // namespace tbh
 

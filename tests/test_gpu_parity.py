@@ -254,13 +254,21 @@ def test_rope_single_position_and_odd_head_dim(dev):
 
 
 # ----------------------------------------------------------------- softmax
-# f32 rows of up to 32768 columns (a multiple of 4, no mask) take the
-# shared-memory-staged kernel; "pipeline" gives every CTA several rows,
-# "staged_max" is its widest row, "past_staged" the first width beyond it.
+# f32 rows of 1024 to 131072 columns (a multiple of 4, no mask, aligned)
+# take the cluster kernel: C = ceil(tiles / 64) CTAs per row, 256-term tiles.
+# "pipeline" gives every cluster many rows (C = 1); "staged_max" (C = 2) and
+# "past_staged" (C = 3, a last tile of 4 terms); "c5" 5 CTAs of 64 tiles;
+# "c3_ragged" a last tile of 4 terms; "cluster_max" the widest row (8 CTAs
+# of 64 tiles); "c8_spiky" 8 CTAs with many binade crossings; "odd" and
+# "one" are below the cluster kernel's width and take the tiled kernel,
+# as do all bf16 cases.
 SOFTMAX_CASES = [("mock", 64, 100, 2.0), ("7b", 256, 32000, 3.0), ("70b", 16, 128256, 3.0),
                  ("odd", 9, 1001, 3.0), ("one", 3, 1, 1.0), ("wide_std", 8, 5000, 20.0),
                  ("pipeline", 600, 4096, 3.0), ("staged_max", 300, 32768, 3.0),
-                 ("past_staged", 5, 32772, 3.0), ("spiky", 40, 32000, 12.0)]
+                 ("past_staged", 5, 32772, 3.0), ("spiky", 40, 32000, 12.0),
+                 ("c5", 33, 81920, 3.0), ("c3_ragged", 17, 40964, 3.0),
+                 ("cluster_max", 20, 131072, 3.0), ("c8_spiky", 40, 128256, 12.0),
+                 ("min_cluster", 50, 1024, 3.0)]
 
 
 @pytest.mark.parametrize("name,rows,cols,std", SOFTMAX_CASES)
@@ -289,6 +297,21 @@ def test_softmax_sum_is_the_sequential_sum(dev):
     assert worst < 2e-6, f"softmax 128K row error {worst:.2e}: not the sequential sum"
 
 
+@pytest.mark.parametrize("std", [3.0, 12.0])
+def test_cluster_softmax_sum_over_many_rows(dev, std):
+    """400 rows of 128256 terms: every cluster takes many rows, so its
+    segment buffers, exchange slots and scanner keys all wrap around.
+    Each row must still be the sequential sum (row error < 2e-6)."""
+    rng = np.random.default_rng(79 + int(std))
+    x = rng.standard_normal((400, 128256), dtype=np.float32) * np.float32(std)
+    y_ref = O.softmax(x, threads=8)
+    gy = to_np(T.softmax(gpu(x, dev)))
+    sync()
+    worst, _ = assert_f32(gy, y_ref, f"cluster softmax std {std}")
+    assert worst < 2e-6, f"cluster softmax std {std}: row error {worst:.2e}"
+    assert T.check_status() == (0, 0)
+
+
 def test_softmax_in_place_and_nan_in_wide_rows(dev):
     """y may alias x; a NaN term makes its row NaN, other rows unaffected."""
     rng = np.random.default_rng(5)
@@ -296,6 +319,8 @@ def test_softmax_in_place_and_nan_in_wide_rows(dev):
     x[7, 20000] = np.float32("nan")
     x[8, :] = -np.inf
     x[9, 31999] = np.inf
+    x[10, 5] = np.float32(3e38)  # a row max beyond the fused exponent's range
+    x[11, :] = np.float32(1e30)
     y_ref = O.softmax(x)
     g = gpu(x, dev)
     T.softmax(g, y=g)
@@ -304,6 +329,10 @@ def test_softmax_in_place_and_nan_in_wide_rows(dev):
     assert (np.isnan(gy) == np.isnan(y_ref)).all()
     keep = ~np.isnan(y_ref).any(axis=1)
     assert_f32(gy[keep], y_ref[keep], "softmax in place")
+    # NaN rows are left unnormalised, as the reference leaves them
+    assert_f32(gy[7][~np.isnan(y_ref[7])][None], y_ref[7][~np.isnan(y_ref[7])][None],
+               "softmax NaN row")
+    assert T.check_status() == (0, 0)
 
 
 def test_staged_softmax_sum_is_the_sequential_sum(dev):
