@@ -398,6 +398,70 @@ int tb_b200_runner_launches_per_token(void* runner, int* launches);
 int tb_b200_runner_destroy(void* runner);
 
 /* ======================================================================
+ * .tbm model containers read into device memory
+ * ====================================================================== */
+
+/* The model config of a .tbm index, the reference's TbModelConfig
+ * (include/tensorbit/run/model.h:34-46) with its parser's defaults
+ * (src/model.c:280-341): norm_eps 1e-6 and rope_theta 10000 when absent,
+ * num_kv_heads = num_heads when 0, head_dim = hidden_size / num_heads. */
+typedef struct {
+    char architecture[64];
+    int hidden_size, num_heads, num_kv_heads, intermediate_size, vocab_size, max_seq_len,
+        num_layers;
+    float norm_eps, rope_theta;
+    int head_dim;
+} TbB200TbmConfig;
+
+/* One tensor of a loaded container: its index entry (the reference's
+ * TbLayerDesc, include/tensorbit/run/model.h:15-26) and DEVICE pointers to
+ * its bytes, copied unchanged from the file: weights (weight_bytes: INT4
+ * ceil(n/2), INT8 n, else n elements), mask (num_mask_bytes; NULL when 0)
+ * and f32 scales (scale_count of them, quantized tensors only; else NULL).
+ * The pointers stay valid until tb_b200_tbm_free. */
+typedef struct {
+    char name[128];
+    int64_t shape[2];
+    int dtype;
+    uint32_t nm_n, nm_m;
+    int64_t num_weights, num_mask_bytes, scale_count;
+    uint32_t group_size;
+    const void* weights;
+    const uint8_t* mask;
+    const float* scales;
+    int64_t weight_bytes;
+} TbB200TbmTensor;
+
+/* Read a .tbm container (docs/TBM_FORMAT.md) into one device allocation on
+ * the current device: the file is mapped read-only, its JSON index parsed as
+ * tb_model_load_tbm parses it (src/model.c:482-580), and every tensor's
+ * weights, mask bytes and scales -- located as the reference's zero-copy
+ * views locate them (src/model.c:681-739) -- streamed to the device through
+ * page-locked staging buffers on `stream`; returns once they have landed.
+ * Errors: TB_ERR_FILE_OPEN / TB_ERR_FILE_READ, TB_ERR_TRUNCATED (a file
+ * shorter than 20 bytes, a bad index length, or a tensor running past the
+ * end of the file), TB_ERR_JSON_PARSE, TB_ERR_DEVICE.  A tensor whose .tb
+ * header has a bad magic gets no device bytes; tb_b200_tbm_tensor reports it
+ * as TB_ERR_BAD_MAGIC, as the reference's views do. */
+int tb_b200_tbm_load(const char* path, void* stream, void** model);
+int tb_b200_tbm_config(const void* model, TbB200TbmConfig* cfg);
+int tb_b200_tbm_count(const void* model, int* count);
+/* Index of the tensor named `name` (tb_model_find_layer), or
+ * TB_ERR_LAYER_NOT_FOUND. */
+int tb_b200_tbm_find(const void* model, const char* name, int* index);
+int tb_b200_tbm_tensor(const void* model, int index, TbB200TbmTensor* out);
+/* A device-runner description of the loaded model, as TransformerRunner
+ * finds its tensors (include/tensorbit/run/ops.hpp:61-116, 259-276:
+ * llama, gpt-j and bare names; the lm head falls back to the embedding) with
+ * its normalised config (ops.hpp:291-323).  `layers` receives the per-layer
+ * descriptions (capacity max_layers); the weights are borrowed from the
+ * loaded model, which must outlive any runner made from it.  Norm weights
+ * must be f32 (TB_ERR_UNSUPPORTED_DTYPE otherwise). */
+int tb_b200_tbm_runner_desc(const void* model, int attention, int use_graph,
+                            TbB200RunnerDesc* desc, TbB200RunnerLayer* layers, int max_layers);
+int tb_b200_tbm_free(void* model);
+
+/* ======================================================================
  * Multi-GPU (one process per GPU)
  * ====================================================================== */
 

@@ -182,6 +182,11 @@ int tb_dispatch_layer_chain(TbTensor* y, TbTensor* h_out, TbTensor* act, const T
  * fallback inside the backend).  Idempotent. */
 int tb_backend_b200_init(void);
 
+/* The engine's CPU backend init (backend.h:143-148, defined in
+ * src/backend/cpu/registry.c:63-84): declared here because this header
+ * replaces backend.h; the engine defines it, this library does not. */
+int tb_backend_cpu_init(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -5,7 +5,7 @@
 //   m = max x (strict '>', from -inf);  e_i = expf(x_i - m);
 //   sum = ((e_0 + e_1) + e_2) + ...  (f32, in order);  y_i = e_i * (1.0f/sum) if sum > 0.
 // Here e_i = 2^fma(x_i, log2(e), -m*log2(e)) on the MUFU pipe (one expression
-// everywhere, so every pass sees the same bits; within a few ulp of expf).
+// everywhere, so every pass sees the same bits; see Expo for its accuracy).
 // The sum is the in-order f32 sum of those e_i, bit for bit: the integer-
 // grid argument of ordered_sum.cuh, applied per 256-term tile.
 //
@@ -177,14 +177,18 @@ __device__ __forceinline__ void work_sync() {
 }
 
 // ---------------------------------------------------------------- e and D
-// e = 2^(x*log2(e) - m*log2(e)): c = -m*log2(e).  When m*log2(e) is not
-// finite (|m| > 2.3e38) the row uses 2^((x - m)*log2(e)) instead.
+// e = 2^fma(x, log2(e), c) with c = rn(-m*log2(e)): one FFMA.  c carries
+// an absolute rounding error of up to ulp(m*log2(e))/2, the same for every
+// term of the row (a common factor that cancels in e / sum); below
+// |m*log2(e)| = 128 it is at most 2^-17.  Rows with a larger max (or no
+// finite max) use 2^((x - m)*log2(e)) instead, whose error is relative to
+// x - m.
 struct Expo {
     float c, m;
     bool slow;
     __device__ __forceinline__ explicit Expo(float mx) : m(mx) {
         c = __fmul_rn(-mx, kLog2e);
-        slow = !(fabsf(c) <= 3.0e38f) && (mx == mx);
+        slow = !(fabsf(c) < 128.0f);
     }
     __device__ __forceinline__ float operator()(float x) const {
         const float a = slow ? __fmul_rn(__fsub_rn(x, m), kLog2e) : __fmaf_rn(x, kLog2e, c);

@@ -94,6 +94,20 @@ class RunnerDesc(C.Structure):  # TbB200RunnerDesc
         ("norm_eps", f32), ("rope_theta", f32), ("attention", i32), ("use_graph", i32),
         ("embed", Weight), ("final_norm", vp), ("lm_head", Weight), ("layer", P(RunnerLayer))]
 
+class TbmConfig(C.Structure):  # TbB200TbmConfig
+    _fields_ = [("architecture", C.c_char * 64)] + [
+        (n, i32) for n in ("hidden_size", "num_heads", "num_kv_heads", "intermediate_size",
+                           "vocab_size", "max_seq_len", "num_layers")] + [
+        ("norm_eps", f32), ("rope_theta", f32), ("head_dim", i32)]
+
+
+class TbmTensor(C.Structure):  # TbB200TbmTensor
+    _fields_ = [("name", C.c_char * 128), ("shape", i64 * 2), ("dtype", i32),
+                ("nm_n", C.c_uint32), ("nm_m", C.c_uint32), ("num_weights", i64),
+                ("num_mask_bytes", i64), ("scale_count", i64), ("group_size", C.c_uint32),
+                ("weights", vp), ("mask", vp), ("scales", vp), ("weight_bytes", i64)]
+
+
 # name -> (restype, argtypes); every entry point of include/tb_b200.h and tb_backend.h.
 SIGNATURES = {
     "tb_b200_version": (i32, []),
@@ -148,6 +162,13 @@ SIGNATURES = {
     "tb_b200_runner_stream": (i32, [vp, P(vp)]),
     "tb_b200_runner_launches_per_token": (i32, [vp, P(i32)]),
     "tb_b200_runner_destroy": (i32, [vp]),
+    "tb_b200_tbm_load": (i32, [C.c_char_p, vp, P(vp)]),
+    "tb_b200_tbm_config": (i32, [vp, P(TbmConfig)]),
+    "tb_b200_tbm_count": (i32, [vp, P(i32)]),
+    "tb_b200_tbm_find": (i32, [vp, C.c_char_p, P(i32)]),
+    "tb_b200_tbm_tensor": (i32, [vp, i32, P(TbmTensor)]),
+    "tb_b200_tbm_runner_desc": (i32, [vp, i32, i32, P(RunnerDesc), P(RunnerLayer), i32]),
+    "tb_b200_tbm_free": (i32, [vp]),
     "tb_b200_partition": (i32, [i64, i32, i32, P(i64), P(i64)]),
     "tb_b200_shard_plan": (i32, [i64, i64, i32, i32, vp, vp, vp, vp, vp, vp, vp, P(i64)]),
     "tb_b200_comm_unique_id": (i32, [vp]),
@@ -684,6 +705,18 @@ class Runner:
         # host arrays were copied during create; device tensors stay borrowed
         self._keep = [a for a in self._keep if hasattr(a, "data_ptr")]
 
+    @classmethod
+    def from_desc(cls, desc, vocab, keep=()):
+        """A runner from a filled RunnerDesc (e.g. tb_b200_tbm_runner_desc);
+        `keep` holds whatever the descriptor points into."""
+        self = cls.__new__(cls)
+        self._keep = list(keep)
+        self.vocab = int(vocab)
+        h = vp()
+        check(lib().tb_b200_runner_create(C.byref(desc), C.byref(h)), "runner_create")
+        self._h = h
+        return self
+
     def forward(self, token):
         """Run one token; returns the device logits address (valid until the
         next forward)."""
@@ -721,6 +754,58 @@ class Runner:
     def close(self):
         if getattr(self, "_h", None):
             lib().tb_b200_runner_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class TbmModel:
+    """A .tbm container read into device memory (tb_b200_tbm_load)."""
+
+    def __init__(self, path, stream=None):
+        h = vp()
+        check(lib().tb_b200_tbm_load(str(path).encode(), stream or cur_stream(), C.byref(h)),
+              "tbm_load")
+        self._h = h
+
+    def config(self) -> TbmConfig:
+        c = TbmConfig()
+        check(lib().tb_b200_tbm_config(self._h, C.byref(c)), "tbm_config")
+        return c
+
+    def __len__(self):
+        n = i32()
+        check(lib().tb_b200_tbm_count(self._h, C.byref(n)), "tbm_count")
+        return n.value
+
+    def tensor(self, i):
+        """(return code, TbmTensor) of tensor i: TB_OK, or TB_ERR_BAD_MAGIC
+        for a tensor whose .tb header is not one."""
+        t = TbmTensor()
+        rc = lib().tb_b200_tbm_tensor(self._h, i, C.byref(t))
+        return rc, t
+
+    def find(self, name):
+        i = i32()
+        rc = lib().tb_b200_tbm_find(self._h, name.encode(), C.byref(i))
+        return i.value if rc == 0 else -1
+
+    def runner(self, attention=ATTN_REFERENCE, use_graph=True, max_layers=512):
+        """A device runner over this model's tensors (borrowed: the model
+        must stay open while the runner lives)."""
+        layers = (RunnerLayer * max_layers)()
+        d = RunnerDesc()
+        check(lib().tb_b200_tbm_runner_desc(self._h, attention, 1 if use_graph else 0,
+                                            C.byref(d), layers, max_layers), "tbm_runner_desc")
+        return Runner.from_desc(d, d.vocab, keep=(layers, self))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            check(lib().tb_b200_tbm_free(self._h), "tbm_free")
             self._h = None
 
     def __del__(self):

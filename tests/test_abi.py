@@ -42,8 +42,13 @@ def test_library_loads_and_reports_version():
     assert T.lib().tb_b200_version() == 1
 
 
+# Declared for the engine (tb_backend.h replaces its backend.h) but defined
+# by the engine itself, not by this library.
+ENGINE_DEFINED = {"tb_backend_cpu_init"}
+
+
 def test_every_declared_function_is_exported():
-    decl = declared_functions()
+    decl = declared_functions() - ENGINE_DEFINED
     assert len(decl) > 60
     missing = decl - exported_functions()
     assert not missing, f"declared but not exported: {sorted(missing)}"
@@ -329,3 +334,92 @@ def test_library_before_torch_keeps_torch_importable():
             "print(torch.__version__)" % os.path.join(ROOT, "tensorbit-run_b200"))
     out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
     assert out.returncode == 0, out.stderr[-2000:]
+
+
+PIN_REGISTRY_SO = os.path.join(ROOT, "oracle", "_ref", "libpinregistry.so")
+
+
+@pytest.mark.skipif(not os.path.exists(PIN_REGISTRY_SO), reason="oracle/_ref not built here")
+def test_engine_backend_registry_builds_against_the_b200_header():
+    """The engine's own C++ registry (BackendRegistry, backend.hpp:19-53,
+    unmodified) compiled with include/tb_backend.h in place of backend.h and
+    its accelerator branch bound to tb_backend_b200_init, linked to
+    libtb_b200.so (oracle/_ref/libpinregistry.so).  Its init registers "cpu"
+    and "b200"; device-aware routing picks "b200" for CUDA tensors and
+    "cpu" for host tensors; the engine's C++ rms_norm wrapper on host
+    tensors reaches the reference's CPU kernel.  In a fresh process: the
+    registry is a process-wide singleton."""
+    import subprocess
+    import sys
+    code = r'''
+import ctypes as C, sys
+import numpy as np
+sys.path[:0] = sys.argv[2:4]
+import tb_b200 as T
+from oracle import oracle as O
+L = C.CDLL(sys.argv[1])
+L.pin_registry_best.restype = C.c_char_p
+L.pin_registry_has.argtypes = [C.c_char_p]
+L.pin_registry_rms_norm_host.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_float]
+assert L.pin_registry_init() == 2
+assert L.pin_registry_init() == 2  # init is once per process
+assert L.pin_registry_has(b"cpu") and L.pin_registry_has(b"b200")
+for op in ("RMS_NORM", "RESIDUAL_ADD", "GELU", "SILU", "SOFTMAX", "ROPE", "EMBEDDING"):
+    assert L.pin_registry_best(T.OP[op], 1) == b"b200", op
+    assert L.pin_registry_best(T.OP[op], 0) == b"cpu", op
+for op in ("RESIDUAL_RMS_NORM", "SWIGLU", "ARGMAX", "ROPE_ROWS", "LAYER_CHAIN"):
+    assert L.pin_registry_best(T.OP[op], 1) == b"b200", op
+assert L.pin_registry_best(T.OP["LAYER_NORM"], 1) == b"cpu"  # no b200 slot: the cpu one
+rng = np.random.default_rng(9)
+x = rng.standard_normal(4096).astype(np.float32)
+w = (1 + 0.1 * rng.standard_normal(4096)).astype(np.float32)
+y = np.zeros_like(x)
+assert L.pin_registry_rms_norm_host(y.ctypes.data, x.ctypes.data, w.ctypes.data, x.size, 1e-5) == 0
+assert np.array_equal(y, O.rms_norm_vec(x, w, 1e-5))
+print("ok")
+'''
+    out = subprocess.run([sys.executable, "-c", code, PIN_REGISTRY_SO, ROOT,
+                          os.path.join(ROOT, "tensorbit-run_b200")],
+                         capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0 and out.stdout.strip().endswith("ok"), out.stderr[-3000:]
+
+
+def test_tbm_load_rejects_bad_files_before_device_work(tmp_path):
+    """tb_b200_tbm_load checks the container before it touches a device, as
+    tb_model_load_tbm does (src/model.c:482-545): a missing file
+    (TB_ERR_FILE_OPEN 1), a file too short or whose index length does not fit
+    (TB_ERR_TRUNCATED 11), an index that is not JSON (TB_ERR_JSON_PARSE 13),
+    and a tensor header or tensor bytes past the end of the file (11)."""
+    import json
+    import struct
+    L = T.lib()
+    h = C.c_void_p()
+
+    def load(p):
+        return L.tb_b200_tbm_load(str(p).encode(), None, C.byref(h))
+
+    assert load(tmp_path / "missing.tbm") == 1
+    (tmp_path / "short.tbm").write_bytes(b"x" * 10)
+    assert load(tmp_path / "short.tbm") == 11
+    (tmp_path / "len.tbm").write_bytes(b"\0" * 60 + struct.pack("<I", 1000))
+    assert load(tmp_path / "len.tbm") == 11
+    js = b"{not json"
+    (tmp_path / "json.tbm").write_bytes(b"\0" * 64 + js + struct.pack("<I", len(js)))
+    assert load(tmp_path / "json.tbm") == 13
+
+    def container(tensors, body=b""):
+        js = json.dumps({"architecture": "llama", "config": {"hidden_size": 8},
+                         "tensors": tensors}).encode()
+        return body + js + struct.pack("<I", len(js))
+
+    t = {"name": "a", "offset": 10 ** 6, "shape": [2, 2], "dtype": "fp32", "num_weights": 4,
+         "num_mask_bytes": 0}
+    (tmp_path / "off.tbm").write_bytes(container([t]))
+    assert load(tmp_path / "off.tbm") == 11
+    hdr = struct.pack("<IIIIQQQQB", 0x31304254, 1, 0, 0, 4, 0, 4096, 4096 + 16, 0)
+    hdr += b"\0" * (4096 - len(hdr))
+    t = dict(t, offset=0, num_weights=10 ** 7)  # 40 MB of weights in a 4 KB file
+    (tmp_path / "big.tbm").write_bytes(container([t], hdr + b"\0" * 16))
+    assert load(tmp_path / "big.tbm") == 11
+    assert not h.value
+    assert L.tb_b200_tbm_load(None, None, C.byref(h)) == 8
