@@ -1453,11 +1453,16 @@ def main():
                          "bandwidth sweep")
     ap.add_argument("--rows", type=int, default=None,
                     help="layer-op rows (70b: of the whole job; else per GPU; config's)")
+    ap.add_argument("--logit-rows", type=int, default=None,
+                    help="softmax/argmax rows (70b: of the whole job; 4096) -- for small ncu "
+                         "captures")
     ap.add_argument("--runner-layers", type=int, default=RUNNER_LAYERS,
                     help="layers of the runner configs' model (32; fewer for small ncu captures)")
     args = ap.parse_args()
     global CFG, LOGIT_ROWS, WORKLOAD
     CFG, LOGIT_ROWS, WORKLOAD = CONFIGS[args.config]
+    if args.logit_rows is not None:
+        LOGIT_ROWS = args.logit_rows
     if args.rows is None:
         args.rows = CFG.rows
     args.warmup = max(args.warmup, 3)

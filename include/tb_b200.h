@@ -402,9 +402,11 @@ int tb_b200_runner_destroy(void* runner);
  * ====================================================================== */
 
 /* The model config of a .tbm index, the reference's TbModelConfig
- * (include/tensorbit/run/model.h:34-46) with its parser's defaults
- * (src/model.c:280-341): norm_eps 1e-6 and rope_theta 10000 when absent,
- * num_kv_heads = num_heads when 0, head_dim = hidden_size / num_heads. */
+ * (include/tensorbit/run/model.h:34-46), read as its parser reads it
+ * (src/model.c:280-475): a "config" object clears the whole config (an
+ * "architecture" read before it included), defaults norm_eps to 1e-6 and
+ * rope_theta to 10000, sets num_kv_heads = num_heads when 0 and head_dim =
+ * hidden_size / num_heads; without one every field is 0. */
 typedef struct {
     char architecture[64];
     int hidden_size, num_heads, num_kv_heads, intermediate_size, vocab_size, max_seq_len,

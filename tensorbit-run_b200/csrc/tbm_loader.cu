@@ -61,11 +61,6 @@ struct JVal {
     std::string str;
     std::vector<JVal> arr;
     std::vector<std::pair<std::string, JVal>> obj;
-    const JVal* get(const char* k) const {
-        for (const auto& kv : obj)
-            if (kv.first == k) return &kv.second;
-        return nullptr;
-    }
 };
 
 struct JParser {
@@ -216,65 +211,91 @@ struct Mapping {
     }
 };
 
-// The JSON index into `m` (config and tensor descriptors), with the
-// reference's defaults (src/model.c:280-341, 474).
+// The JSON index into `m` (config and tensor descriptors), read as the
+// reference reads it (src/model.c:280-475): the top-level keys in file
+// order, a repeated key read again; "config" first clears the whole config
+// -- the architecture read before it included -- then sets norm_eps 1e-6
+// and rope_theta 10000, reads its fields, and makes num_kv_heads =
+// num_heads when 0 and head_dim = hidden_size / num_heads.  Without a
+// "config" key every field stays 0.  Within a tensor the last of a
+// repeated field wins; at most kMaxTensors tensors are read.
 int parse_index(const JVal& root, TbmModel& m) {
     if (root.kind != JVal::kObj) return TB_ERR_JSON_PARSE;
     TbB200TbmConfig& c = m.cfg;
     memset(&c, 0, sizeof c);
-    c.norm_eps = 1e-6f;
-    c.rope_theta = 10000.0f;
-    if (const JVal* a = root.get("architecture")) {
-        if (a->kind != JVal::kStr) return TB_ERR_JSON_PARSE;
-        strncpy(c.architecture, a->str.c_str(), sizeof c.architecture - 1);
-    }
-    if (const JVal* cf = root.get("config")) {
-        if (cf->kind != JVal::kObj) return TB_ERR_JSON_PARSE;
-        c.hidden_size = (int)jint(cf->get("hidden_size"));
-        c.num_heads = (int)jint(cf->get("num_heads"));
-        c.num_kv_heads = (int)jint(cf->get("num_kv_heads"));
-        c.intermediate_size = (int)jint(cf->get("intermediate_size"));
-        c.vocab_size = (int)jint(cf->get("vocab_size"));
-        c.num_layers = (int)jint(cf->get("num_layers"));
-        c.max_seq_len = (int)jint(cf->get("max_seq_len"));
-        c.norm_eps = (float)jnum(cf->get("norm_eps"), 1e-6);
-        c.rope_theta = (float)jnum(cf->get("rope_theta"), 10000.0);
-        if (c.num_kv_heads == 0) c.num_kv_heads = c.num_heads;
-        c.head_dim = c.num_heads > 0 ? c.hidden_size / c.num_heads : 0;
-    }
-    const JVal* ts = root.get("tensors");
-    if (ts) {
-        if (ts->kind != JVal::kArr) return TB_ERR_JSON_PARSE;
-        for (const JVal& tv : ts->arr) {
-            if ((int)m.recs.size() >= kMaxTensors) break;
-            if (tv.kind != JVal::kObj) return TB_ERR_JSON_PARSE;
-            Rec r;
-            memset(&r.t, 0, sizeof r.t);
-            if (const JVal* n = tv.get("name")) strncpy(r.t.name, n->str.c_str(), sizeof r.t.name - 1);
-            r.w_off = (uint64_t)jint(tv.get("offset"));
-            if (const JVal* sh = tv.get("shape")) {
-                if (sh->kind != JVal::kArr) return TB_ERR_JSON_PARSE;
-                for (size_t i = 0; i < sh->arr.size() && i < 2; ++i) r.t.shape[i] = jint(&sh->arr[i]);
+    for (const auto& kv : root.obj) {
+        const std::string& key = kv.first;
+        const JVal& v = kv.second;
+        if (key == "architecture") {
+            if (v.kind != JVal::kStr) return TB_ERR_JSON_PARSE;
+            memset(c.architecture, 0, sizeof c.architecture);
+            strncpy(c.architecture, v.str.c_str(), sizeof c.architecture - 1);
+        } else if (key == "config") {
+            if (v.kind != JVal::kObj) return TB_ERR_JSON_PARSE;
+            memset(&c, 0, sizeof c);
+            c.norm_eps = 1e-6f;
+            c.rope_theta = 10000.0f;
+            for (const auto& f : v.obj) {
+                const JVal* x = &f.second;
+                if (f.first == "hidden_size") c.hidden_size = (int)jint(x);
+                else if (f.first == "num_heads") c.num_heads = (int)jint(x);
+                else if (f.first == "num_kv_heads") c.num_kv_heads = (int)jint(x);
+                else if (f.first == "intermediate_size") c.intermediate_size = (int)jint(x);
+                else if (f.first == "vocab_size") c.vocab_size = (int)jint(x);
+                else if (f.first == "num_layers") c.num_layers = (int)jint(x);
+                else if (f.first == "max_seq_len") c.max_seq_len = (int)jint(x);
+                else if (f.first == "norm_eps") c.norm_eps = (float)jnum(x, 0.0);
+                else if (f.first == "rope_theta") c.rope_theta = (float)jnum(x, 0.0);
             }
-            r.t.nm_n = (uint32_t)jint(tv.get("nm_n"));
-            r.t.nm_m = (uint32_t)jint(tv.get("nm_m"));
-            r.t.dtype = TB_DTYPE_F32;  // memset default of the reference's descriptor
-            if (const JVal* d = tv.get("dtype")) {
-                const std::string& s = d->str;
-                if (s == "fp32") r.t.dtype = TB_DTYPE_F32;
-                else if (s == "fp16") r.t.dtype = TB_DTYPE_F16;
-                else if (s == "bf16") r.t.dtype = TB_DTYPE_BF16;
-                else if (s == "fp64") r.t.dtype = TB_DTYPE_F64;
-                else if (s == "int8") r.t.dtype = TB_DTYPE_INT8;
-                else if (s == "int4") r.t.dtype = TB_DTYPE_INT4;
+            if (c.num_kv_heads == 0) c.num_kv_heads = c.num_heads;
+            c.head_dim = c.num_heads > 0 ? c.hidden_size / c.num_heads : 0;
+        } else if (key == "tensors") {
+            if (v.kind != JVal::kArr) return TB_ERR_JSON_PARSE;
+            m.recs.clear();
+            for (const JVal& tv : v.arr) {
+                if ((int)m.recs.size() >= kMaxTensors) break;
+                if (tv.kind != JVal::kObj) return TB_ERR_JSON_PARSE;
+                Rec r;
+                memset(&r.t, 0, sizeof r.t);
+                r.t.dtype = TB_DTYPE_F32;  // the zeroed descriptor's dtype
+                for (const auto& f : tv.obj) {
+                    const JVal* x = &f.second;
+                    if (f.first == "name") {
+                        memset(r.t.name, 0, sizeof r.t.name);
+                        if (x->kind == JVal::kStr)
+                            strncpy(r.t.name, x->str.c_str(), sizeof r.t.name - 1);
+                    } else if (f.first == "offset") {
+                        r.w_off = (uint64_t)jint(x);
+                    } else if (f.first == "shape") {
+                        if (x->kind != JVal::kArr) return TB_ERR_JSON_PARSE;
+                        for (size_t i = 0; i < x->arr.size() && i < 2; ++i)
+                            r.t.shape[i] = jint(&x->arr[i]);
+                    } else if (f.first == "nm_n") {
+                        r.t.nm_n = (uint32_t)jint(x);
+                    } else if (f.first == "nm_m") {
+                        r.t.nm_m = (uint32_t)jint(x);
+                    } else if (f.first == "dtype") {
+                        const std::string& d = x->str;
+                        if (d == "fp32") r.t.dtype = TB_DTYPE_F32;
+                        else if (d == "fp16") r.t.dtype = TB_DTYPE_F16;
+                        else if (d == "bf16") r.t.dtype = TB_DTYPE_BF16;
+                        else if (d == "fp64") r.t.dtype = TB_DTYPE_F64;
+                        else if (d == "int8") r.t.dtype = TB_DTYPE_INT8;
+                        else if (d == "int4") r.t.dtype = TB_DTYPE_INT4;
+                    } else if (f.first == "num_weights") {
+                        r.t.num_weights = jint(x);
+                    } else if (f.first == "num_mask_bytes") {
+                        r.t.num_mask_bytes = jint(x);
+                    } else if (f.first == "scale_count") {
+                        r.t.scale_count = jint(x);
+                    } else if (f.first == "group_size") {
+                        r.t.group_size = (uint32_t)jint(x);
+                    }
+                }
+                if (r.t.num_weights < 0 || r.t.num_mask_bytes < 0 || r.t.scale_count < 0)
+                    return TB_ERR_JSON_PARSE;
+                m.recs.push_back(r);
             }
-            r.t.num_weights = jint(tv.get("num_weights"));
-            r.t.num_mask_bytes = jint(tv.get("num_mask_bytes"));
-            r.t.scale_count = jint(tv.get("scale_count"));
-            r.t.group_size = (uint32_t)jint(tv.get("group_size"));
-            if (r.t.num_weights < 0 || r.t.num_mask_bytes < 0 || r.t.scale_count < 0)
-                return TB_ERR_JSON_PARSE;
-            m.recs.push_back(r);
         }
     }
     if (c.num_layers == 0 && !m.recs.empty()) c.num_layers = 1;
