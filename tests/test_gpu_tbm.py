@@ -95,17 +95,21 @@ def assert_logits(got, want, tol=TOL):
         assert err <= tol * np.abs(want[t]).max(), f"token {t}: max err {err:.3e}"
 
 
-def test_f32_model_written_by_the_reference(dev, tmp_path):
-    """The engine's mock shape with random 2:4 masks, written by the
-    reference's tb_tbm_create; GQA and random norm weights."""
-    cfg, model = mock(seed=61, masks="rand", norms="rand", heads=8, kv=2)
+@pytest.mark.parametrize("kv", [8, 2])
+def test_f32_model_written_by_the_reference(dev, tmp_path, kv):
+    """The engine's mock shape with random 2:4 masks and random norm
+    weights, written by the reference's tb_tbm_create.  With kv < heads
+    (GQA) the reference runner reads past k and v at position 0
+    (ops.hpp:176), so only the device runners are compared there."""
+    cfg, model = mock(seed=61, masks="rand", norms="rand", heads=8, kv=kv)
     path = tmp_path / "mock.tbm"
     F.write_ref(path, cfg, model)
     m = compare_with_reference(path)
     toks = np.random.default_rng(3).integers(0, cfg["vocab"], 24).astype(np.int32)
     got = logits_of(m.runner(), toks)
     assert np.array_equal(got, logits_of(T.Runner(cfg, model), toks))
-    assert_logits(got, F.ref_runner(path, toks, cfg["vocab"]))
+    if kv == cfg["n_heads"]:
+        assert_logits(got, F.ref_runner(path, toks, cfg["vocab"]))
     m.close()
 
 
