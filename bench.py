@@ -7,9 +7,11 @@ scaled: the token rows, the logit rows and the embedding table's vocabulary
 rows are split over the N ranks (tb_b200_partition).
   embedding gather          16384 ids -> rows of a [128256, 8192] bf16 table,
                             vocab-sharded: each rank holds 128256/N table
-                            rows and gathers its token part with the NCCL
-                            exchange (tb_b200_embedding_sharded); the one-
-                            kernel peer-memory gather (..._sharded_p2p) is
+                            rows in NCCL symmetric memory and gathers its
+                            token part in one kernel that loads rows from
+                            the owners' windows
+                            (tb_b200_embedding_sharded_window); the NCCL
+                            send/recv exchange and the CUDA IPC gather are
                             timed beside the step
   residual + RMSNorm        [16384/N, 8192]                   } one fused
   RoPE on Q and K           [16384/N, 64 | 8, 128], pos % 2048 } layer-chain
@@ -956,8 +958,9 @@ def run_sharded(args, rank, world, local):
     rows tb_b200_partition(16384, world, r), logit rows
     tb_b200_partition(4096, world, r) and table rows
     tb_b200_partition(128256, world, r).  The embedding gather is the
-    library's NCCL exchange over its own communicator (one grouped
-    send/recv per step); every other op is local to the rank."""
+    library's one-kernel gather over its communicator's symmetric memory
+    (NCCL windows; the NCCL send/recv exchange and the CUDA IPC gather are
+    timed beside it); every other op is local to the rank."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -996,6 +999,14 @@ def run_sharded(args, rank, world, local):
     ids = np.random.default_rng(c.seed + 8).integers(0, c.vocab, NT).astype(np.int32)
     table_seed = c.seed + 700
     shard = table_shard(torch, dev, c, vlo, vhi, table_seed)
+    # The table part in the communicator's symmetric memory: every rank's
+    # window has the size of the largest part.
+    win_bytes = -(-c.vocab // world) * c.hidden * 2
+    win = T.comm_window_alloc(win_bytes)
+    T.check(L.tb_b200_memcpy_d2d(C.c_void_p(win), T.ptr(shard), shard.numel() * 2, None), "d2d")
+    torch.cuda.synchronize()
+    barrier()  # every part written before any rank gathers
+    my_ids = torch.from_numpy(ids[tlo:thi]).to(dev)
     g = torch.Generator(device=dev)
     base = 12345 + 1000 * rank
 
@@ -1026,9 +1037,9 @@ def run_sharded(args, rank, world, local):
                          t["pos"], c.theta, rope, t["gate"], t["up"], o["act"])
     ids_p = ids.ctypes.data
     ops = {
-        "embedding": lambda: T.check(L.tb_b200_embedding_sharded(
-            T.BF16, NT, c.hidden, c.vocab, ids_p, T.ptr(shard), T.ptr(o["emb"]), sp),
-            "embedding_sharded"),
+        "embedding": lambda: T.check(L.tb_b200_embedding_sharded_window(
+            T.BF16, R, c.hidden, c.vocab, T.ptr(my_ids), C.c_void_p(win), T.ptr(o["emb"]), sp),
+            "embedding_sharded_window"),
         "layer_chain": lambda: T.check(L.tb_b200_layer_chain(C.byref(chain), sp), "layer_chain"),
         "softmax": lambda: T.check(L.tb_b200_softmax(T.F32, LR, c.vocab, T.ptr(t["logits_s"]),
                                                      None, T.ptr(o["probs"]), sp), "softmax"),
@@ -1044,6 +1055,7 @@ def run_sharded(args, rank, world, local):
         for _ in range(args.warmup + args.steps):
             ops[args.profile_op]()
         torch.cuda.synchronize()
+        barrier()
         T.comm_destroy()
         return None
 
@@ -1082,8 +1094,9 @@ def run_sharded(args, rank, world, local):
                  for n in names}
     barrier()
 
-    # the same gather as one kernel over peer memory (no collective), timed
-    # alone: this rank's rows read straight from the owners' shards
+    # The same gather two other ways, each timed alone: the NCCL exchange
+    # (host ids, a host plan, pack, grouped send/recv, scatter) and one
+    # kernel over CUDA IPC mappings of the other ranks' parts.
     if world > 1:
         handles = [None] * world
         dist.all_gather_object(handles, T.p2p_export(shard))
@@ -1091,32 +1104,42 @@ def run_sharded(args, rank, world, local):
                  for r in range(world)]
     else:
         handles, addrs = None, [shard.data_ptr()]
-    my_ids = torch.from_numpy(ids[tlo:thi]).to(dev)
     y_p2p = torch.empty_like(o["emb"])
+    y_nccl = torch.empty_like(o["emb"])
     darr = (C.c_void_p * world)(*addrs)
 
     def p2p():
         T.check(L.tb_b200_embedding_sharded_p2p(T.BF16, R, c.hidden, c.vocab, T.ptr(my_ids), darr,
                                                 world, T.ptr(y_p2p), sp), "embedding_sharded_p2p")
 
-    for _ in range(3):
-        p2p()
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    n_p2p = max(5, min(args.steps, 20))
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(stream)
-    for _ in range(n_p2p):
-        p2p()
-    b.record(stream)
-    b.synchronize()
-    p2p_ms = max_over_ranks(a.elapsed_time(b)) / n_p2p
-    # both gathers against each other and against the table itself: a sample
-    # of token rows regenerated from their chunk's seed
+    def nccl():
+        T.check(L.tb_b200_embedding_sharded(T.BF16, NT, c.hidden, c.vocab, ids_p, C.c_void_p(win),
+                                            T.ptr(y_nccl), sp), "embedding_sharded")
+
+    def time_alone(f, n):
+        for _ in range(3):
+            f()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(n):
+            f()
+        b.record(stream)
+        b.synchronize()
+        return max_over_ranks(a.elapsed_time(b)) / n
+
+    n_side = max(5, min(args.steps, 20))
+    win_ms = time_alone(ops["embedding"], n_side)
+    p2p_ms = time_alone(p2p, n_side)
+    nccl_ms = time_alone(nccl, n_side)
+    # all three gathers against each other and against the table itself: a
+    # sample of token rows regenerated from their chunk's seed
     ops["embedding"]()
     torch.cuda.synchronize()
-    same = bool(torch.equal(o["emb"].view(torch.int16), y_p2p.view(torch.int16)))
+    as16 = lambda t: t.view(torch.int16)  # noqa: E731
+    same = bool(torch.equal(as16(o["emb"]), as16(y_p2p)) and torch.equal(as16(o["emb"]), as16(y_nccl)))
     rs = np.random.default_rng(11 + rank)
     sample = sorted(set(rs.integers(0, R, 8).tolist()) | {0, R - 1}) if R else []
     by_chunk = {}
@@ -1126,8 +1149,8 @@ def run_sharded(args, rank, world, local):
         lo_, hi_ = j * TABLE_CHUNK, min((j + 1) * TABLE_CHUNK, c.vocab)
         chunk = table_shard(torch, dev, c, lo_, hi_, table_seed)
         for r_ in rows_:
-            same = same and bool(torch.equal(o["emb"][r_].view(torch.int16),
-                                             chunk[int(ids[tlo + r_]) - lo_].view(torch.int16)))
+            same = same and bool(torch.equal(as16(o["emb"][r_]),
+                                              as16(chunk[int(ids[tlo + r_]) - lo_])))
         del chunk
     verified = max_over_ranks(0.0 if same else 1.0) == 0.0
     if world > 1:
@@ -1152,7 +1175,7 @@ def run_sharded(args, rank, world, local):
         host_in[n].copy_(t[n])
     host_out = {n: torch.empty_like((o.get(n) if n in o else t[n]), device="cpu").pin_memory()
                 for n in outs}
-    bi = sum(host_in[n].numel() * host_in[n].element_size() for n in ins) + ids.nbytes
+    bi = sum(host_in[n].numel() * host_in[n].element_size() for n in ins) + 4 * R
     bo = sum(host_out[n].numel() * host_out[n].element_size() for n in outs)
     nb = E2E_BLOCKS if R % E2E_BLOCKS == 0 and LR % E2E_BLOCKS == 0 else 1
     rb, lrb = R // nb, LR // nb
@@ -1172,11 +1195,16 @@ def run_sharded(args, rank, world, local):
                           sl["k"], sl["pos"], c.theta, rope, sl["gate"], sl["up"], sl["act"])
         blocks.append((span, sl, ch))
 
+    ids_host = torch.from_numpy(ids[tlo:thi].copy()).pin_memory()
+
     def e2e_step():
         main = torch.cuda.current_stream()
         for st in streams:
             st.wait_stream(main)
-        ops["embedding"]()  # host ids in, on the main stream
+        # this rank's ids in, then the gather, on the main stream
+        T.check(L.tb_b200_memcpy_h2d(T.ptr(my_ids), C.c_void_p(ids_host.data_ptr()), R * 4, sp),
+                "h2d")
+        ops["embedding"]()
         gathered = torch.cuda.Event()
         gathered.record(main)
         for j, (span, sl, ch) in enumerate(blocks):
@@ -1211,7 +1239,9 @@ def run_sharded(args, rank, world, local):
     b.record(stream)
     b.synchronize()
     e2e_ms = max_over_ranks(a.elapsed_time(b)) / e2e_steps
+    torch.cuda.synchronize()
     barrier()
+    T.comm_window_free(win)
     T.comm_destroy()
 
     parts = step_bytes(NT, 2, NLG)  # the whole job's algorithmic bytes
@@ -1238,21 +1268,27 @@ def run_sharded(args, rank, world, local):
                    "logits": "f32", "bytes_per_step": total_bytes,
                    "l2": f"inputs larger than L2: {sum(mine.values()) / 1e9:.2f} GB of distinct "
                          "buffers per step per GPU",
-                   "parallelism": f"rows and vocab sharded x{world}; NCCL exchange in the "
-                                  "embedding gather only"},
+                   "parallelism": f"rows and vocab sharded x{world}; the embedding gather "
+                                  "reads peers' table parts through NCCL symmetric memory"},
         "rows_per_s": round(NT / (ms / 1e3), 1),
         "per_op": per_op,
         "largest_share": dom,
-        "gather": {"nccl_ms": round(per_op_ms["embedding"], 4), "p2p_ms": round(p2p_ms, 4),
+        "gather": {"in_step": "one kernel over NCCL symmetric memory "
+                              "(tb_b200_embedding_sharded_window)",
+                   "window_ms": round(win_ms, 4), "nccl_sendrecv_ms": round(nccl_ms, 4),
+                   "ipc_p2p_ms": round(p2p_ms, 4),
                    "rows_per_gpu": R, "row_bytes": c.hidden * 2,
                    "algorithmic_bytes_per_gpu": mine["embedding"],
                    "nvlink_read_bytes_per_gpu_max": int(nvlink_bytes),
-                   "nccl_nvlink_GBps": (round(nvlink_bytes / per_op_ms["embedding"] / 1e6, 1)
-                                        if world > 1 else None),
-                   "p2p_nvlink_GBps": (round(nvlink_bytes / p2p_ms / 1e6, 1)
-                                       if world > 1 else None),
+                   "window_nvlink_GBps": (round(nvlink_bytes / win_ms / 1e6, 1)
+                                          if world > 1 else None),
+                   "nccl_sendrecv_nvlink_GBps": (round(nvlink_bytes / nccl_ms / 1e6, 1)
+                                                 if world > 1 else None),
+                   "ipc_p2p_nvlink_GBps": (round(nvlink_bytes / p2p_ms / 1e6, 1)
+                                           if world > 1 else None),
                    "bit_exact": verified,
-                   "check": "NCCL and P2P outputs equal; sampled rows equal the table rows"},
+                   "check": "window, send/recv and IPC outputs equal; sampled rows equal the "
+                            "table rows"},
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1),
                      "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
                      "frac": round(achieved / peak, 3),

@@ -521,6 +521,33 @@ int tb_b200_embedding_sharded(int dtype, int64_t n_tokens, int64_t dim, int64_t 
                               const int32_t* ids_host, const void* table_shard, void* y_local,
                               void* stream);
 
+/* Symmetric memory of the communicator (NCCL windows): every rank calls
+ * tb_b200_comm_window_alloc with the same size, in the same order, and gets
+ * `bytes` (rounded up to 4 KB) of device memory that NCCL maps into every
+ * other rank's address space; tb_b200_comm_window_free (collective, same
+ * order) releases it, and tb_b200_comm_destroy releases what is left.
+ * TB_ERR_DEVICE when the loaded NCCL has no windows.  Bounded like every
+ * host-side wait on the communicator.  No counterpart in the reference. */
+int tb_b200_comm_window_alloc(size_t bytes, void** ptr);
+int tb_b200_comm_window_free(void* ptr);
+
+/* The vocab-sharded gather as one kernel over the communicator's symmetric
+ * memory: the same computation as tb_b200_embedding_sharded (the
+ * reference's per-token row copy, src/ops/embedding.c:4-14, over a table
+ * split by vocabulary rows), with no exchange step.  Every rank keeps its
+ * table part (tb_b200_partition(vocab, nranks, rank)) at the same byte
+ * offset of a window from tb_b200_comm_window_alloc and passes its own
+ * pointer as `shard`; ids (n_tokens DEVICE int32) are the tokens whose rows
+ * this call writes to y [n_tokens, dim] -- usually this rank's token part.
+ * Each row is read from its owner's window (a peer load over NVLink when the
+ * owner is another GPU; nothing waits on another GPU, the shards being
+ * written before any gather) and written once: bit-exact with
+ * tb_cpu_embedding_f32 over the full table.  Ids outside [0, vocab) give a
+ * zero row and raise TB_B200_FLAG_TOKEN_RANGE. */
+int tb_b200_embedding_sharded_window(int dtype, int64_t n_tokens, int64_t dim, int64_t vocab,
+                                     const int32_t* ids, const void* shard, void* y,
+                                     void* stream);
+
 /* Peer memory of the other GPUs of one box, through CUDA IPC, for the
  * one-kernel sharded gather below.  The owner of a device buffer exports a
  * handle (TB_B200_P2P_HANDLE_BYTES bytes) and the buffer's offset within its

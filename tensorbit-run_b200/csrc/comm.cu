@@ -30,6 +30,7 @@
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 #include <nccl.h>
+#include <nccl_device.h>
 
 #include <mutex>
 
@@ -56,6 +57,11 @@ struct NcclApi {
     ncclResult_t (*GroupEnd)();
     ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
     ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
+    // symmetric memory windows (NCCL 2.27+); null when the NCCL has none
+    ncclResult_t (*MemAlloc)(void**, size_t);
+    ncclResult_t (*MemFree)(void*);
+    ncclResult_t (*WindowRegister)(ncclComm_t, void*, size_t, ncclWindow_t*, int);
+    ncclResult_t (*WindowDeregister)(ncclComm_t, ncclWindow_t);
 };
 
 NcclApi g_nccl;
@@ -85,6 +91,10 @@ bool nccl_api() {
         sym(g_nccl.Send, "ncclSend");
         sym(g_nccl.Recv, "ncclRecv");
         g_nccl_ok = ok;
+        *reinterpret_cast<void**>(&g_nccl.MemAlloc) = dlsym(h, "ncclMemAlloc");
+        *reinterpret_cast<void**>(&g_nccl.MemFree) = dlsym(h, "ncclMemFree");
+        *reinterpret_cast<void**>(&g_nccl.WindowRegister) = dlsym(h, "ncclCommWindowRegister");
+        *reinterpret_cast<void**>(&g_nccl.WindowDeregister) = dlsym(h, "ncclCommWindowDeregister");
     });
     if (!g_nccl_ok) tbh::set_error_text("NCCL (libnccl.so.2) could not be loaded");
     return g_nccl_ok;
@@ -241,6 +251,56 @@ void release_bufs() {
     g_bufs = GatherBufs();
 }
 
+// Symmetric windows made by tb_b200_comm_window_alloc on this process's
+// communicator: NCCL maps every rank's window of a registration into this
+// GPU's address space, so a peer's bytes are a plain load away.
+struct WinRec {
+    char* ptr;
+    size_t bytes;
+    ncclWindow_t win;
+};
+std::vector<WinRec> g_wins;
+
+// One row per warp: row j of y is row ids[j] of the full table, read from
+// its owner's shard through the window (a peer load over NVLink/NVSwitch
+// when the owner is another GPU).  Every rank's shard sits at byte `base`
+// of its window.  Ids outside [0, vocab) zero the row and raise the flag.
+template <typename W>
+__global__ void __launch_bounds__(256)
+k_embed_window(const int32_t* __restrict__ ids, int64_t n, int64_t vocab, int nranks,
+               ncclWindow_t win, size_t base, int64_t words, W* __restrict__ y,
+               unsigned* status) {
+    constexpr int kBatch = 4;
+    const int64_t j = (int64_t)blockIdx.x * 8 + threadIdx.x / 32;
+    if (j >= n) return;
+    const int lane = threadIdx.x & 31;
+    W* d = y + j * words;
+    const int64_t id = ids[j];
+    if (id < 0 || id >= vocab) {
+        for (int64_t i = lane; i < words; i += 32) d[i] = W{};
+        if (lane == 0) atomicOr(status, TB_B200_FLAG_TOKEN_RANGE);
+        return;
+    }
+    const int64_t pb = vocab / nranks, extra = vocab % nranks, big = extra * (pb + 1);
+    const int r = id < big ? (int)(id / (pb + 1)) : (int)(extra + (id - big) / pb);
+    const int64_t lo = (int64_t)r * pb + (r < extra ? r : extra);
+    const W* s = static_cast<const W*>(
+        ncclGetPeerPointer(win, base + (size_t)((id - lo) * words) * sizeof(W), r));
+    int64_t i = lane;
+    for (; i + 32 * (kBatch - 1) < words; i += 32 * kBatch) {
+        W v[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) v[u] = s[i + 32 * u];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) d[i + 32 * u] = v[u];
+    }
+    for (; i < words; i += 32) d[i] = s[i];
+}
+
+bool have_windows() {
+    return g_nccl.MemAlloc && g_nccl.MemFree && g_nccl.WindowRegister && g_nccl.WindowDeregister;
+}
+
 }  // namespace
 
 extern "C" {
@@ -344,7 +404,12 @@ int tb_b200_comm_init(int nranks, int rank, const void* unique_id, int device) {
 
 int tb_b200_comm_destroy(void) {
     release_bufs();
-    if (!g_comm) return TB_OK;
+    if (!g_comm) {
+        g_wins.clear();  // an aborted communicator took its windows with it
+        return TB_OK;
+    }
+    while (!g_wins.empty())  // every rank destroys: deregister in allocation order
+        tb_b200_comm_window_free(g_wins.front().ptr);  // (drops the record first)
     ncclResult_t r = g_nccl.CommFinalize(g_comm);
     int rc = TB_OK;
     if (r != ncclSuccess && r != ncclInProgress) {
@@ -538,6 +603,115 @@ int tb_b200_embedding_sharded(int dtype, int64_t n_tokens, int64_t dim, int64_t 
     rc = copy_rows(y_local, d_recv, recvbuf, nullptr, nr, row_bytes, s);
     if (rc) return rc;
     TB_CUDA_TRY(cudaEventRecord(B.dev_free, s));
+    return TB_OK;
+}
+
+int tb_b200_comm_window_alloc(size_t bytes, void** ptr) {
+    if (!ptr || !bytes) return TB_ERR_INVALID_ARG;
+    *ptr = nullptr;
+    if (!g_comm) {
+        tbh::set_error_text("tb_b200_comm_window_alloc: no communicator (tb_b200_comm_init)");
+        return TB_ERR_INVALID_ARG;
+    }
+    if (!have_windows()) {
+        tbh::set_error_text("the loaded NCCL has no symmetric memory windows");
+        return TB_ERR_DEVICE;
+    }
+    bytes = (bytes + NCCL_WIN_REQUIRED_ALIGNMENT - 1) / NCCL_WIN_REQUIRED_ALIGNMENT *
+            NCCL_WIN_REQUIRED_ALIGNMENT;
+    void* p = nullptr;
+    ncclResult_t r = g_nccl.MemAlloc(&p, bytes);
+    if (r != ncclSuccess) {
+        nccl_error("ncclMemAlloc", r);
+        return TB_ERR_DEVICE;
+    }
+    ncclWindow_t w = nullptr;
+    r = g_nccl.WindowRegister(g_comm, p, bytes, &w, NCCL_WIN_COLL_SYMMETRIC);
+    if (r != ncclSuccess && r != ncclInProgress) {
+        nccl_error("ncclCommWindowRegister", r);
+        g_nccl.MemFree(p);
+        return TB_ERR_DEVICE;
+    }
+    const int rc = wait_comm("ncclCommWindowRegister");
+    if (rc) {
+        if (g_comm) g_nccl.MemFree(p);  // after an abort the memory went with the communicator
+        return rc;
+    }
+    g_wins.push_back(WinRec{static_cast<char*>(p), bytes, w});
+    *ptr = p;
+    return TB_OK;
+}
+
+int tb_b200_comm_window_free(void* ptr) {
+    if (!ptr) return TB_OK;
+    for (size_t i = 0; i < g_wins.size(); ++i) {
+        if (g_wins[i].ptr != ptr) continue;
+        const WinRec w = g_wins[i];
+        g_wins.erase(g_wins.begin() + (ptrdiff_t)i);
+        if (!g_comm) return TB_OK;
+        ncclResult_t r = g_nccl.WindowDeregister(g_comm, w.win);
+        int rc = TB_OK;
+        if (r != ncclSuccess && r != ncclInProgress) {
+            nccl_error("ncclCommWindowDeregister", r);
+            rc = TB_ERR_DEVICE;
+        } else {
+            rc = wait_comm("ncclCommWindowDeregister");
+        }
+        if (rc == TB_OK) {
+            r = g_nccl.MemFree(w.ptr);
+            if (r != ncclSuccess) {
+                nccl_error("ncclMemFree", r);
+                rc = TB_ERR_DEVICE;
+            }
+        }
+        return rc;
+    }
+    return TB_ERR_INVALID_ARG;
+}
+
+int tb_b200_embedding_sharded_window(int dtype, int64_t n_tokens, int64_t dim, int64_t vocab,
+                                     const int32_t* ids, const void* shard, void* y,
+                                     void* stream) {
+    if (!g_comm) {
+        tbh::set_error_text("tb_b200_embedding_sharded_window: no communicator");
+        return TB_ERR_INVALID_ARG;
+    }
+    if (dtype != TB_DTYPE_F32 && dtype != TB_DTYPE_BF16) return TB_ERR_UNSUPPORTED_DTYPE;
+    if (n_tokens < 0 || dim < 0 || vocab < g_nranks) return TB_ERR_INVALID_SHAPE;
+    if (n_tokens == 0 || dim == 0) return TB_OK;
+    if (!ids || !shard || !y) return TB_ERR_INVALID_ARG;
+    const WinRec* w = nullptr;
+    for (const WinRec& r : g_wins)
+        if (static_cast<const char*>(shard) >= r.ptr &&
+            static_cast<const char*>(shard) < r.ptr + r.bytes)
+            w = &r;
+    if (!w) {
+        tbh::set_error_text("tb_b200_embedding_sharded_window: shard is not in a window");
+        return TB_ERR_INVALID_ARG;
+    }
+    const int64_t row_bytes = dim * (dtype == TB_DTYPE_F32 ? 4 : 2);
+    const size_t base = (size_t)(static_cast<const char*>(shard) - w->ptr);
+    int64_t lo, hi;
+    tb_b200_partition(vocab, g_nranks, g_rank, &lo, &hi);
+    if (base + (size_t)((hi - lo) * row_bytes) > w->bytes) return TB_ERR_INVALID_SHAPE;
+    const tbh::DeviceState* ds = tbh::current_device_state();
+    if (!ds) return TB_ERR_DEVICE;
+    cudaStream_t s = tbh::stream_of(stream);
+    const unsigned grid = (unsigned)((n_tokens + 7) / 8);
+    const uintptr_t a = reinterpret_cast<uintptr_t>(y) | (uintptr_t)base | (uintptr_t)row_bytes;
+    if ((a & 15) == 0)
+        k_embed_window<uint4><<<grid, 256, 0, s>>>(ids, n_tokens, vocab, g_nranks, w->win, base,
+                                                   row_bytes / 16, static_cast<uint4*>(y),
+                                                   ds->status);
+    else if ((a & 3) == 0)
+        k_embed_window<uint32_t><<<grid, 256, 0, s>>>(ids, n_tokens, vocab, g_nranks, w->win,
+                                                      base, row_bytes / 4,
+                                                      static_cast<uint32_t*>(y), ds->status);
+    else
+        k_embed_window<uint16_t><<<grid, 256, 0, s>>>(ids, n_tokens, vocab, g_nranks, w->win,
+                                                      base, row_bytes / 2,
+                                                      static_cast<uint16_t*>(y), ds->status);
+    TB_LAUNCH_CHECK("sharded embedding kernel (window)");
     return TB_OK;
 }
 

@@ -177,6 +177,9 @@ SIGNATURES = {
     "tb_b200_comm_info": (i32, [P(i32), P(i32)]),
     "tb_b200_comm_wait": (i32, [vp]),
     "tb_b200_selftest_wait": (i32, [i32, C.c_uint32, vp]),
+    "tb_b200_comm_window_alloc": (i32, [C.c_size_t, P(vp)]),
+    "tb_b200_comm_window_free": (i32, [vp]),
+    "tb_b200_embedding_sharded_window": (i32, [i32, i64, i64, i64, vp, vp, vp, vp]),
     "tb_b200_embedding_sharded": (i32, [i32, i64, i64, i64, vp, vp, vp, vp]),
     "tb_b200_embedding_sharded_p2p": (i32, [i32, i64, i64, i64, vp, P(vp), i32, vp, vp]),
     "tb_b200_p2p_export": (i32, [vp, vp, P(i64)]),
@@ -551,6 +554,32 @@ def comm_wait(stream=None) -> int:
     (tb_b200_comm_wait): TB_OK, or TB_ERR_DEVICE after aborting the
     communicator on an error or a timeout.  Returns the code."""
     return lib().tb_b200_comm_wait(stream or cur_stream())
+
+
+def comm_window_alloc(nbytes: int) -> int:
+    """Device address of `nbytes` of the communicator's symmetric memory
+    (collective: every rank, same size, same order)."""
+    p = vp()
+    check(lib().tb_b200_comm_window_alloc(nbytes, C.byref(p)), "comm_window_alloc")
+    return p.value
+
+
+def comm_window_free(addr: int) -> None:
+    check(lib().tb_b200_comm_window_free(vp(addr)), "comm_window_free")
+
+
+def embedding_sharded_window(ids, shard_addr: int, vocab: int, dim: int, dtype, y=None,
+                             stream=None):
+    """Rows of `ids` (int32 CUDA tensor) from the vocab shards held in the
+    communicator's symmetric memory (tb_b200_embedding_sharded_window)."""
+    torch = _torch()
+    _dev(ids)
+    if y is None:
+        y = torch.empty((ids.numel(), dim), dtype=dtype, device=ids.device)
+    check(lib().tb_b200_embedding_sharded_window(dtype_code(y), ids.numel(), dim, vocab, ptr(ids),
+                                                 vp(shard_addr), ptr(y), stream or cur_stream()),
+          "embedding_sharded_window")
+    return y
 
 
 def comm_info():

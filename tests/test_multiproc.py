@@ -12,6 +12,7 @@ the one-kernel gather over peer memory (tb_b200_embedding_sharded_p2p,
 shards mapped through CUDA IPC), both bit-exact against the oracle for f32
 and bf16 tables.
 """
+import ctypes as C
 import os
 import socket
 import sys
@@ -216,3 +217,67 @@ def test_sharded_embedding_p2p_two_gpus(n, vocab, dim):
     assert len(res) == 2
     for rank, ok, err in res:
         assert ok, f"rank {rank}: {err or 'p2p gather differs from the full-table gather'}"
+
+
+def _window_rank(rank, world, port, n, vocab, dim, q):
+    """One kernel over NCCL symmetric memory: each rank's table part sits in
+    a window every rank can load from (tb_b200_embedding_sharded_window)."""
+    import torch
+    import torch.distributed as dist
+    import tb_b200 as T
+    from oracle import oracle as O
+    try:
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=world)
+        uid = [T.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        T.comm_init(world, rank, uid[0], rank)
+        ids, table = problem(n, vocab, dim, 97)
+        vlo, vhi = T.partition(vocab, world, rank)
+        tlo, thi = T.partition(n, world, rank)
+        oks = []
+        for host in (table, O.f32_to_bf16(table)):  # f32, then bf16 bits
+            esz = host.dtype.itemsize
+            cap = -(-vocab // world) * dim * esz  # the largest part: same size everywhere
+            addr = T.comm_window_alloc(cap)
+            part = torch.from_numpy(np.ascontiguousarray(host[vlo:vhi])).cuda()
+            T.check(T.lib().tb_b200_memcpy_d2d(C.c_void_p(addr), T.ptr(part), part.numel() * esz,
+                                               None), "d2d")
+            torch.cuda.synchronize()
+            dist.barrier()  # every shard written before any rank gathers
+            tdt = torch.bfloat16 if host.dtype == np.uint16 else torch.float32
+            my_ids = torch.from_numpy(ids[tlo:thi].astype(np.int32)).cuda()
+            for _ in range(2):
+                y = T.embedding_sharded_window(my_ids, addr, vocab, dim, tdt)
+                torch.cuda.synchronize()
+                got = y.cpu().view(torch.int16 if tdt == torch.bfloat16 else torch.int32).numpy()
+                oks.append(np.array_equal(got.view(host.dtype), O.embedding(ids[tlo:thi], host)))
+            oks.append(T.check_status() == (0, 0))
+            bad = torch.tensor([-1, vocab, 0], dtype=torch.int32, device="cuda")
+            y = T.embedding_sharded_window(bad, addr, vocab, dim, tdt)
+            rc, flags = T.check_status()
+            got = y.cpu().view(torch.int16 if tdt == torch.bfloat16 else torch.int32).numpy()
+            oks.append(rc != 0 and flags == 1 and not got[:2].any()
+                       and np.array_equal(got[2].view(host.dtype), host[0]))
+            dist.barrier()  # every rank done reading before the windows go
+            T.comm_window_free(addr)
+        T.comm_destroy()
+        dist.destroy_process_group()
+        q.put((rank, all(oks), "" if all(oks) else f"checks {oks}"))
+    except Exception as e:
+        q.put((rank, False, repr(e)))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n,vocab,dim", [(4096, 32003, 4096), (333, 1001, 1000)])
+def test_sharded_embedding_window_two_gpus(n, vocab, dim):
+    """Odd vocabularies (uneven parts); 16 KB rows and 4000 / 2000-byte rows."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    res = run_ranks(_window_rank, 2, n, vocab, dim)
+    assert len(res) == 2
+    for rank, ok, err in res:
+        assert ok, f"rank {rank}: {err or 'window gather differs from the full-table gather'}"
