@@ -987,6 +987,23 @@ def run_sharded(args, rank, world, local):
         dist.all_reduce(x, op=op or dist.ReduceOp.MAX)
         return float(x.item())
 
+    if args.profile_op in ("softmax", "argmax"):
+        # a small case for ncu: only this op's buffers (world 1)
+        g = torch.Generator(device=dev)
+        g.manual_seed(12345 + 9)
+        x = torch.empty((LR, c.vocab), device=dev).normal_(0.0, c.logit_std, generator=g)
+        out = (torch.empty_like(x) if args.profile_op == "softmax"
+               else torch.empty(LR, dtype=torch.int32, device=dev))
+        sp = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+        for _ in range(args.warmup + args.steps):
+            if args.profile_op == "softmax":
+                T.check(L.tb_b200_softmax(T.F32, LR, c.vocab, T.ptr(x), None, T.ptr(out), sp),
+                        "softmax")
+            else:
+                T.check(L.tb_b200_argmax(T.F32, LR, c.vocab, T.ptr(x), T.ptr(out), sp), "argmax")
+        torch.cuda.synchronize()
+        return None
+
     # the library's NCCL communicator over the same ranks
     if world > 1:
         uid = [T.comm_unique_id() if rank == 0 else None]
