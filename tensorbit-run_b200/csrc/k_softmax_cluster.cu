@@ -17,36 +17,41 @@
 // each): a segment is read from HBM once, two rows ahead of its use.
 //
 // Roles (16 warps per CTA):
-//   workers (9 warps), per row j, three phases interleaved with the next row
+//   workers (9 warps), per row j, three phases interleaved with the next row,
+//     two tiles per warp at a time:
 //     A(j)  max over the segment; the segment max goes to every CTA of the
 //           cluster (st.shared::cluster + a remote mbarrier arrive);
-//     B(j)  with the row max: e in place, a sum estimate per tile, the
-//           segment's estimate to every CTA;
+//     B(j)  with the row max: e in place, a sum estimate per tile (integer
+//           redux), the segment's estimate to every CTA;
 //     A(j+1)
 //     C(j)  with the estimates of the segments before this one: the running-
 //           sum estimate at each tile start -> the binade the exact running
 //           sum is predicted to be in -> per tile the integer sum of
 //           rne(e / u) on that binade's grid u, as (D0, D1) for an even / odd
 //           running sum at the tile start (they differ only when a term is an
-//           exact tie); the summaries go to the row's scanner (remote
-//           stores); the buffer is released and the row three ahead is
-//           copied into it.
+//           exact tie), into this CTA's summary slot of the row; one remote
+//           arrive tells the row's scanner; the buffer is released and the
+//           row three ahead is copied into it.
 //     So each cluster exchange has a whole phase of work to land in.
-//   scanners (2 warps; row j's scanner is warp (j / C) % 2 of CTA j % C):
-//     tile 0 summed in order by one lane; then 32 tiles per step: an ordered
-//     composition scan of the (D0, D1) functions gives each tile's start;
-//     the first tile that is not on its predicted grid, crosses the binade
-//     or is flagged is summed term by term (ordered_sum_tile, its terms
-//     recomputed from x in L2).  The row's sum and max go to every CTA.
-//   finalizers (5 warps): y = e * (1/sum) of the CTA's segment of each row,
+//   scanners (3 warps; row j's scanner is warp (j / C) % 3 of CTA j % C):
+//     tile 0 summed in order by one lane; then 32 tiles per step, their
+//     summaries read from the owning CTAs' shared memory (ld.shared::cluster):
+//     an ordered composition scan of the (D0, D1) functions gives each tile's
+//     start; the first tile that is not on its predicted grid, crosses the
+//     binade or is flagged is summed term by term (ordered_sum_tile, its
+//     terms recomputed from x in L2; tiles predicted to cross are loaded
+//     ahead).  The row's sum and max go to every CTA.
+//   finalizers (4 warps): y = e * (1/sum) of the CTA's segment of each row,
 //     in row order, e recomputed from x (still in L2: the copies keep it
-//     there), streaming stores.
+//     there), 16 loads in flight per thread, streaming stores.
 // Every wait is bounded (%globaltimer, 2 s): a timeout raises
 // TB_B200_FLAG_WAIT_TIMEOUT and the CTA skips its remaining waits; every
 // thread of every CTA still reaches the final cluster barrier, so no CTA
 // leaves while a peer may write its shared memory, and no copy is in flight
 // when a CTA exits.  Only this GPU's memory is read; no multicast.
 #include <math.h>
+
+#include <type_traits>
 
 #include "ordered_sum.cuh"
 #include "tb_device.cuh"
@@ -60,31 +65,32 @@ constexpr int kSegTiles = 64;  // tiles per CTA segment, at most
 constexpr int kMaxC = 8;       // CTAs per cluster (portable limit)
 constexpr int kMaxTiles = kSegTiles * kMaxC;
 constexpr int kNB = 3;         // segment buffers per CTA
-constexpr int kScanW = 2;      // scanner warps per CTA
-constexpr int kFinW = 5;       // finalizer warps
+constexpr int kScanW = 3;      // scanner warps per CTA
+constexpr int kFinW = 4;       // finalizer warps
 constexpr int kWorkW = 9;      // worker warps
 constexpr int kNT = 512;
 constexpr int kKeys = kMaxC * kScanW;  // one per scanner warp of the cluster
 constexpr uint32_t kSat = 1u << 30;
 constexpr uint32_t kLimit = 1u << 24;
 constexpr uint32_t kExact = 1u << 16;  // meta flag: sum the tile term by term
+constexpr uint32_t kCross = 1u << 17;  // meta flag: predicted to cross a binade
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
 constexpr float kLog2e = 1.44269504f;
 static_assert(kScanW + kFinW + kWorkW == kNT / 32, "warp roles");
 
-// Warp roles: scanners on warps 0 and 4 and finalizers on 8 and 12 share
-// warp scheduler 0 (warp id mod 4), so the scanners' latency-bound chains
-// never compete with the throughput-bound workers for issue slots.
-__device__ __forceinline__ int scanner_of(int w) { return w == 0 ? 0 : w == 4 ? 1 : -1; }
-__device__ __forceinline__ int finalizer_of(int w) { return w == 8 ? 0 : w >= 12 ? w - 11 : -1; }
-__device__ __forceinline__ int worker_of(int w) { return w - 1 - (w > 4) - (w > 8); }
+// Warp roles: the scanners (warps 0, 4, 8) and a finalizer (12) share warp
+// scheduler 0 (warp id mod 4), so the scanners' latency-bound chains never
+// compete with the throughput-bound workers for issue slots.
+__device__ __forceinline__ int scanner_of(int w) { return (w & 3) == 0 && w < 12 ? w >> 2 : -1; }
+__device__ __forceinline__ int finalizer_of(int w) { return w >= 12 ? w - 12 : -1; }
+__device__ __forceinline__ int worker_of(int w) { return w - 1 - (w >> 2); }
 
 struct Ctl {
-    uint2 D[kScanW][kMaxTiles];          // summaries pushed by every CTA (row of scanner s)
-    uint32_t meta[kScanW][kMaxTiles];    // predicted binade (int8) | kExact
-    float row_m[kScanW];                 // the row max, pushed by CTA 0
+    uint2 D[kKeys][kSegTiles];           // this CTA's summaries of the row of key k
+    uint32_t meta[kKeys][kSegTiles];     // predicted binade (int8) | kExact | kCross
+    float row_m[kKeys];                  // the row max (read from CTA 0 by the scanner)
     float tsum[kSegTiles];               // this CTA's tile sum estimates
-    uint32_t lmeta[kSegTiles];           // this CTA's predicted binades
+    uint32_t lmeta[kSegTiles];           // this CTA's predicted binades and flags
     float xmax[2][kMaxC];                // segment maxima of rows of parity p
     float xtot[2][kMaxC];                // segment sum estimates
     float res_sum[kKeys];                // row results, by key j % (C * kScanW)
@@ -93,8 +99,8 @@ struct Ctl {
     float scratch[kScanW][kTileN];       // tile 0 of a scanner's row
     uint64_t bar_x[kNB];                 // segment landed
     uint64_t bar_max[2], bar_tot[2];     // C arrivals
-    uint64_t bar_sfree[kKeys];           // scanner of that key released its summaries
-    uint64_t bar_ready[kScanW];          // C arrivals: summaries of the row pushed
+    uint64_t bar_sfree[kKeys];           // scanner of that key is done with the summaries
+    uint64_t bar_ready[kScanW];          // C arrivals: every CTA's summaries of the row
     uint64_t bar_res[kKeys];             // the row's result is here
     uint64_t bar_fcred[kScanW];          // C * kFinW arrivals: result slot read everywhere
     int abort_flag;
@@ -134,6 +140,23 @@ __device__ __forceinline__ void st_remote(uint32_t a, uint2 v) {
     asm volatile("st.shared::cluster.v2.u32 [%0], {%1, %2};" ::"r"(a), "r"(v.x), "r"(v.y)
                  : "memory");
 }
+__device__ __forceinline__ uint2 ld_remote_u2(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared::cluster.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ uint32_t ld_remote_u32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ float ld_remote_f32(uint32_t a) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+    return v;
+}
+
 // One arrival on an mbarrier of any CTA of the cluster, ordered after this
 // thread's earlier shared-memory stores (release at cluster scope).
 __device__ __forceinline__ void arrive_remote(uint32_t bar) {
@@ -190,13 +213,40 @@ struct Expo {
         c = __fmul_rn(-mx, kLog2e);
         slow = !(fabsf(c) < 128.0f);
     }
-    __device__ __forceinline__ float operator()(float x) const {
-        const float a = slow ? __fmul_rn(__fsub_rn(x, m), kLog2e) : __fmaf_rn(x, kLog2e, c);
+    // the row's form, chosen by the caller once per row
+    template <bool SLOW>
+    __device__ __forceinline__ float at(float x) const {
+        const float a = SLOW ? __fmul_rn(__fsub_rn(x, m), kLog2e) : __fmaf_rn(x, kLog2e, c);
         float r;
         asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
         return r;
     }
+    __device__ __forceinline__ float operator()(float x) const {
+        return slow ? at<true>(x) : at<false>(x);
+    }
 };
+
+// Sum over the warp of nonnegative lane values v, to about 2^-21 relative:
+// the largest lane value sets a power-of-two scale, each lane rounds
+// v * scale to an integer, and one redux.sync adds them (two redux
+// instructions instead of a five-step shuffle tree).
+__device__ __forceinline__ float warp_sum_est(float v) {
+    const uint32_t mx = __reduce_max_sync(tbk::kFull, __float_as_uint(v));  // v >= 0: bits order
+    if (mx == 0u) return 0.0f;
+    if (mx >= 0x7f800000u) return __uint_as_float(0x7fc00000u);  // inf or NaN
+    const int ex = (int)(mx >> 23) - 127;  // the largest lane value is in [2^ex, 2^(ex+1))
+    const int sh = 25 - ex;                // lane values < 2^26 after scaling
+    if (sh > 126) return 0.0f;             // below 2^-100: no binade anyway
+    const float sc = __uint_as_float((uint32_t)(sh + 127) << 23);
+    const uint32_t q = __float2uint_rn(__fmul_rn(v, sc));
+    const uint32_t tot = __reduce_add_sync(tbk::kFull, q);  // < 32 * 2^26 = 2^31
+    return __fmul_rn((float)tot, __uint_as_float((uint32_t)(127 - sh) << 23));
+}
+
+__device__ __forceinline__ bool near_pow2(float v) {
+    const uint32_t mant = __float_as_uint(v) & 0x7fffffu;
+    return mant < (1u << 13) || mant > (1u << 23) - (1u << 13);
+}
 
 // Units added by one term given the parity of the partial sum before it.
 struct Fn {
@@ -229,93 +279,125 @@ __device__ __forceinline__ Fn warp_compose(Fn f) {  // lane 0 first; valid in la
     return f;
 }
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(tbk::kFull, v, o);
-    return v;
-}
 
 // ------------------------------------------------------------------ scanner
-// Tile `tile` of the row, term by term from x (lane l: terms 8l .. 8l+7).
-__device__ void resolve_tile(tbk::RunSum& st, const float* xr, const Expo& ex, int tile,
-                             int cols) {
+// x of tile `tile` of the row (lane l: terms 8l .. 8l+7; past the row: -inf).
+__device__ __forceinline__ void load_tile_x(const float* xr, int tile, int cols, float (&v)[8]) {
     const int lane = threadIdx.x & 31;
     const int n = min(kTileN, cols - tile * kTileN);
-    float e[8];
     const float* p = xr + (int64_t)tile * kTileN + 8 * lane;
     if (8 * lane + 8 <= n) {
         const float4 a = __ldcg(reinterpret_cast<const float4*>(p));
         const float4 b = __ldcg(reinterpret_cast<const float4*>(p + 4));
-        e[0] = ex(a.x); e[1] = ex(a.y); e[2] = ex(a.z); e[3] = ex(a.w);
-        e[4] = ex(b.x); e[5] = ex(b.y); e[6] = ex(b.z); e[7] = ex(b.w);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
     } else {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) e[k] = 8 * lane + k < n ? ex(__ldcg(p + k)) : 0.0f;
+        for (int k = 0; k < 8; ++k) v[k] = 8 * lane + k < n ? __ldcg(p + k) : -INFINITY;
     }
+}
+
+// Tile `tile` of the row term by term, from its x values.
+__device__ __forceinline__ void resolve_tile(tbk::RunSum& st, const float (&xv)[8],
+                                             const Expo& ex, int tile, int cols) {
+    const int n = min(kTileN, cols - tile * kTileN);
+    float e[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) e[k] = ex(xv[k]);
     tbk::ordered_sum_tile<8>(st, e, n, 0);
 }
 
-// The in-order sum of the row from its summaries (lane-uniform result).
-__device__ float scan_row(const uint2* D, const uint32_t* meta, float* scratch, const float* xr,
+// The in-order sum of the row from the summaries in the cluster's CTAs
+// (tile t: CTA t / seg_tiles, slot `key`; lane-uniform result).
+__device__ float scan_row(const Ctl& ctl, int key, int seg_tiles, float* scratch, const float* xr,
                           const Expo& ex, int cols) {
     const int lane = threadIdx.x & 31;
     const int ntiles = (cols + kTileN - 1) / kTileN;
-    // tile 0: strictly in order, one lane
+    // tile 0: strictly in order, one lane (four terms per shared load)
     const int n0 = min(cols, kTileN);
     for (int k = lane; k < n0; k += 32) scratch[k] = ex(__ldcg(xr + k));
     __syncwarp();
     float acc = 0.0f;
-    if (lane == 0)
-        for (int k = 0; k < n0; ++k) acc = __fadd_rn(acc, scratch[k]);
+    if (lane == 0) {
+        int k = 0;
+        for (; k + 4 <= n0; k += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(scratch + k);
+            acc = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc, v.x), v.y), v.z), v.w);
+        }
+        for (; k < n0; ++k) acc = __fadd_rn(acc, scratch[k]);
+    }
     acc = __shfl_sync(tbk::kFull, acc, 0);
     __syncwarp();
     tbk::RunSum st;
     st.set(acc);
     for (int t0 = 1; t0 < ntiles && !st.nan; t0 += 32) {
-            const int cnt = min(32, ntiles - t0);
-            uint2 dl = make_uint2(0u, 0u);
-            uint32_t mt = 0;
-            if (lane < cnt) {
-                dl = D[t0 + lane];
-                mt = meta[t0 + lane];
-            }
-            const int tb = (int)(int8_t)(mt & 0xffu);
-            int pos = 0;
-            while (pos < cnt && !st.nan) {
-                const bool valid = lane >= pos && lane < cnt;
-                const bool ok = valid && st.fast && !(mt & kExact) && tb == st.b;
-                const Fn f = ok ? Fn{dl.x, dl.y} : Fn{0u, 0u};
-                Fn inc = f;
+        const int cnt = min(32, ntiles - t0);
+        uint2 dl = make_uint2(0u, 0u);
+        uint32_t mt = 0;
+        if (lane < cnt) {
+            const int t = t0 + lane;
+            const uint32_t c = (uint32_t)(t / seg_tiles), i = (uint32_t)(t % seg_tiles);
+            dl = ld_remote_u2(remote(&ctl.D[key][i], c));
+            mt = ld_remote_u32(remote(&ctl.meta[key][i], c));
+        }
+        const int tb = (int)(int8_t)(mt & 0xffu);
+        // the first tile predicted to cross: its x is on its way during the scan
+        unsigned flagged = __ballot_sync(tbk::kFull, lane < cnt && (mt & kCross));
+        int pf = -1;
+        float pre[8];
+        if (flagged) {
+            pf = __ffs(flagged) - 1;
+            load_tile_x(xr, t0 + pf, cols, pre);
+        }
+        int pos = 0;
+        while (pos < cnt && !st.nan) {
+            const bool valid = lane >= pos && lane < cnt;
+            const bool ok = valid && st.fast && !(mt & kExact) && tb == st.b;
+            const Fn f = ok ? Fn{dl.x, dl.y} : Fn{0u, 0u};
+            Fn inc = f;
 #pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    Fn g;
-                    g.a0 = __shfl_up_sync(tbk::kFull, inc.a0, o);
-                    g.a1 = __shfl_up_sync(tbk::kFull, inc.a1, o);
-                    if (lane >= o) inc = compose(g, inc);
-                }
-                Fn exc;
-                exc.a0 = __shfl_up_sync(tbk::kFull, inc.a0, 1);
-                exc.a1 = __shfl_up_sync(tbk::kFull, inc.a1, 1);
-                if (lane == 0) exc = Fn{0u, 0u};
-                const uint32_t p = st.S & 1u;
-                const uint32_t exs = p ? exc.a1 : exc.a0;
-                const uint32_t mine = ((p + exs) & 1u) ? f.a1 : f.a0;
-                const bool ev = valid && (!ok || st.S + exs + mine >= kLimit);
-                const unsigned bal = __ballot_sync(tbk::kFull, ev);
-                if (bal == 0) {
-                    st.S += __shfl_sync(tbk::kFull, p ? inc.a1 : inc.a0, 31);
-                    st.s = __fmul_rn((float)st.S, st.u);
-                    break;
-                }
-                const int fl = __ffs(bal) - 1;
-                const uint32_t pre = __shfl_sync(tbk::kFull, exs, fl);
-                if (st.fast && pre) {
-                    st.S += pre;
-                    st.s = __fmul_rn((float)st.S, st.u);
-                }
-                resolve_tile(st, xr, ex, t0 + fl, cols);
-                pos = fl + 1;
+            for (int o = 1; o < 32; o <<= 1) {
+                Fn g;
+                g.a0 = __shfl_up_sync(tbk::kFull, inc.a0, o);
+                g.a1 = __shfl_up_sync(tbk::kFull, inc.a1, o);
+                if (lane >= o) inc = compose(g, inc);
             }
+            Fn exc;
+            exc.a0 = __shfl_up_sync(tbk::kFull, inc.a0, 1);
+            exc.a1 = __shfl_up_sync(tbk::kFull, inc.a1, 1);
+            if (lane == 0) exc = Fn{0u, 0u};
+            const uint32_t p = st.S & 1u;
+            const uint32_t exs = p ? exc.a1 : exc.a0;
+            const uint32_t mine = ((p + exs) & 1u) ? f.a1 : f.a0;
+            const bool ev = valid && (!ok || st.S + exs + mine >= kLimit);
+            const unsigned bal = __ballot_sync(tbk::kFull, ev);
+            if (bal == 0) {
+                st.S += __shfl_sync(tbk::kFull, p ? inc.a1 : inc.a0, 31);
+                st.s = __fmul_rn((float)st.S, st.u);
+                break;
+            }
+            const int fl = __ffs(bal) - 1;
+            const uint32_t pre_u = __shfl_sync(tbk::kFull, exs, fl);
+            if (st.fast && pre_u) {
+                st.S += pre_u;
+                st.s = __fmul_rn((float)st.S, st.u);
+            }
+            float xv[8];
+            if (fl == pf) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) xv[k] = pre[k];
+            } else {
+                load_tile_x(xr, t0 + fl, cols, xv);
+            }
+            // the next flagged tile after this one, on its way during the resolve
+            flagged &= ~((2u << fl) - 1u);
+            if (fl >= pf && flagged) {
+                pf = __ffs(flagged) - 1;
+                load_tile_x(xr, t0 + pf, cols, pre);
+            }
+            resolve_tile(st, xv, ex, t0 + fl, cols);
+            pos = fl + 1;
+        }
     }
     return st.s;
 }
@@ -375,11 +457,11 @@ k_softmax_cluster(const float* __restrict__ x, float* y, int rows, int cols, int
             const int j = key + keys * k;
             if (j >= nloc) break;
             if (!wait_c(&ctl.bar_ready[sw], (uint32_t)k & 1u, status, abort_v)) break;
-            const float m = ctl.row_m[sw];
+            const float m = ld_remote_f32(remote(&ctl.row_m[key], 0u));
             const Expo ex(m);
             const float* xr = x + row_of(j) * row_stride;
-            const float sum = scan_row(ctl.D[sw], ctl.meta[sw], ctl.scratch[sw], xr, ex, cols);
-            // the summaries are consumed: every CTA may push its next row
+            const float sum = scan_row(ctl, key, seg_tiles, ctl.scratch[sw], xr, ex, cols);
+            // the summaries are read: every CTA may write its next row of this key
             __syncwarp();
             if (lane < ncl) arrive_remote(remote(&ctl.bar_sfree[key], (uint32_t)lane));
             // the result slot is free once every finalizer read row j - keys
@@ -395,6 +477,7 @@ k_softmax_cluster(const float* __restrict__ x, float* y, int rows, int cols, int
         // ------------------------------------------------------ finalizers
         const int ft = fw * 32 + lane;
         constexpr int kFin = kFinW * 32;
+        constexpr int kU = 16;
         const uint64_t pol = tbk::policy_evict_first();  // last use of x
         const int nv = (col1 - col0) / 4;
         for (int j = 0; j < nloc; ++j) {
@@ -411,33 +494,32 @@ k_softmax_cluster(const float* __restrict__ x, float* y, int rows, int cols, int
             const int64_t base = row_of(j) * row_stride + col0;
             const float4* xr = reinterpret_cast<const float4*>(x + base);
             float4* yr = reinterpret_cast<float4*>(y + base);
-            constexpr int kU = 8;
-            int v = ft;
-            for (; v + (kU - 1) * kFin < nv; v += kU * kFin) {
-                float4 a[kU];
-#pragma unroll
-                for (int u = 0; u < kU; ++u) a[u] = tbk::ld_f4_hint(xr + v + u * kFin, pol);
-#pragma unroll
-                for (int u = 0; u < kU; ++u) {
+            auto run = [&](auto slow_tag) {
+                constexpr bool SLOW = decltype(slow_tag)::value;
+                auto out = [&](float4 a) {
                     float4 o;
-                    o.x = ex(a[u].x); o.y = ex(a[u].y); o.z = ex(a[u].z); o.w = ex(a[u].w);
+                    o.x = ex.at<SLOW>(a.x); o.y = ex.at<SLOW>(a.y);
+                    o.z = ex.at<SLOW>(a.z); o.w = ex.at<SLOW>(a.w);
                     if (norm) {
                         o.x = __fmul_rn(o.x, inv); o.y = __fmul_rn(o.y, inv);
                         o.z = __fmul_rn(o.z, inv); o.w = __fmul_rn(o.w, inv);
                     }
-                    __stcs(yr + v + u * kFin, o);
+                    return o;
+                };
+                int v = ft;
+                for (; v + (kU - 1) * kFin < nv; v += kU * kFin) {
+                    float4 a[kU];
+#pragma unroll
+                    for (int u = 0; u < kU; ++u) a[u] = tbk::ld_f4_hint(xr + v + u * kFin, pol);
+#pragma unroll
+                    for (int u = 0; u < kU; ++u) __stcs(yr + v + u * kFin, out(a[u]));
                 }
-            }
-            for (; v < nv; v += kFin) {
-                const float4 a = tbk::ld_f4_hint(xr + v, pol);
-                float4 o;
-                o.x = ex(a.x); o.y = ex(a.y); o.z = ex(a.z); o.w = ex(a.w);
-                if (norm) {
-                    o.x = __fmul_rn(o.x, inv); o.y = __fmul_rn(o.y, inv);
-                    o.z = __fmul_rn(o.z, inv); o.w = __fmul_rn(o.w, inv);
-                }
-                __stcs(yr + v, o);
-            }
+                for (; v < nv; v += kFin) __stcs(yr + v, out(tbk::ld_f4_hint(xr + v, pol)));
+            };
+            if (ex.slow)
+                run(std::true_type{});
+            else
+                run(std::false_type{});
         }
     } else {
         // ------------------------------------------------------ workers
@@ -455,26 +537,44 @@ k_softmax_cluster(const float* __restrict__ x, float* y, int rows, int cols, int
         int issued = 0;  // rows whose copy was issued
         if (producer)
             for (; issued < min(kNB, nloc); ++issued) issue(issued);
+        const int nfull = (col1 - col0) / kTileN;  // full tiles of the segment
+        // lane l holds terms 4l..4l+3 and 128+4l..128+4l+3 of a tile
+        auto ld2 = [&](const float* xt, int t, float4& a, float4& c) {
+            if (t < nfull) {
+                a = *reinterpret_cast<const float4*>(xt + 4 * lane);
+                c = *reinterpret_cast<const float4*>(xt + 128 + 4 * lane);
+            } else {  // the row's ragged last tile (a multiple of 4 terms)
+                const int n = (col1 - col0) - t * kTileN;
+                a = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+                c = a;
+                if (4 * lane < n) a = *reinterpret_cast<const float4*>(xt + 4 * lane);
+                if (128 + 4 * lane < n) c = *reinterpret_cast<const float4*>(xt + 128 + 4 * lane);
+            }
+        };
+        auto st2 = [&](float* xt, int t, const float4& a, const float4& c) {
+            const int n = t < nfull ? kTileN : (col1 - col0) - t * kTileN;
+            if (4 * lane < n) *reinterpret_cast<float4*>(xt + 4 * lane) = a;
+            if (128 + 4 * lane < n) *reinterpret_cast<float4*>(xt + 128 + 4 * lane) = c;
+        };
 
         // Phase A: segment max -> every CTA.
         auto phase_a = [&](int j) {
             const int b = j % kNB;
             wait_c(&ctl.bar_x[b], (uint32_t)(j / kNB) & 1u, status, abort_v);
             const float* s = seg(b);
-            float mx = -INFINITY;
-            for (int t = wi; t < nt; t += kWorkW) {
-                const float* xt = s + t * kTileN;
-                const int n = min(kTileN, (col1 - col0) - t * kTileN);
-                if (n == kTileN) {
-                    const float4 a = *reinterpret_cast<const float4*>(xt + 4 * lane);
-                    const float4 c = *reinterpret_cast<const float4*>(xt + 128 + 4 * lane);
-                    mx = fmaxf(mx, fmaxf(fmaxf(fmaxf(a.x, a.y), fmaxf(a.z, a.w)),
-                                         fmaxf(fmaxf(c.x, c.y), fmaxf(c.z, c.w))));
-                } else {
-                    for (int k = lane; k < n; k += 32) mx = fmaxf(mx, xt[k]);
-                }
+            float mx = -INFINITY, my = -INFINITY;
+            for (int t = wi; t < nt; t += 2 * kWorkW) {
+                const int u = t + kWorkW;
+                float4 a, c, a2, c2;
+                ld2(s + t * kTileN, t, a, c);
+                if (u < nt) ld2(s + u * kTileN, u, a2, c2);
+                mx = fmaxf(mx, fmaxf(fmaxf(fmaxf(a.x, a.y), fmaxf(a.z, a.w)),
+                                     fmaxf(fmaxf(c.x, c.y), fmaxf(c.z, c.w))));
+                if (u < nt)
+                    my = fmaxf(my, fmaxf(fmaxf(fmaxf(a2.x, a2.y), fmaxf(a2.z, a2.w)),
+                                         fmaxf(fmaxf(c2.x, c2.y), fmaxf(c2.z, c2.w))));
             }
-            mx = tbk::warp_max(mx);
+            mx = tbk::warp_max(fmaxf(mx, my));
             if (lane == 0) ctl.red[wi] = mx;
             work_sync();
             if (wi == 0) {
@@ -494,33 +594,42 @@ k_softmax_cluster(const float* __restrict__ x, float* y, int rows, int cols, int
             for (int c = 1; c < ncl; ++c) m = fmaxf(m, ctl.xmax[j & 1][c]);
             const Expo ex(m);
             float* s = seg(j % kNB);
-            for (int t = wi; t < nt; t += kWorkW) {
-                float* xt = s + t * kTileN;
-                const int n = min(kTileN, (col1 - col0) - t * kTileN);
-                float acc = 0.0f;
-                if (n == kTileN) {
-                    float4 a = *reinterpret_cast<float4*>(xt + 4 * lane);
-                    float4 c = *reinterpret_cast<float4*>(xt + 128 + 4 * lane);
-                    a.x = ex(a.x); a.y = ex(a.y); a.z = ex(a.z); a.w = ex(a.w);
-                    c.x = ex(c.x); c.y = ex(c.y); c.z = ex(c.z); c.w = ex(c.w);
-                    *reinterpret_cast<float4*>(xt + 4 * lane) = a;
-                    *reinterpret_cast<float4*>(xt + 128 + 4 * lane) = c;
-                    acc = ((a.x + a.y) + (a.z + a.w)) + ((c.x + c.y) + (c.z + c.w));
-                } else {
-                    for (int k = lane; k < n; k += 32) {
-                        const float e = ex(xt[k]);
-                        xt[k] = e;
-                        acc += e;
+            auto run = [&](auto slow_tag) {
+                constexpr bool SLOW = decltype(slow_tag)::value;
+                auto e4 = [&](float4& v) {
+                    v.x = ex.at<SLOW>(v.x); v.y = ex.at<SLOW>(v.y);
+                    v.z = ex.at<SLOW>(v.z); v.w = ex.at<SLOW>(v.w);
+                };
+                for (int t = wi; t < nt; t += 2 * kWorkW) {
+                    const int u = t + kWorkW;
+                    float4 a, c, a2, c2;
+                    ld2(s + t * kTileN, t, a, c);
+                    if (u < nt) ld2(s + u * kTileN, u, a2, c2);
+                    e4(a); e4(c);
+                    if (u < nt) {
+                        e4(a2); e4(c2);
+                    }
+                    st2(s + t * kTileN, t, a, c);
+                    if (u < nt) st2(s + u * kTileN, u, a2, c2);
+                    const float s1 = warp_sum_est(((a.x + a.y) + (a.z + a.w)) +
+                                                  ((c.x + c.y) + (c.z + c.w)));
+                    if (lane == 0) ctl.tsum[t] = s1;
+                    if (u < nt) {
+                        const float s2 = warp_sum_est(((a2.x + a2.y) + (a2.z + a2.w)) +
+                                                      ((c2.x + c2.y) + (c2.z + c2.w)));
+                        if (lane == 0) ctl.tsum[u] = s2;
                     }
                 }
-                acc = warp_sum(acc);
-                if (lane == 0) ctl.tsum[t] = acc;
-            }
+            };
+            if (ex.slow)
+                run(std::true_type{});
+            else
+                run(std::false_type{});
             work_sync();
             if (wi == 0) {
                 float v = 0.0f;
                 for (int t = lane; t < nt; t += 32) v += ctl.tsum[t];
-                v = warp_sum(v);
+                v = tbk::warp_sum(v);
                 if (lane < ncl) {
                     st_remote(remote(&ctl.xtot[j & 1][me], (uint32_t)lane), v);
                     arrive_remote(remote(&ctl.bar_tot[j & 1], (uint32_t)lane));
@@ -528,7 +637,8 @@ k_softmax_cluster(const float* __restrict__ x, float* y, int rows, int cols, int
             }
             return m;
         };
-        // Phase C: predicted binades, (D0, D1) per tile -> the row's scanner.
+        // Phase C: predicted binades, (D0, D1) per tile -> this CTA's summary
+        // slot of the row's key; one arrive tells the row's scanner.
         auto phase_c = [&](int j, float m) {
             wait_c(&ctl.bar_tot[j & 1], (uint32_t)(j >> 1) & 1u, status, abort_v);
             const int key = j % keys;
@@ -548,84 +658,102 @@ k_softmax_cluster(const float* __restrict__ x, float* y, int rows, int cols, int
                 }
                 float ex0 = __shfl_up_sync(tbk::kFull, inc, 1);
                 if (lane == 0) ex0 = 0.0f;
-                const float p0 = run + ex0, p1 = p0 + v0;
-                const int b0 = tbk::binade_of(p0), b1 = tbk::binade_of(p1);
-                if (2 * lane < nt)
-                    ctl.lmeta[2 * lane] = ((uint32_t)b0 & 0xffu) | (b0 == tbk::kNoBinade ? kExact : 0u);
-                if (2 * lane + 1 < nt)
-                    ctl.lmeta[2 * lane + 1] =
-                        ((uint32_t)b1 & 0xffu) | (b1 == tbk::kNoBinade ? kExact : 0u);
+                const float p0 = run + ex0, p1 = p0 + v0, p2 = p1 + v1;
+                auto meta_of = [](float a, float b) {
+                    const int ba = tbk::binade_of(a);
+                    uint32_t f = (uint32_t)ba & 0xffu;
+                    if (ba == tbk::kNoBinade) f |= kExact;
+                    if (tbk::binade_of(b) != ba || near_pow2(a) || near_pow2(b)) f |= kCross;
+                    return f;
+                };
+                if (2 * lane < nt) ctl.lmeta[2 * lane] = meta_of(p0, p1);
+                if (2 * lane + 1 < nt) ctl.lmeta[2 * lane + 1] = meta_of(p1, p2);
             }
             // the scanner of this key must be done with row j - keys
             if (j >= keys)
                 wait_c(&ctl.bar_sfree[key], (uint32_t)(j / keys - 1) & 1u, status, abort_v);
             work_sync();
             const float* s = seg(j % kNB);
-            const uint32_t rD = remote(&ctl.D[slot][0], tgt);
-            const uint32_t rM = remote(&ctl.meta[slot][0], tgt);
-            for (int t = wi; t < nt; t += kWorkW) {
-                const float* xt = s + t * kTileN;
-                const int n = min(kTileN, (col1 - col0) - t * kTileN);
+            auto units = [&](int t, const float4& a, const float4& c, bool& big, bool& tie,
+                             float& iu_out) -> uint32_t {
                 const uint32_t mt = ctl.lmeta[t];
-                const int b = (int)(int8_t)(mt & 0xffu);
-                uint2 D = make_uint2(0u, 0u);
-                if (!(mt & kExact)) {
-                    const float iu = tbk::inv_grid(b);
-                    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), c = a;
-                    if (n == kTileN) {
-                        a = *reinterpret_cast<const float4*>(xt + 4 * lane);
-                        c = *reinterpret_cast<const float4*>(xt + 128 + 4 * lane);
-                    } else {
-                        if (4 * lane < n) a = *reinterpret_cast<const float4*>(xt + 4 * lane);
-                        if (128 + 4 * lane < n)
-                            c = *reinterpret_cast<const float4*>(xt + 128 + 4 * lane);
-                        // (n is a multiple of 4: a float4 is wholly in or out)
-                    }
+                const float iu = tbk::inv_grid((int)(int8_t)(mt & 0xffu));
+                iu_out = iu;
+                const float e[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+                // Every term below 2^22 grid units makes the magic rounding
+                // exact: certain when the tile's estimate is below 2^21
+                // units, checked term by term otherwise.
+                const bool small = __fmul_rn(ctl.tsum[t], iu) < 2097152.0f;
+                uint32_t acc = 0;
+                float dm = 0.0f;
+                bool bad = false;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const float fa = __fmaf_rn(e[k], iu, kMagic);
+                    acc += __float_as_uint(fa);
+                    const float r = __fsub_rn(fa, kMagic);
+                    dm = fmaxf(dm, fabsf(__fmaf_rn(e[k], iu, -r)));
+                    if (!small) bad |= !(fa < 16777216.0f);  // t >= 2^22, or NaN
+                }
+                big = !small && __any_sync(tbk::kFull, bad);
+                tie = __any_sync(tbk::kFull, dm == 0.5f);
+                return __reduce_add_sync(tbk::kFull, acc - 8u * 0x4B400000u);
+            };
+            auto finish = [&](int t, const float4& a, const float4& c, uint32_t sum_u, bool big,
+                              bool tie, float iu) {
+                const uint32_t mt = ctl.lmeta[t];
+                uint2 D = make_uint2(sum_u, sum_u);
+                if (mt & kExact) {
+                    D = make_uint2(0u, 0u);
+                } else if (big) {
+                    D = make_uint2(kSat, kSat);
+                } else if (tie) {
                     const float e[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
-                    // Every term below 2^22 grid units makes the magic
-                    // rounding exact: certain when the tile's estimate is
-                    // below 2^21 units, checked term by term otherwise.
-                    const bool small = __fmul_rn(ctl.tsum[t], iu) < 2097152.0f;
-                    uint32_t acc = 0;
-                    float dm = 0.0f;
-                    bool bad = false;
+                    Fn fa{0u, 0u}, fb{0u, 0u};
 #pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        const float fa = __fmaf_rn(e[k], iu, kMagic);
-                        acc += __float_as_uint(fa);
-                        const float r = __fsub_rn(fa, kMagic);
-                        dm = fmaxf(dm, fabsf(__fmaf_rn(e[k], iu, -r)));
-                        if (!small) bad |= !(fa < 16777216.0f);  // t >= 2^22, or NaN
-                    }
-                    acc -= 8u * 0x4B400000u;  // sum of the eight rne(t), mod 2^32
-                    const bool big = !small && __any_sync(tbk::kFull, bad);
-                    const bool tie = __any_sync(tbk::kFull, dm == 0.5f);
-                    const uint32_t sum_u = __reduce_add_sync(tbk::kFull, acc);
-                    D = make_uint2(sum_u, sum_u);
-                    if (big) {
-                        D = make_uint2(kSat, kSat);
-                    } else if (tie) {
-                        Fn fa{0u, 0u}, fb{0u, 0u};
+                    for (int k = 0; k < 4; ++k) fa = compose(fa, term_fn(e[k], iu));
 #pragma unroll
-                        for (int k = 0; k < 4; ++k) fa = compose(fa, term_fn(e[k], iu));
-#pragma unroll
-                        for (int k = 4; k < 8; ++k) fb = compose(fb, term_fn(e[k], iu));
-                        fa = warp_compose(fa);
-                        fb = warp_compose(fb);
-                        const Fn ft = compose(fa, fb);
-                        D = make_uint2(ft.a0, ft.a1);
-                    }
+                    for (int k = 4; k < 8; ++k) fb = compose(fb, term_fn(e[k], iu));
+                    fa = warp_compose(fa);
+                    fb = warp_compose(fb);
+                    const Fn ft = compose(fa, fb);
+                    D = make_uint2(ft.a0, ft.a1);
                 }
                 if (lane == 0) {
-                    st_remote(rD + 8u * (uint32_t)(t0 + t), D);
-                    st_remote(rM + 4u * (uint32_t)(t0 + t), mt);
+                    ctl.D[key][t] = D;
+                    ctl.meta[key][t] = mt;
                 }
+            };
+            for (int t = wi; t < nt; t += 2 * kWorkW) {
+                const int u = t + kWorkW;
+                float4 a, c, a2, c2;
+                ld2(s + t * kTileN, t, a, c);
+                if (u < nt) ld2(s + u * kTileN, u, a2, c2);
+                // terms past the row are -inf before the exp pass and 0 after it
+                if (t >= nfull) {
+                    const int n = (col1 - col0) - t * kTileN;
+                    if (4 * lane >= n) a = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (128 + 4 * lane >= n) c = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+                if (u < nt && u >= nfull) {
+                    const int n = (col1 - col0) - u * kTileN;
+                    if (4 * lane >= n) a2 = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (128 + 4 * lane >= n) c2 = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+                bool big1, tie1, big2 = false, tie2 = false;
+                float iu1, iu2 = 0.0f;
+                const uint32_t s1 = units(t, a, c, big1, tie1, iu1);
+                uint32_t s2 = 0;
+                if (u < nt) s2 = units(u, a2, c2, big2, tie2, iu2);
+                finish(t, a, c, s1, big1, tie1, iu1);
+                if (u < nt) finish(u, a2, c2, s2, big2, tie2, iu2);
             }
-            // this warp's summary stores, ordered before the arrive below
-            if (lane == 0) asm volatile("fence.acq_rel.cluster;" ::: "memory");
+            if (me == 0 && wi == 0 && lane == 0) ctl.row_m[key] = m;
             work_sync();
             if (wi == 0 && lane == 0) {
-                if (me == 0) st_remote(remote(&ctl.row_m[slot], tgt), m);
+                // every worker's summary stores (ordered by the barrier above)
+                // before the scanner's CTA sees this CTA arrive
+                asm volatile("fence.acq_rel.cluster;" ::: "memory");
                 arrive_remote(remote(&ctl.bar_ready[slot], tgt));
             }
             // the buffer is free: the row kNB ahead is copied into it
