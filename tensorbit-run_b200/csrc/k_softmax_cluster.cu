@@ -50,6 +50,7 @@
 // leaves while a peer may write its shared memory, and no copy is in flight
 // when a CTA exits.  Only this GPU's memory is read; no multicast.
 #include <math.h>
+#include <stddef.h>
 
 #include <type_traits>
 
@@ -96,7 +97,7 @@ struct Ctl {
     float res_sum[kKeys];                // row results, by key j % (C * kScanW)
     float res_m[kKeys];
     float red[kWorkW];
-    float scratch[kScanW][kTileN];       // tile 0 of a scanner's row
+    __align__(16) float scratch[kScanW][kTileN];  // tile 0 of a scanner's row (float4 reads)
     uint64_t bar_x[kNB];                 // segment landed
     uint64_t bar_max[2], bar_tot[2];     // C arrivals
     uint64_t bar_sfree[kKeys];           // scanner of that key is done with the summaries
@@ -105,6 +106,13 @@ struct Ctl {
     uint64_t bar_fcred[kScanW];          // C * kFinW arrivals: result slot read everywhere
     int abort_flag;
 };
+
+// Members read or written with vector accesses start on their access size.
+static_assert(offsetof(Ctl, D) % 8 == 0, "uint2 summaries");
+static_assert(offsetof(Ctl, scratch) % 16 == 0, "float4 reads of the scratch tile");
+static_assert(offsetof(Ctl, bar_x) % 8 == 0 && offsetof(Ctl, bar_max) % 8 == 0 &&
+                  offsetof(Ctl, bar_sfree) % 8 == 0 && offsetof(Ctl, bar_fcred) % 8 == 0,
+              "mbarriers");
 
 // ------------------------------------------------------------- cluster PTX
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -132,13 +140,6 @@ __device__ __forceinline__ uint32_t remote(const void* p, uint32_t cta) {
 }
 __device__ __forceinline__ void st_remote(uint32_t a, float v) {
     asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
-}
-__device__ __forceinline__ void st_remote(uint32_t a, uint32_t v) {
-    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
-}
-__device__ __forceinline__ void st_remote(uint32_t a, uint2 v) {
-    asm volatile("st.shared::cluster.v2.u32 [%0], {%1, %2};" ::"r"(a), "r"(v.x), "r"(v.y)
-                 : "memory");
 }
 __device__ __forceinline__ uint2 ld_remote_u2(uint32_t a) {
     uint2 v;
