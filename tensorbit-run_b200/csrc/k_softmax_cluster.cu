@@ -141,6 +141,21 @@ __device__ __forceinline__ uint32_t remote(const void* p, uint32_t cta) {
 __device__ __forceinline__ void st_remote(uint32_t a, float v) {
     asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
 }
+// 16-byte loads and stores of this CTA's shared memory by 32-bit shared
+// address, so the segment buffers are never reached through generic pointers.
+__device__ __forceinline__ float4 lds4(uint32_t a) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void sts4(uint32_t a, const float4& v) {
+    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(v.x), "f"(v.y),
+                 "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+
 __device__ __forceinline__ uint2 ld_remote_u2(uint32_t a) {
     uint2 v;
     asm volatile("ld.shared::cluster.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a)
@@ -528,6 +543,11 @@ k_softmax_cluster(const float* __restrict__ x, float* y, int rows, int cols, int
         const bool producer = wi == 0 && lane == 0;
         const uint64_t pol_keep = tbk::policy_evict_last();  // the finalizers read x again
         auto seg = [&](int b) { return xbuf + (size_t)b * seg_floats; };
+        const uint32_t xbuf_s = tbk::smem_addr(xbuf);
+        // shared address of term 0 of tile t of buffer b
+        auto tile_s = [&](int b, int t) {
+            return xbuf_s + (uint32_t)(b * seg_floats + t * kTileN) * 4u;
+        };
         auto issue = [&](int j) {  // one thread: row j's segment into buffer j % kNB
             const int b = j % kNB;
             tbk::mbar_expect_tx(&ctl.bar_x[b], seg_bytes);
@@ -540,35 +560,34 @@ k_softmax_cluster(const float* __restrict__ x, float* y, int rows, int cols, int
             for (; issued < min(kNB, nloc); ++issued) issue(issued);
         const int nfull = (col1 - col0) / kTileN;  // full tiles of the segment
         // lane l holds terms 4l..4l+3 and 128+4l..128+4l+3 of a tile
-        auto ld2 = [&](const float* xt, int t, float4& a, float4& c) {
+        auto ld2 = [&](uint32_t ts, int t, float4& a, float4& c) {
             if (t < nfull) {
-                a = *reinterpret_cast<const float4*>(xt + 4 * lane);
-                c = *reinterpret_cast<const float4*>(xt + 128 + 4 * lane);
+                a = lds4(ts + 16u * lane);
+                c = lds4(ts + 512u + 16u * lane);
             } else {  // the row's ragged last tile (a multiple of 4 terms)
                 const int n = (col1 - col0) - t * kTileN;
                 a = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
                 c = a;
-                if (4 * lane < n) a = *reinterpret_cast<const float4*>(xt + 4 * lane);
-                if (128 + 4 * lane < n) c = *reinterpret_cast<const float4*>(xt + 128 + 4 * lane);
+                if (4 * lane < n) a = lds4(ts + 16u * lane);
+                if (128 + 4 * lane < n) c = lds4(ts + 512u + 16u * lane);
             }
         };
-        auto st2 = [&](float* xt, int t, const float4& a, const float4& c) {
+        auto st2 = [&](uint32_t ts, int t, const float4& a, const float4& c) {
             const int n = t < nfull ? kTileN : (col1 - col0) - t * kTileN;
-            if (4 * lane < n) *reinterpret_cast<float4*>(xt + 4 * lane) = a;
-            if (128 + 4 * lane < n) *reinterpret_cast<float4*>(xt + 128 + 4 * lane) = c;
+            if (4 * lane < n) sts4(ts + 16u * lane, a);
+            if (128 + 4 * lane < n) sts4(ts + 512u + 16u * lane, c);
         };
 
         // Phase A: segment max -> every CTA.
         auto phase_a = [&](int j) {
             const int b = j % kNB;
             wait_c(&ctl.bar_x[b], (uint32_t)(j / kNB) & 1u, status, abort_v);
-            const float* s = seg(b);
             float mx = -INFINITY, my = -INFINITY;
             for (int t = wi; t < nt; t += 2 * kWorkW) {
                 const int u = t + kWorkW;
                 float4 a, c, a2, c2;
-                ld2(s + t * kTileN, t, a, c);
-                if (u < nt) ld2(s + u * kTileN, u, a2, c2);
+                ld2(tile_s(b, t), t, a, c);
+                if (u < nt) ld2(tile_s(b, u), u, a2, c2);
                 mx = fmaxf(mx, fmaxf(fmaxf(fmaxf(a.x, a.y), fmaxf(a.z, a.w)),
                                      fmaxf(fmaxf(c.x, c.y), fmaxf(c.z, c.w))));
                 if (u < nt)
@@ -594,7 +613,7 @@ k_softmax_cluster(const float* __restrict__ x, float* y, int rows, int cols, int
             float m = ctl.xmax[j & 1][0];
             for (int c = 1; c < ncl; ++c) m = fmaxf(m, ctl.xmax[j & 1][c]);
             const Expo ex(m);
-            float* s = seg(j % kNB);
+            const int b = j % kNB;
             auto run = [&](auto slow_tag) {
                 constexpr bool SLOW = decltype(slow_tag)::value;
                 auto e4 = [&](float4& v) {
@@ -604,14 +623,14 @@ k_softmax_cluster(const float* __restrict__ x, float* y, int rows, int cols, int
                 for (int t = wi; t < nt; t += 2 * kWorkW) {
                     const int u = t + kWorkW;
                     float4 a, c, a2, c2;
-                    ld2(s + t * kTileN, t, a, c);
-                    if (u < nt) ld2(s + u * kTileN, u, a2, c2);
+                    ld2(tile_s(b, t), t, a, c);
+                    if (u < nt) ld2(tile_s(b, u), u, a2, c2);
                     e4(a); e4(c);
                     if (u < nt) {
                         e4(a2); e4(c2);
                     }
-                    st2(s + t * kTileN, t, a, c);
-                    if (u < nt) st2(s + u * kTileN, u, a2, c2);
+                    st2(tile_s(b, t), t, a, c);
+                    if (u < nt) st2(tile_s(b, u), u, a2, c2);
                     const float s1 = warp_sum_est(((a.x + a.y) + (a.z + a.w)) +
                                                   ((c.x + c.y) + (c.z + c.w)));
                     if (lane == 0) ctl.tsum[t] = s1;
@@ -674,7 +693,7 @@ k_softmax_cluster(const float* __restrict__ x, float* y, int rows, int cols, int
             if (j >= keys)
                 wait_c(&ctl.bar_sfree[key], (uint32_t)(j / keys - 1) & 1u, status, abort_v);
             work_sync();
-            const float* s = seg(j % kNB);
+            const int b = j % kNB;
             auto units = [&](int t, const float4& a, const float4& c, bool& big, bool& tie,
                              float& iu_out) -> uint32_t {
                 const uint32_t mt = ctl.lmeta[t];
@@ -728,8 +747,8 @@ k_softmax_cluster(const float* __restrict__ x, float* y, int rows, int cols, int
             for (int t = wi; t < nt; t += 2 * kWorkW) {
                 const int u = t + kWorkW;
                 float4 a, c, a2, c2;
-                ld2(s + t * kTileN, t, a, c);
-                if (u < nt) ld2(s + u * kTileN, u, a2, c2);
+                ld2(tile_s(b, t), t, a, c);
+                if (u < nt) ld2(tile_s(b, u), u, a2, c2);
                 // terms past the row are -inf before the exp pass and 0 after it
                 if (t >= nfull) {
                     const int n = (col1 - col0) - t * kTileN;
