@@ -86,33 +86,34 @@ __device__ __forceinline__ int scanner_of(int w) { return (w & 3) == 0 && w < 12
 __device__ __forceinline__ int finalizer_of(int w) { return w >= 12 ? w - 12 : -1; }
 __device__ __forceinline__ int worker_of(int w) { return w - 1 - (w >> 2); }
 
+// Cross-CTA words carry their row: (seq << 32) | payload bits, seq = row + 1
+// (0: never written).  A reader polls the word until the seq is the row it
+// wants, so the payload needs no separate signal and no fence.
 struct Ctl {
-    uint2 D[kKeys][kSegTiles];           // this CTA's summaries of the row of key k
-    uint32_t meta[kKeys][kSegTiles];     // predicted binade (int8) | kExact | kCross
-    float row_m[kKeys];                  // the row max (read from CTA 0 by the scanner)
+    uint64_t sumw[kKeys][kSegTiles];     // this CTA's tile summaries of the row of key k
+    uint64_t rowm[kKeys];                // the row max of the row of key k (this CTA's copy)
+    uint64_t res[kKeys];                 // the row sum, from the row's scanner
+    uint64_t resm[kKeys];                // the row max, from the row's scanner
+    uint64_t xm[2][kMaxC];               // segment maxima of rows of parity p
+    uint64_t xt[2][kMaxC];               // segment sum estimates
     float tsum[kSegTiles];               // this CTA's tile sum estimates
     uint32_t lmeta[kSegTiles];           // this CTA's predicted binades and flags
-    float xmax[2][kMaxC];                // segment maxima of rows of parity p
-    float xtot[2][kMaxC];                // segment sum estimates
-    float res_sum[kKeys];                // row results, by key j % (C * kScanW)
-    float res_m[kKeys];
     float red[kWorkW];
     __align__(16) float scratch[kScanW][kTileN];  // tile 0 of a scanner's row (float4 reads)
     uint64_t bar_x[kNB];                 // segment landed
-    uint64_t bar_max[2], bar_tot[2];     // C arrivals
     uint64_t bar_sfree[kKeys];           // scanner of that key is done with the summaries
-    uint64_t bar_ready[kScanW];          // C arrivals: every CTA's summaries of the row
-    uint64_t bar_res[kKeys];             // the row's result is here
     uint64_t bar_fcred[kScanW];          // C * kFinW arrivals: result slot read everywhere
     int abort_flag;
 };
 
 // Members read or written with vector accesses start on their access size.
-static_assert(offsetof(Ctl, D) % 8 == 0, "uint2 summaries");
+static_assert(offsetof(Ctl, sumw) % 8 == 0 && offsetof(Ctl, rowm) % 8 == 0 &&
+                  offsetof(Ctl, res) % 8 == 0 && offsetof(Ctl, resm) % 8 == 0 &&
+                  offsetof(Ctl, xm) % 8 == 0 &&
+                  offsetof(Ctl, xt) % 8 == 0, "64-bit words");
 static_assert(offsetof(Ctl, scratch) % 16 == 0, "float4 reads of the scratch tile");
-static_assert(offsetof(Ctl, bar_x) % 8 == 0 && offsetof(Ctl, bar_max) % 8 == 0 &&
-                  offsetof(Ctl, bar_sfree) % 8 == 0 && offsetof(Ctl, bar_fcred) % 8 == 0,
-              "mbarriers");
+static_assert(offsetof(Ctl, bar_x) % 8 == 0 && offsetof(Ctl, bar_sfree) % 8 == 0 &&
+                  offsetof(Ctl, bar_fcred) % 8 == 0, "mbarriers");
 
 // ------------------------------------------------------------- cluster PTX
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -138,9 +139,6 @@ __device__ __forceinline__ uint32_t remote(const void* p, uint32_t cta) {
                  : "r"(tbk::smem_addr(p)), "r"(cta));
     return r;
 }
-__device__ __forceinline__ void st_remote(uint32_t a, float v) {
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
-}
 // 16-byte loads and stores of this CTA's shared memory by 32-bit shared
 // address, so the segment buffers are never reached through generic pointers.
 __device__ __forceinline__ float4 lds4(uint32_t a) {
@@ -156,21 +154,61 @@ __device__ __forceinline__ void sts4(uint32_t a, const float4& v) {
                  : "memory");
 }
 
-__device__ __forceinline__ uint2 ld_remote_u2(uint32_t a) {
-    uint2 v;
-    asm volatile("ld.shared::cluster.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a)
-                 : "memory");
+// Tagged words: relaxed 64-bit stores and loads at cluster scope (one
+// store is seen whole), local or in another CTA of the cluster.
+__device__ __forceinline__ uint64_t tag(uint32_t seq, uint32_t payload) {
+    return ((uint64_t)seq << 32) | payload;
+}
+__device__ __forceinline__ void put_word(uint32_t a, uint64_t v) {  // a: cluster address
+    asm volatile("st.relaxed.cluster.shared::cluster.u64 [%0], %1;" ::"r"(a), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t get_word(uint32_t a) {  // a: cluster address
+    uint64_t v;
+    asm volatile("ld.relaxed.cluster.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(a) : "memory");
     return v;
 }
-__device__ __forceinline__ uint32_t ld_remote_u32(uint32_t a) {
-    uint32_t v;
-    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
-    return v;
+
+// Poll lane-wise words until each active lane's word carries `seq` (each
+// lane its own address; inactive lanes pass).  Bounded like every wait: on
+// timeout raise the flag, set the abort flag and return what was read.
+__device__ __forceinline__ uint64_t poll_word(uint32_t a, bool active, uint32_t seq,
+                                              unsigned* status, volatile int* abort_flag) {
+    uint64_t v = active ? get_word(a) : 0;
+    if (__all_sync(tbk::kFull, !active || (uint32_t)(v >> 32) == seq) || *abort_flag) return v;
+    const uint64_t t0 = tbk::global_ns();
+    for (;;) {
+        if (active) v = get_word(a);
+        if (__all_sync(tbk::kFull, !active || (uint32_t)(v >> 32) == seq)) return v;
+        if (tbk::global_ns() - t0 > 2000000000ull) {
+            if ((threadIdx.x & 31) == 0) atomicOr(status, tbk::kFlagTimeout);
+            *abort_flag = 1;
+            return v;
+        }
+    }
 }
-__device__ __forceinline__ float ld_remote_f32(uint32_t a) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
-    return v;
+
+// A tile summary in one word: D0 (31 bits), D1 - D0 (10 bits, signed), the
+// predicted binade (8 bits), kExact, kCross (bits 49, 50), and the row's
+// seq modulo 2^13 (bits 51..63).
+constexpr int kSeqBits = 13;
+__device__ __forceinline__ uint64_t pack_summary(uint2 D, uint32_t mt, uint32_t seq) {
+    const int dd = (int)D.y - (int)D.x;
+    uint64_t w = (uint64_t)(D.x & 0x7fffffffu);
+    w |= (uint64_t)((uint32_t)dd & 0x3ffu) << 31;
+    w |= (uint64_t)(mt & 0xffu) << 41;
+    w |= (uint64_t)((mt & kExact) ? 1u : 0u) << 49;
+    w |= (uint64_t)((mt & kCross) ? 1u : 0u) << 50;
+    w |= (uint64_t)(seq & ((1u << kSeqBits) - 1u)) << 51;
+    return w;
+}
+__device__ __forceinline__ uint32_t summary_seq(uint64_t w) { return (uint32_t)(w >> 51); }
+__device__ __forceinline__ void unpack_summary(uint64_t w, uint2& D, uint32_t& mt) {
+    D.x = (uint32_t)(w & 0x7fffffffu);
+    const int dd = ((int)((uint32_t)(w >> 31) & 0x3ffu) << 22) >> 22;
+    D.y = (uint32_t)((int)D.x + dd);
+    mt = (uint32_t)(w >> 41) & 0xffu;
+    if ((w >> 49) & 1u) mt |= kExact;
+    if ((w >> 50) & 1u) mt |= kCross;
 }
 
 // One arrival on an mbarrier of any CTA of the cluster, ordered after this
@@ -325,8 +363,9 @@ __device__ __forceinline__ void resolve_tile(tbk::RunSum& st, const float (&xv)[
 
 // The in-order sum of the row from the summaries in the cluster's CTAs
 // (tile t: CTA t / seg_tiles, slot `key`; lane-uniform result).
-__device__ float scan_row(const Ctl& ctl, int key, int seg_tiles, float* scratch, const float* xr,
-                          const Expo& ex, int cols) {
+__device__ float scan_row(Ctl& ctl, int key, uint32_t seq, int seg_tiles, float* scratch,
+                          const float* xr, const Expo& ex, int cols, unsigned* status,
+                          volatile int* abort_flag) {
     const int lane = threadIdx.x & 31;
     const int ntiles = (cols + kTileN - 1) / kTileN;
     // tile 0: strictly in order, one lane (four terms per shared load)
@@ -350,11 +389,27 @@ __device__ float scan_row(const Ctl& ctl, int key, int seg_tiles, float* scratch
         const int cnt = min(32, ntiles - t0);
         uint2 dl = make_uint2(0u, 0u);
         uint32_t mt = 0;
-        if (lane < cnt) {
+        {
             const int t = t0 + lane;
-            const uint32_t c = (uint32_t)(t / seg_tiles), i = (uint32_t)(t % seg_tiles);
-            dl = ld_remote_u2(remote(&ctl.D[key][i], c));
-            mt = ld_remote_u32(remote(&ctl.meta[key][i], c));
+            const uint32_t a = lane < cnt ? remote(&ctl.sumw[key][t % seg_tiles],
+                                                   (uint32_t)(t / seg_tiles))
+                                          : 0u;
+            // a summary word is there once it carries this row's seq
+            const uint32_t want = seq & ((1u << kSeqBits) - 1u);
+            uint64_t w = lane < cnt ? get_word(a) : 0;
+            if (!__all_sync(tbk::kFull, lane >= cnt || summary_seq(w) == want) && !*abort_flag) {
+                const uint64_t ts = tbk::global_ns();
+                for (;;) {
+                    if (lane < cnt) w = get_word(a);
+                    if (__all_sync(tbk::kFull, lane >= cnt || summary_seq(w) == want)) break;
+                    if (tbk::global_ns() - ts > 2000000000ull) {
+                        if (lane == 0) atomicOr(status, tbk::kFlagTimeout);
+                        *abort_flag = 1;
+                        break;
+                    }
+                }
+            }
+            if (lane < cnt) unpack_summary(w, dl, mt);
         }
         const int tb = (int)(int8_t)(mt & 0xffu);
         // the first tile predicted to cross: its x is on its way during the scan
@@ -444,20 +499,15 @@ k_softmax_cluster(const float* __restrict__ x, float* y, int rows, int cols, int
 
     if (threadIdx.x == 0) {
         for (int b = 0; b < kNB; ++b) tbk::mbar_init(&ctl.bar_x[b], 1);
-        for (int p = 0; p < 2; ++p) {
-            tbk::mbar_init(&ctl.bar_max[p], nc);
-            tbk::mbar_init(&ctl.bar_tot[p], nc);
-        }
-        for (int k = 0; k < kKeys; ++k) {
-            tbk::mbar_init(&ctl.bar_sfree[k], 1);
-            tbk::mbar_init(&ctl.bar_res[k], 1);
-        }
-        for (int s = 0; s < kScanW; ++s) {
-            tbk::mbar_init(&ctl.bar_ready[s], nc);
-            tbk::mbar_init(&ctl.bar_fcred[s], nc * kFinW);
-        }
+        for (int k = 0; k < kKeys; ++k) tbk::mbar_init(&ctl.bar_sfree[k], 1);
+        for (int s = 0; s < kScanW; ++s) tbk::mbar_init(&ctl.bar_fcred[s], nc * kFinW);
         ctl.abort_flag = 0;
         tbk::fence_mbar_init();
+    }
+    {  // every tagged word starts with seq 0: never written
+        uint64_t* w = &ctl.sumw[0][0];
+        const int n = (int)((reinterpret_cast<uint64_t*>(&ctl.tsum) - w));
+        for (int i = threadIdx.x; i < n; i += kNT) w[i] = 0;
     }
     __syncthreads();
     cluster_sync_all();  // every CTA's barriers exist before any remote arrive
@@ -471,22 +521,25 @@ k_softmax_cluster(const float* __restrict__ x, float* y, int rows, int cols, int
         const int key = (int)me + ncl * sw;
         for (int k = 0;; ++k) {
             const int j = key + keys * k;
-            if (j >= nloc) break;
-            if (!wait_c(&ctl.bar_ready[sw], (uint32_t)k & 1u, status, abort_v)) break;
-            const float m = ld_remote_f32(remote(&ctl.row_m[key], 0u));
+            if (j >= nloc || *abort_v) break;
+            const uint32_t seq = (uint32_t)j + 1u;
+            const uint64_t mw = poll_word(tbk::smem_addr(&ctl.rowm[key]), true, seq, status, abort_v);
+            const float m = __uint_as_float((uint32_t)mw);
             const Expo ex(m);
             const float* xr = x + row_of(j) * row_stride;
-            const float sum = scan_row(ctl, key, seg_tiles, ctl.scratch[sw], xr, ex, cols);
+            const float sum =
+                scan_row(ctl, key, seq, seg_tiles, ctl.scratch[sw], xr, ex, cols, status, abort_v);
             // the summaries are read: every CTA may write its next row of this key
             __syncwarp();
             if (lane < ncl) arrive_remote(remote(&ctl.bar_sfree[key], (uint32_t)lane));
             // the result slot is free once every finalizer read row j - keys
             if (k >= 1 && !wait_c(&ctl.bar_fcred[sw], (uint32_t)(k - 1) & 1u, status, abort_v))
                 break;
+            // the result to every CTA: the sum, and the max (the workers'
+            // copy of it may already hold a later row when a finalizer looks)
             if (lane < ncl) {
-                st_remote(remote(&ctl.res_sum[key], (uint32_t)lane), sum);
-                st_remote(remote(&ctl.res_m[key], (uint32_t)lane), m);
-                arrive_remote(remote(&ctl.bar_res[key], (uint32_t)lane));
+                put_word(remote(&ctl.resm[key], (uint32_t)lane), tag(seq, __float_as_uint(m)));
+                put_word(remote(&ctl.res[key], (uint32_t)lane), tag(seq, __float_as_uint(sum)));
             }
         }
     } else if (fw >= 0) {
@@ -498,9 +551,12 @@ k_softmax_cluster(const float* __restrict__ x, float* y, int rows, int cols, int
         const int nv = (col1 - col0) / 4;
         for (int j = 0; j < nloc; ++j) {
             const int key = j % keys;
-            if (!wait_c(&ctl.bar_res[key], (uint32_t)(j / keys) & 1u, status, abort_v)) break;
-            const float sum = ctl.res_sum[key];
-            const float m = ctl.res_m[key];
+            const uint32_t seq = (uint32_t)j + 1u;
+            const float sum = __uint_as_float(
+                (uint32_t)poll_word(tbk::smem_addr(&ctl.res[key]), true, seq, status, abort_v));
+            const float m = __uint_as_float(
+                (uint32_t)poll_word(tbk::smem_addr(&ctl.resm[key]), true, seq, status, abort_v));
+            if (*abort_v) break;
             __syncwarp();
             if (lane == 0)
                 arrive_remote(remote(&ctl.bar_fcred[key / ncl], (uint32_t)(key % ncl)));
@@ -601,17 +657,17 @@ k_softmax_cluster(const float* __restrict__ x, float* y, int rows, int cols, int
                 float mc = ctl.red[0];
 #pragma unroll
                 for (int w = 1; w < kWorkW; ++w) mc = fmaxf(mc, ctl.red[w]);
-                if (lane < ncl) {
-                    st_remote(remote(&ctl.xmax[j & 1][me], (uint32_t)lane), mc);
-                    arrive_remote(remote(&ctl.bar_max[j & 1], (uint32_t)lane));
-                }
+                if (lane < ncl)
+                    put_word(remote(&ctl.xm[j & 1][me], (uint32_t)lane),
+                             tag((uint32_t)j + 1u, __float_as_uint(mc)));
             }
         };
         // Phase B: e in place, tile estimates, segment estimate -> every CTA.
         auto phase_b = [&](int j) -> float {
-            wait_c(&ctl.bar_max[j & 1], (uint32_t)(j >> 1) & 1u, status, abort_v);
-            float m = ctl.xmax[j & 1][0];
-            for (int c = 1; c < ncl; ++c) m = fmaxf(m, ctl.xmax[j & 1][c]);
+            // every warp reads the cluster's segment maxima itself (lane c: CTA c's)
+            const uint64_t mw = poll_word(tbk::smem_addr(&ctl.xm[j & 1][lane & (kMaxC - 1)]),
+                                          lane < ncl, (uint32_t)j + 1u, status, abort_v);
+            const float m = tbk::warp_max(lane < ncl ? __uint_as_float((uint32_t)mw) : -INFINITY);
             const Expo ex(m);
             const int b = j % kNB;
             auto run = [&](auto slow_tag) {
@@ -650,23 +706,25 @@ k_softmax_cluster(const float* __restrict__ x, float* y, int rows, int cols, int
                 float v = 0.0f;
                 for (int t = lane; t < nt; t += 32) v += ctl.tsum[t];
                 v = tbk::warp_sum(v);
-                if (lane < ncl) {
-                    st_remote(remote(&ctl.xtot[j & 1][me], (uint32_t)lane), v);
-                    arrive_remote(remote(&ctl.bar_tot[j & 1], (uint32_t)lane));
-                }
+                if (lane < ncl)
+                    put_word(remote(&ctl.xt[j & 1][me], (uint32_t)lane),
+                             tag((uint32_t)j + 1u, __float_as_uint(v)));
             }
             return m;
         };
         // Phase C: predicted binades, (D0, D1) per tile -> this CTA's summary
         // slot of the row's key; one arrive tells the row's scanner.
         auto phase_c = [&](int j, float m) {
-            wait_c(&ctl.bar_tot[j & 1], (uint32_t)(j >> 1) & 1u, status, abort_v);
             const int key = j % keys;
-            const uint32_t tgt = (uint32_t)(key % ncl);
-            const int slot = key / ncl;
+            const uint32_t seq = (uint32_t)j + 1u;
             if (wi == 0) {
-                float run = 0.0f;  // estimate of the running sum at the segment start
-                for (int c = 0; c < (int)me; ++c) run += ctl.xtot[j & 1][c];
+                // the segments' sum estimates; the running sum at this
+                // segment's start is the sum of those before it
+                const uint64_t tw = poll_word(tbk::smem_addr(&ctl.xt[j & 1][lane & (kMaxC - 1)]),
+                                              lane < ncl, seq, status, abort_v);
+                float run = 0.0f;
+                for (int c = 0; c < (int)me; ++c)
+                    run += __uint_as_float((uint32_t)__shfl_sync(tbk::kFull, (uint32_t)tw, c));
                 // warp scan of the segment's tile estimates (two per lane)
                 const float v0 = 2 * lane < nt ? ctl.tsum[2 * lane] : 0.0f;
                 const float v1 = 2 * lane + 1 < nt ? ctl.tsum[2 * lane + 1] : 0.0f;
@@ -739,10 +797,14 @@ k_softmax_cluster(const float* __restrict__ x, float* y, int rows, int cols, int
                     const Fn ft = compose(fa, fb);
                     D = make_uint2(ft.a0, ft.a1);
                 }
-                if (lane == 0) {
-                    ctl.D[key][t] = D;
-                    ctl.meta[key][t] = mt;
+                const int dd = (int)D.y - (int)D.x;
+                uint32_t mw = mt;
+                if (dd < -512 || dd > 511) {  // cannot be packed: term by term
+                    D = make_uint2(0u, 0u);
+                    mw |= kExact;
                 }
+                if (lane == 0)
+                    put_word(tbk::smem_addr(&ctl.sumw[key][t]), pack_summary(D, mw, seq));
             };
             for (int t = wi; t < nt; t += 2 * kWorkW) {
                 const int u = t + kWorkW;
@@ -768,14 +830,10 @@ k_softmax_cluster(const float* __restrict__ x, float* y, int rows, int cols, int
                 finish(t, a, c, s1, big1, tie1, iu1);
                 if (u < nt) finish(u, a2, c2, s2, big2, tie2, iu2);
             }
-            if (me == 0 && wi == 0 && lane == 0) ctl.row_m[key] = m;
+            // the row max for this CTA's scanner and finalizers
+            if (wi == 0 && lane == 0)
+                put_word(tbk::smem_addr(&ctl.rowm[key]), tag(seq, __float_as_uint(m)));
             work_sync();
-            if (wi == 0 && lane == 0) {
-                // every worker's summary stores (ordered by the barrier above)
-                // before the scanner's CTA sees this CTA arrive
-                asm volatile("fence.acq_rel.cluster;" ::: "memory");
-                arrive_remote(remote(&ctl.bar_ready[slot], tgt));
-            }
             // the buffer is free: the row kNB ahead is copied into it
             if (producer && issued < nloc && !*abort_v) {
                 tbk::fence_proxy_async_shared();
