@@ -562,7 +562,9 @@ extern "C" int tb_b200_softmax(int dtype, int64_t rows, int64_t cols, const void
     cudaStream_t s = tbh::stream_of(stream);
     if (dtype == TB_DTYPE_F32) {
         if (!mask) {
-            int rc = tbh::softmax_cluster_f32(rows, cols, static_cast<const float*>(x),
+            int rc = 1;
+            if (tbh::softmax_use_cluster())
+                rc = tbh::softmax_cluster_f32(rows, cols, static_cast<const float*>(x),
                                               static_cast<float*>(y), s);
             if (rc != 1) return rc;
             rc = tbh::softmax_staged_f32(rows, cols, static_cast<const float*>(x),

@@ -50,6 +50,8 @@
 // leaves while a peer may write its shared memory, and no copy is in flight
 // when a CTA exits.  Only this GPU's memory is read; no multicast.
 #include <math.h>
+#include <stdlib.h>
+#include <string.h>
 #include <stddef.h>
 
 #include <type_traits>
@@ -862,6 +864,11 @@ k_softmax_cluster(const float* __restrict__ x, float* y, int rows, int cols, int
 }  // namespace
 
 namespace tbh {
+
+bool softmax_use_cluster() {
+    const char* e = getenv("TB_B200_SOFTMAX");
+    return e && !strcmp(e, "cluster");
+}
 
 // f32 softmax through k_softmax_cluster.  Returns 1 (nothing launched) when
 // the shape is not one it handles: fewer than 1024 or more than 131072

@@ -65,6 +65,10 @@ int softmax_staged_f32(int64_t rows, int64_t cols, const float* x, float* y, cud
 // f32 softmax with each row split over a thread-block cluster
 // (k_softmax_cluster.cu): same return convention.
 int softmax_cluster_f32(int64_t rows, int64_t cols, const float* x, float* y, cudaStream_t s);
+// Whether f32 softmax tries the cluster kernel first: TB_B200_SOFTMAX=cluster
+// in the environment (read at each call); otherwise the staged and tiled
+// kernels.
+bool softmax_use_cluster();
 
 }  // namespace tbh
 

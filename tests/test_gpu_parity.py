@@ -254,14 +254,15 @@ def test_rope_single_position_and_odd_head_dim(dev):
 
 
 # ----------------------------------------------------------------- softmax
-# f32 rows of 1024 to 131072 columns (a multiple of 4, no mask, aligned)
-# take the cluster kernel: C = ceil(tiles / 64) CTAs per row, 256-term tiles.
-# "pipeline" gives every cluster many rows (C = 1); "staged_max" (C = 2) and
-# "past_staged" (C = 3, a last tile of 4 terms); "c5" 5 CTAs of 64 tiles;
-# "c3_ragged" a last tile of 4 terms; "cluster_max" the widest row (8 CTAs
-# of 64 tiles); "c8_spiky" 8 CTAs with many binade crossings; "odd" and
-# "one" are below the cluster kernel's width and take the tiled kernel,
-# as do all bf16 cases.
+# By default f32 rows of up to 32768 columns (a multiple of 4, no mask,
+# aligned) take the shared-memory-staged kernel and the rest the tiled one;
+# with TB_B200_SOFTMAX=cluster, rows of 1024 to 131072 such columns take the
+# cluster kernel (C = ceil(tiles / 64) CTAs per row, 256-term tiles).
+# "pipeline" gives every CTA many rows (cluster: C = 1); "staged_max" the
+# widest staged row (C = 2) and "past_staged" the first width beyond it (C =
+# 3, a last tile of 4 terms); "c5" 5 CTAs of 64 tiles; "c3_ragged" a last
+# tile of 4 terms; "cluster_max" the cluster kernel's widest row (8 CTAs of
+# 64 tiles); "c8_spiky" many binade crossings; bf16 takes the tiled kernel.
 SOFTMAX_CASES = [("mock", 64, 100, 2.0), ("7b", 256, 32000, 3.0), ("70b", 16, 128256, 3.0),
                  ("odd", 9, 1001, 3.0), ("one", 3, 1, 1.0), ("wide_std", 8, 5000, 20.0),
                  ("pipeline", 600, 4096, 3.0), ("staged_max", 300, 32768, 3.0),
@@ -297,11 +298,34 @@ def test_softmax_sum_is_the_sequential_sum(dev):
     assert worst < 2e-6, f"softmax 128K row error {worst:.2e}: not the sequential sum"
 
 
+@pytest.fixture
+def cluster_softmax(monkeypatch):
+    """Route f32 softmax to the cluster kernel (k_softmax_cluster.cu)."""
+    monkeypatch.setenv("TB_B200_SOFTMAX", "cluster")
+
+
+@pytest.mark.parametrize("name,rows,cols,std", [c for c in SOFTMAX_CASES if c[2] >= 1024])
+def test_cluster_softmax(dev, cluster_softmax, name, rows, cols, std):
+    """The cluster kernel on every f32 case wide enough for it."""
+    x = np.random.default_rng(cols).standard_normal((rows, cols), dtype=np.float32) * \
+        np.float32(std)
+    y_ref = O.softmax(x, None, threads=8)
+    gy = T.softmax(gpu(x, dev))
+    sync()
+    worst, _ = assert_f32(to_np(gy), y_ref, f"cluster softmax {name}")
+    assert worst < 2e-6, f"cluster softmax {name}: row error {worst:.2e}"
+    assert T.check_status() == (0, 0)
+
+
 @pytest.mark.parametrize("std", [3.0, 12.0])
-def test_cluster_softmax_sum_over_many_rows(dev, std):
-    """400 rows of 128256 terms: every cluster takes many rows, so its
-    segment buffers, exchange slots and scanner keys all wrap around.
-    Each row must still be the sequential sum (row error < 2e-6)."""
+@pytest.mark.parametrize("cluster", [False, True])
+def test_cluster_softmax_sum_over_many_rows(dev, monkeypatch, std, cluster):
+    """400 rows of 128256 terms, through the default kernel and through the
+    cluster kernel, where every cluster takes many rows, so its segment
+    buffers, exchange slots and scanner keys all wrap around.  Each row must
+    still be the sequential sum (row error < 2e-6)."""
+    if cluster:
+        monkeypatch.setenv("TB_B200_SOFTMAX", "cluster")
     rng = np.random.default_rng(79 + int(std))
     x = rng.standard_normal((400, 128256), dtype=np.float32) * np.float32(std)
     y_ref = O.softmax(x, threads=8)
@@ -312,8 +336,11 @@ def test_cluster_softmax_sum_over_many_rows(dev, std):
     assert T.check_status() == (0, 0)
 
 
-def test_softmax_in_place_and_nan_in_wide_rows(dev):
+@pytest.mark.parametrize("cluster", [False, True])
+def test_softmax_in_place_and_nan_in_wide_rows(dev, monkeypatch, cluster):
     """y may alias x; a NaN term makes its row NaN, other rows unaffected."""
+    if cluster:
+        monkeypatch.setenv("TB_B200_SOFTMAX", "cluster")
     rng = np.random.default_rng(5)
     x = rng.standard_normal((300, 32000), dtype=np.float32) * np.float32(3)
     x[7, 20000] = np.float32("nan")
