@@ -51,15 +51,16 @@ for _p in (ROOT, PKG):
 
 import workloads as W  # noqa: E402
 
-# --config: the default is the Llama-7B prefill (the headline); 70b runs
-# the Llama-70B prefill's layer ops on 16384 tokens and the bandwidth
-# sweep's widest softmax/argmax point (4096 rows of 128256 logits).
+# --config: the default (70b) is the Llama-70B prefill's row ops on 16384
+# tokens with softmax/argmax over 4096 rows of 128256 logits, strong-scaled
+# over the ranks; 7b is the Llama-7B prefill of 4096 tokens on every rank.
 CONFIGS = {
     "7b": (W.CONFIGS["7b"], None, "llama7b-prefill-4096 row ops (embedding, residual+RMSNorm, "
                                   "RoPE, SwiGLU, softmax, argmax)"),
     "70b": (W.CONFIGS["70b"], 4096, "llama70b-prefill-16384 (8 x 2048) row ops strong-scaled "
                                     "over the ranks: vocab-sharded 128256 x 8192 embedding "
-                                    "gather (NCCL exchange), residual+RMSNorm, RoPE, SwiGLU, "
+                                    "gather (one kernel over the NCCL symmetric-memory "
+                                    "windows), residual+RMSNorm, RoPE, SwiGLU, "
                                     "softmax/argmax over 4096 x 128256 logits"),
     "sweep": (W.CONFIGS["7b"], None, "bandwidth sweep: residual+RMSNorm and SwiGLU over rows "
                                      "2^10..2^20 x hidden {2048, 4096, 8192, 16384} in f32 and "

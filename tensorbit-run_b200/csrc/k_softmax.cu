@@ -1,59 +1,60 @@
 // k_softmax.cu -- numerically stable row softmax, with the reference's exact
-// row sum.
+// row sum: rows wider than the staged kernel's (k_softmax_staged.cu), masked
+// rows, and bf16.
 //
 // Reference arithmetic (tb_cpu_softmax_f32, src/ops/softmax.c:4-32), per row:
 //   v_i   = x_i (+ mask_i)                      (one f32 add when a mask is given)
 //   m     = max_i v_i  (strict '>', from -inf: NaN never becomes the max)
 //   e_i   = expf(v_i - m);   sum = ((e_0 + e_1) + e_2) + ...   (f32, in order)
 //   y_i   = e_i * (1.0f/sum)   if sum > 0,   else y_i = e_i
-// The max is exact in any order.  The sum is reproduced bit-for-bit (see
-// ordered_sum.cuh for why an in-order f32 sum can be computed with integer
-// prefix sums); expf is CUDA's full-precision expf (within 2 ulp of the C
-// library's), the only source of difference from the CPU.
+// The max is exact in any order.  e_i is tbsm::expo(v_i, m) (ex2-based, the
+// same expression as the staged kernel's), and the sum is the in-order f32
+// sum of those terms, bit for bit (scan_tiles.cuh).
 //
 // One CTA per row (512 threads, two CTAs per SM), the row cut into 256-term
 // tiles (32 lanes x 8 terms); each warp keeps kU tiles of loads in flight:
 //   pass 1  per-tile max and an approximate per-tile sum of exp(v - tile
 //           max) (fast __expf; an estimate only).  Row max m.
 //   est     block scan of the rescaled tile sums: an estimate of the running
-//           sum at each tile start, hence a predicted binade b_i per tile.
+//           sum at each tile start, hence a predicted binade b_t per tile.
 //           Tiles likely to need term-by-term work (the first tile, a
 //           predicted binade change, an estimate near a power of two) get a
 //           shared-memory slot for their terms.
-//   pass 2  e_i = expf(v_i - m) (stored into y for f32 output, and into the
-//           tile's slot); per tile the exact integer sum D_i = sum rne(e/u)
-//           on the grid of b_i and whether it holds an exact tie (tie tiles
-//           take a free slot too).
-//   pass 3  warp 0, 32 tiles per step: while the exact running sum is in a
-//           tile's predicted binade, the tile holds no tie, and the sum does
-//           not cross into the next binade, the tile is consumed in O(1)
-//           (S += D_i).  Otherwise -- about log2(V) binade crossings per row
-//           plus the rare tie or misprediction, ~5% of the tiles -- it is
-//           summed term by term (ordered_sum_tile), from its slot when it
-//           has one.  The first tile, where the sum crosses many binades, is
-//           one lane's plain f32 additions.  The result is the sequential
-//           sum.
+//   pass 2  e_i (stored into y for f32 output); per tile the integer sum D
+//           of rne(e/u) on the grid of b_t; a tile with an exact tie or a
+//           term of 2^22 units or more is flagged (kStop) and takes a free
+//           slot.  A slotted tile keeps its terms and the prefix sums of
+//           their units on the grids of b_t and b_t + 1 (scan_tiles.cuh,
+//           slot tables).  The warp that has tile 0 sums its terms in order.
+//   pass 3  warp 0: scan_tiles_tab -- runs of plain tiles added with one
+//           redux per 32 tiles, each slotted or flagged tile resolved with
+//           a ballot per event over its prefix table, a misprediction
+//           located with a scan, a tile without a slot summed term by term
+//           (terms from y, or recomputed from x for bf16).
 //   pass 4  y = e * (1/sum).
 // HBM: one read of x, one write of y; the re-reads hit L2 (two rows per SM
-// in flight: ~80 MB at V = 32000 f32), helped by evict-first hints on the
-// last read of x and streaming stores of y.  Rows wider than the tile table
-// (> 2.8M terms) use one warp for the whole ordered sum.
+// in flight), helped by evict-first hints on the last read of x and
+// streaming stores of y.  Rows wider than the tile table (> 2.7M terms) use
+// one warp for the whole ordered sum.
 #include <math.h>
 
+#include <algorithm>
+
 #include "ordered_sum.cuh"
+#include "scan_tiles.cuh"
 #include "tb_device.cuh"
 #include "tb_internal.h"
 
 namespace {
 
 using tbk::Elt;
+using tbsm::expo;
 
 constexpr int kK = 8;            // terms per lane per tile
 constexpr int kTile = 32 * kK;   // terms per tile
-constexpr int kTileBytes = 11;   // shared bytes per tile (see k_softmax_tiles)
+static_assert(kTile == tbsm::kTileN, "tile size shared with scan_tiles.cuh");
+constexpr int kTileBytes = 12;   // shared bytes per tile (see k_softmax_tiles)
 constexpr int kSlots = 24;       // tiles whose terms are kept in shared memory
-constexpr int kNoSlot = 255;
-constexpr int kU = 2;            // tiles a warp has in flight
 
 enum Cache { kKeep = 0, kLast = 1 };
 
@@ -120,37 +121,6 @@ __device__ __forceinline__ int load_oct(const T* xr, const T* mr, int64_t cols, 
     return nv;
 }
 
-// Integer grid units of one tile on the FMA pipe.  For t = e/u < 2^22,
-// (t + 1.5*2^23) - 1.5*2^23 is t rounded to the nearest integer (the add
-// rounds at the units place); |t - r| == 0.5 is an exact tie (its rounding
-// depends on the running sum's parity); the units add exactly in f32 while
-// the partial sums stay below 2^24, and a tile whose sum reaches 2^24 is an
-// event anyway (the running sum leaves its binade).  t >= 2^22 or NaN is an
-// event.  Returns the lane's sum; *ev collects the events.
-template <int N>
-__device__ __forceinline__ float tile_units(const float (&e)[N], int nv, float inv_u, bool* ev) {
-    constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-    float acc = 0.0f;
-    bool bad = false;
-#pragma unroll
-    for (int j = 0; j < N; ++j) {
-        const float t = __fmul_rn(j < nv ? e[j] : 0.0f, inv_u);
-        const float r = __fsub_rn(__fadd_rn(t, kMagic), kMagic);
-        bad |= !(t < 4194304.0f) || fabsf(__fsub_rn(t, r)) == 0.5f;
-        acc = __fadd_rn(acc, r);
-    }
-    *ev |= bad;
-    return acc;
-}
-
-
-// Within ~2^-10 relative of a power of two: the exact sum may sit on either
-// side of the binade edge the estimate sees.
-__device__ __forceinline__ bool near_edge(float v) {
-    const uint32_t m = __float_as_uint(v) & 0x7fffffu;
-    return m < (1u << 13) || m > (1u << 23) - (1u << 13);
-}
-
 // Block-wide exclusive scan (NT threads); `carry` holds NT/32 partials.
 template <typename V, int NT>
 __device__ __forceinline__ V block_excl_scan(V local, V* carry) {
@@ -169,23 +139,89 @@ __device__ __forceinline__ V block_excl_scan(V local, V* carry) {
     return base + incl - local;
 }
 
-template <typename T, int NT, bool VEC>
+// Terms of a tile without a slot, for the scanner: from y, where pass 2
+// stored e (f32 output), else recomputed from x (+ mask).
+template <typename T, bool VEC, bool FROM_Y>
+struct RowTerms {
+    const T* xr;
+    const T* mr;
+    const T* yr;
+    int64_t cols;
+    float m;
+    __device__ __forceinline__ void operator()(int tile, int n, float (&e)[kK]) const {
+        const int lane = threadIdx.x & 31;
+        const int64_t i0 = (int64_t)tile * kTile + lane * kK;
+        if constexpr (FROM_Y) {
+#pragma unroll
+            for (int j = 0; j < kK; ++j) e[j] = lane * kK + j < n ? Elt<T>::load(yr + i0 + j) : 0.0f;
+        } else {
+            float v[kK];
+            load_oct<T, VEC>(xr, mr, cols, tile, lane, v);
+#pragma unroll
+            for (int j = 0; j < kK; ++j) e[j] = lane * kK + j < n ? expo(v[j], m) : 0.0f;
+        }
+    }
+};
+
+// A warp's tiles warp, warp + NW, ... in steps of KU tiles, each step's
+// loads issued before the previous step is processed (two register sets):
+// load(t, v) fills the lane's kK terms of tile t and returns how many are in
+// the row; proc(t, v, nv) may overwrite v.
+template <int NW, int KU, class Load, class Proc>
+__device__ __forceinline__ void warp_tiles(int warp, int ntiles, const Load& load,
+                                           const Proc& proc) {
+    float a[KU][kK], b[KU][kK];
+    int na[KU], nb[KU];
+#pragma unroll
+    for (int u = 0; u < KU; ++u) {
+        const int t = warp + u * NW;
+        na[u] = t < ntiles ? load(t, a[u]) : 0;
+    }
+    for (int tb = warp; tb < ntiles; tb += NW * KU) {
+#pragma unroll
+        for (int u = 0; u < KU; ++u) {
+            const int t = tb + (KU + u) * NW;
+            nb[u] = t < ntiles ? load(t, b[u]) : 0;
+        }
+#pragma unroll
+        for (int u = 0; u < KU; ++u) {
+            const int t = tb + u * NW;
+            if (t < ntiles) proc(t, a[u], na[u]);  // warp-uniform
+        }
+#pragma unroll
+        for (int u = 0; u < KU; ++u) {
+            na[u] = nb[u];
+#pragma unroll
+            for (int j = 0; j < kK; ++j) a[u][j] = b[u][j];
+        }
+    }
+}
+
+// Max over the warp of lane values that are not NaN: one redux.sync over
+// their bits mapped to an order-preserving unsigned key.
+__device__ __forceinline__ float warp_max_redux(float v) {
+    const uint32_t b = __float_as_uint(v);
+    const uint32_t k = __reduce_max_sync(tbk::kFull, (b & 0x80000000u) ? ~b : (b | 0x80000000u));
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+template <typename T, int NT, bool VEC, int KU, int KU2>
 __global__ void __launch_bounds__(NT, 2)
-k_softmax_tiles(const T* x, const T* mask, T* y, int64_t cols, int ntiles) {
+k_softmax_tiles(const T* x, const T* mask, T* y, int64_t cols, int ntiles, int nslot) {
     constexpr int NW = NT / 32;
+    constexpr int kU = KU;    // tiles per step of a warp in passes 1 and 4
+    constexpr int kU2 = KU2;  // the same in pass 2 (more registers per tile)
     constexpr bool kStoreE = sizeof(T) == 4;  // f32 output can hold e exactly
     extern __shared__ __align__(16) unsigned char smem[];
-    float (*slots)[kTile] = reinterpret_cast<float (*)[kTile]>(smem);   // kSlots tiles of e
-    float* tmax = reinterpret_cast<float*>(smem + sizeof(float) * kSlots * kTile);
-    float* tsum = tmax + ntiles;                          // pass 1: tile sum estimate
-    uint32_t* tD = reinterpret_cast<uint32_t*>(tmax);    // pass 2: D_i (reuses tmax)
-    signed char* tbin = reinterpret_cast<signed char*>(tsum + ntiles);  // predicted binade
-    unsigned char* tev = reinterpret_cast<unsigned char*>(tbin + ntiles);  // tile is an event
-    unsigned char* tslot = tev + ntiles;                  // slot of the tile's terms
+    tbsm::SlotTab* slots = reinterpret_cast<tbsm::SlotTab*>(smem);  // nslot slotted tiles
+    float2* tms = reinterpret_cast<float2*>(smem + sizeof(tbsm::SlotTab) * nslot);
+    uint32_t* tD = reinterpret_cast<uint32_t*>(tms);      // pass 2: units per tile, reuses tms
+    uint32_t* tmeta = reinterpret_cast<uint32_t*>(tms + ntiles);  // binade | flags | slot << 24
     __shared__ float red[NW];
     __shared__ float fcarry[NW];
     __shared__ int icarry[NW];
     __shared__ float row_sum;
+    __shared__ float tile0_sum;
     __shared__ int nslots;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -195,38 +231,26 @@ k_softmax_tiles(const T* x, const T* mask, T* y, int64_t cols, int ntiles) {
     T* yr = y + base;
 
     // ---- pass 1: tile max and tile sum estimate
-    for (int tb = warp; tb < ntiles; tb += NW * kU) {
-        float v[kU][kK];
-        int nv[kU];
-#pragma unroll
-        for (int u = 0; u < kU; ++u) {
-            const int t = tb + u * NW;
-            nv[u] = t < ntiles ? load_oct<T, VEC>(xr, mr, cols, t, lane, v[u]) : 0;
-        }
-#pragma unroll
-        for (int u = 0; u < kU; ++u) {
-            const int t = tb + u * NW;
-            if (t >= ntiles) continue;  // warp-uniform
+    warp_tiles<NW, kU>(
+        warp, ntiles,
+        [&](int t, float (&v)[kK]) { return load_oct<T, VEC>(xr, mr, cols, t, lane, v); },
+        [&](int t, float (&v)[kK], int nv) {
             float tm = -INFINITY;
 #pragma unroll
-            for (int j = 0; j < kK; ++j) tm = v[u][j] > tm ? v[u][j] : tm;
-            tm = tbk::warp_max(tm);
+            for (int j = 0; j < kK; ++j) tm = v[j] > tm ? v[j] : tm;
+            tm = warp_max_redux(tm);
             float ts = 0.0f;
             if (tm > -INFINITY) {
 #pragma unroll
                 for (int j = 0; j < kK; ++j)
-                    if (j < nv[u]) ts += __expf(v[u][j] - tm);
+                    if (j < nv) ts += __expf(v[j] - tm);
             }
-            ts = tbk::warp_sum(ts);
-            if (lane == 0) {
-                tmax[t] = tm;
-                tsum[t] = ts;
-            }
-        }
-    }
+            ts = tbsm::warp_sum_est(ts);
+            if (lane == 0) tms[t] = make_float2(tm, ts);
+        });
     __syncthreads();
     float m = -INFINITY;
-    for (int t = threadIdx.x; t < ntiles; t += NT) m = fmaxf(m, tmax[t]);
+    for (int t = threadIdx.x; t < ntiles; t += NT) m = fmaxf(m, tms[t].x);
     m = tbk::block_max(m, red);
 
     // ---- estimate of the running sum at each tile start -> predicted binade;
@@ -237,168 +261,111 @@ k_softmax_tiles(const T* x, const T* mask, T* y, int64_t cols, int ntiles) {
         const int t1 = min(t0 + per, ntiles);
         float local = 0.0f;
         for (int t = t0; t < t1; ++t) {
-            const float tm = tmax[t];
-            local += tm > -INFINITY ? tsum[t] * __expf(tm - m) : 0.0f;
+            const float2 q = tms[t];
+            local += q.x > -INFINITY ? q.y * __expf(q.x - m) : 0.0f;
         }
         float run = block_excl_scan<float, NT>(local, fcarry);
         int likely = 0;
         for (int t = t0; t < t1; ++t) {
             const int b = tbk::binade_of(run);
-            const float tm = tmax[t];
-            const float nxt = run + (tm > -INFINITY ? tsum[t] * __expf(tm - m) : 0.0f);
+            const float2 q = tms[t];
+            const float nxt = run + (q.x > -INFINITY ? q.y * __expf(q.x - m) : 0.0f);
             const bool lk = t == 0 || b == tbk::kNoBinade || tbk::binade_of(nxt) != b ||
-                            near_edge(run) || near_edge(nxt);
-            tbin[t] = (signed char)b;
-            tslot[t] = lk ? 1 : 0;
+                            tbsm::near_pow2(run) || tbsm::near_pow2(nxt);
+            tmeta[t] = ((uint32_t)b & 0xffu) | (lk ? (1u << 31) : 0u);
             likely += lk;
             run = nxt;
         }
         int slot = block_excl_scan<int, NT>(likely, icarry);
         for (int t = t0; t < t1; ++t) {
-            if (tslot[t]) {
-                tslot[t] = slot < kSlots ? (unsigned char)slot : (unsigned char)kNoSlot;
+            uint32_t sl = tbsm::kNoSlot;
+            if (tmeta[t] >> 31) {
+                if (slot < nslot) sl = (uint32_t)slot;
                 ++slot;
-            } else {
-                tslot[t] = kNoSlot;
             }
+            tmeta[t] = (tmeta[t] & 0xffu) | (sl << 24);
         }
         if (threadIdx.x == NT - 1) nslots = slot;
     }
-    __syncthreads();  // tmax/tsum fully consumed: tD may now overwrite tmax
+    __syncthreads();  // tms fully consumed: tD may now overwrite it
 
-    // ---- pass 2: e, the integer tile sums and tie flags
-    for (int tb = warp; tb < ntiles; tb += NW * kU) {
-        float v[kU][kK];
-        int nv[kU];
+    // ---- pass 2: e, the tiles' units, slots, tile 0's in-order sum
+    warp_tiles<NW, kU2>(
+        warp, ntiles,
+        [&](int t, float (&v)[kK]) {
+            return load_oct<T, VEC, kStoreE ? kLast : kKeep>(xr, mr, cols, t, lane, v);
+        },
+        [&](int t, float (&e)[kK], int nv) {
 #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-            const int t = tb + u * NW;
-            nv[u] = t < ntiles ? load_oct<T, VEC, kStoreE ? kLast : kKeep>(xr, mr, cols, t, lane,
-                                                                            v[u])
-                               : 0;
-        }
-#pragma unroll
-        for (int u = 0; u < kU; ++u) {
-            const int t = tb + u * NW;
-            if (t >= ntiles) continue;  // warp-uniform
-            float e[kK];
-#pragma unroll
-            for (int j = 0; j < kK; ++j) e[j] = j < nv[u] ? expf(__fsub_rn(v[u][j], m)) : 0.0f;
+            for (int j = 0; j < kK; ++j) e[j] = j < nv ? expo(e[j], m) : 0.0f;
             const int64_t i0 = (int64_t)t * kTile + lane * kK;
             if constexpr (kStoreE) {
-                if (VEC && nv[u] == kK) {
+                if (VEC && nv == kK) {
                     *reinterpret_cast<float4*>(yr + i0) = make_float4(e[0], e[1], e[2], e[3]);
                     *reinterpret_cast<float4*>(yr + i0 + 4) = make_float4(e[4], e[5], e[6], e[7]);
                 } else {
 #pragma unroll
                     for (int j = 0; j < kK; ++j)
-                        if (j < nv[u]) Elt<T>::store(yr + i0 + j, e[j]);
+                        if (j < nv) Elt<T>::store(yr + i0 + j, e[j]);
                 }
             }
-            const int b = tbin[t];
-            bool ev = b == tbk::kNoBinade;
-            float dl = 0.0f;
-            if (!ev) dl = tile_units<kK>(e, nv[u], tbk::inv_grid(b), &ev);
-            const float dsum = tbk::warp_sum(dl);  // exact below 2^24
-            ev = __any_sync(tbk::kFull, ev) || !(dsum < 16777216.0f);
-            const uint32_t d = ev ? 0u : (uint32_t)dsum;
-            int slot = tslot[t];
-            if (slot == kNoSlot && ev) {
-                int s = 0;
-                if (lane == 0) s = atomicAdd(&nslots, 1);
-                s = __shfl_sync(tbk::kFull, s, 0);
-                if (s < kSlots) {
-                    slot = s;
-                    if (lane == 0) tslot[t] = (unsigned char)s;
+            uint32_t meta = tmeta[t];
+            const int b = (int)(int8_t)(meta & 0xffu);
+            const float iu = tbk::inv_grid(b == tbk::kNoBinade ? 0 : b);
+            float acc = 0.0f, dm = 0.0f;
+#pragma unroll
+            for (int j = 0; j < kK; ++j) {
+                const float tt = __fmul_rn(e[j], iu);
+                const float r = __fsub_rn(__fadd_rn(tt, tbsm::kMagic), tbsm::kMagic);
+                acc = __fadd_rn(acc, r);
+                dm = fmaxf(dm, fabsf(__fsub_rn(tt, r)));
+            }
+            // acc < 2^22 - 1 implies every t < 2^22 - 1/2: the magic rounding
+            // was exact; NaN fails the test too.  A tile with an exact tie or
+            // such a term is resolved by the scanner (kStop).
+            const bool big = __any_sync(tbk::kFull, !(acc < 4194303.0f));
+            const bool tie = __any_sync(tbk::kFull, dm == 0.5f);
+            const uint32_t d = __reduce_add_sync(
+                tbk::kFull, tbsm::magic_int(__fadd_rn(fminf(acc, 4194303.0f), tbsm::kMagic)));
+            if (b == tbk::kNoBinade)
+                meta |= tbsm::kExact;
+            else if (big || tie)
+                meta |= tbsm::kStop;
+            uint32_t slot = meta >> 24;
+            if (slot == tbsm::kNoSlot && (meta & (tbsm::kExact | tbsm::kStop))) {
+                int sn = 0;
+                if (lane == 0) sn = atomicAdd(&nslots, 1);
+                sn = __shfl_sync(tbk::kFull, sn, 0);
+                if (sn < nslot) {
+                    slot = (uint32_t)sn;
+                    meta = (meta & 0x00ffffffu) | (slot << 24);
                 }
             }
-            if (slot != kNoSlot) {
-                *reinterpret_cast<float4*>(&slots[slot][lane * kK]) =
-                    make_float4(e[0], e[1], e[2], e[3]);
-                *reinterpret_cast<float4*>(&slots[slot][lane * kK + 4]) =
-                    make_float4(e[4], e[5], e[6], e[7]);
+            if (slot != tbsm::kNoSlot)
+                tbsm::slot_tab_fill(slots[slot], e, (meta & tbsm::kExact) ? tbk::kNoBinade : b);
+            if (t == 0) {  // tile 0 (always slotted): one lane's in-order additions
+                __syncwarp();
+                if (lane == 0) {
+                    const float* e0 = slots[slot].e;
+                    const int n0 = cols < kTile ? (int)cols : kTile;
+                    float s0 = 0.0f;
+                    for (int q = 0; q < n0; ++q) s0 = __fadd_rn(s0, e0[q]);
+                    tile0_sum = s0;
+                }
             }
             if (lane == 0) {
                 tD[t] = d;
-                tev[t] = ev;
+                tmeta[t] = meta;
             }
-        }
-    }
+        });
     __syncthreads();
 
     // ---- pass 3: the ordered sum over tiles (warp 0)
     if (warp == 0) {
-        tbk::RunSum st;
-        // Tile 0 (always slotted): one lane's plain sequential additions.
-        {
-            const int n0 = cols < kTile ? (int)cols : kTile;
-            float s0 = 0.0f;
-            if (lane == 0) {
-                const float* e0 = slots[tslot[0]];
-                for (int i = 0; i < n0; ++i) s0 = __fadd_rn(s0, e0[i]);
-            }
-            st.set(__shfl_sync(tbk::kFull, s0, 0));
-        }
-        for (int t0 = 0; t0 < ntiles && !st.nan; t0 += 32) {
-            const int cnt = min(32, ntiles - t0);
-            int pos = t0 == 0 ? 1 : 0;
-            while (pos < cnt && !st.nan) {
-                const int t = t0 + lane;
-                const bool valid = lane >= pos && lane < cnt;
-                bool ok = false;
-                uint32_t d = 0;
-                if (valid && st.fast && !tev[t] && tbin[t] == st.b) {
-                    ok = true;
-                    d = tD[t];
-                }
-                uint32_t incl = d;
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const uint32_t n = __shfl_up_sync(tbk::kFull, incl, o);
-                    if (lane >= o) incl = min(incl + n, 1u << 30);
-                }
-                uint32_t excl = __shfl_up_sync(tbk::kFull, incl, 1);
-                if (lane == 0) excl = 0;
-                const bool ev = valid && (!ok || st.S + excl + d >= (1u << 24));
-                const unsigned bal = __ballot_sync(tbk::kFull, ev);
-                if (bal == 0) {
-                    st.S += __shfl_sync(tbk::kFull, incl, 31);
-                    st.s = __fmul_rn((float)st.S, st.u);
-                    break;
-                }
-                const int f = __ffs(bal) - 1;
-                const uint32_t pre = __shfl_sync(tbk::kFull, excl, f);
-                if (st.fast && pre) {
-                    st.S += pre;
-                    st.s = __fmul_rn((float)st.S, st.u);
-                }
-                // term-by-term through tile t0 + f
-                const int tile = t0 + f;
-                const int64_t i0 = (int64_t)tile * kTile + lane * kK;
-                const int64_t rem = cols - i0;
-                const int nv = rem <= 0 ? 0 : (rem >= kK ? kK : (int)rem);
-                float e[kK];
-                const int slot = tslot[tile];
-                if (slot != kNoSlot) {
-                    const float4 a = *reinterpret_cast<const float4*>(&slots[slot][lane * kK]);
-                    const float4 c = *reinterpret_cast<const float4*>(&slots[slot][lane * kK + 4]);
-                    e[0] = a.x; e[1] = a.y; e[2] = a.z; e[3] = a.w;
-                    e[4] = c.x; e[5] = c.y; e[6] = c.z; e[7] = c.w;
-                } else if constexpr (kStoreE) {
-#pragma unroll
-                    for (int j = 0; j < kK; ++j) e[j] = j < nv ? Elt<T>::load(yr + i0 + j) : 0.0f;
-                } else {
-                    float v[kK];
-                    load_oct<T, VEC>(xr, mr, cols, tile, lane, v);
-#pragma unroll
-                    for (int j = 0; j < kK; ++j) e[j] = j < nv ? expf(__fsub_rn(v[j], m)) : 0.0f;
-                }
-                const int64_t left = cols - (int64_t)tile * kTile;
-                tbk::ordered_sum_tile<kK>(st, e, left < kTile ? (int)left : kTile);
-                pos = f + 1;
-            }
-        }
-        if (lane == 0) row_sum = st.s;
+        const float s = tbsm::scan_tiles_tab(tD, tmeta, tile0_sum, slots, nslot,
+                                             RowTerms<T, VEC, kStoreE>{xr, mr, yr, cols, m},
+                                             (int)cols);
+        if (lane == 0) row_sum = s;
     }
     __syncthreads();
 
@@ -408,61 +375,46 @@ k_softmax_tiles(const T* x, const T* mask, T* y, int64_t cols, int ntiles) {
     const float inv = __fdiv_rn(1.0f, sum);
     if constexpr (kStoreE) {
         if (!norm) return;  // y already holds e (softmax.c:24)
-        for (int tb = warp; tb < ntiles; tb += NW * kU) {
-            float4 a[kU][2];
+        warp_tiles<NW, kU>(
+            warp, ntiles,
+            [&](int t, float (&v)[kK]) { return load_oct<T, VEC, kLast>(yr, nullptr, cols, t, lane, v); },
+            [&](int t, float (&v)[kK], int nv) {
+                const int64_t i0 = (int64_t)t * kTile + lane * kK;
 #pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                const int64_t i0 = (int64_t)(tb + u * NW) * kTile + lane * kK;
-                if (VEC && i0 + kK <= cols) {
-                    a[u][0] = __ldcs(reinterpret_cast<const float4*>(yr + i0));
-                    a[u][1] = __ldcs(reinterpret_cast<const float4*>(yr + i0 + 4));
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                const int64_t i0 = (int64_t)(tb + u * NW) * kTile + lane * kK;
-                if (VEC && i0 + kK <= cols) {
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        a[u][h].x = __fmul_rn(a[u][h].x, inv); a[u][h].y = __fmul_rn(a[u][h].y, inv);
-                        a[u][h].z = __fmul_rn(a[u][h].z, inv); a[u][h].w = __fmul_rn(a[u][h].w, inv);
-                        __stcs(reinterpret_cast<float4*>(yr + i0 + 4 * h), a[u][h]);
-                    }
+                for (int j = 0; j < kK; ++j) v[j] = __fmul_rn(v[j], inv);
+                if (VEC && nv == kK) {
+                    __stcs(reinterpret_cast<float4*>(yr + i0), make_float4(v[0], v[1], v[2], v[3]));
+                    __stcs(reinterpret_cast<float4*>(yr + i0 + 4), make_float4(v[4], v[5], v[6], v[7]));
                 } else {
-                    for (int j = 0; j < kK && i0 + j < cols; ++j)
-                        Elt<T>::store(yr + i0 + j, __fmul_rn(Elt<T>::load(yr + i0 + j), inv));
+#pragma unroll
+                    for (int j = 0; j < kK; ++j)
+                        if (j < nv) Elt<T>::store(yr + i0 + j, v[j]);
                 }
-            }
-        }
+            });
     } else {
-        for (int tb = warp; tb < ntiles; tb += NW * kU) {
-            float v[kU][kK];
-            int nv[kU];
-#pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                const int t = tb + u * NW;
-                nv[u] = t < ntiles ? load_oct<T, VEC, kLast>(xr, mr, cols, t, lane, v[u]) : 0;
-            }
-#pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                const int64_t i0 = (int64_t)(tb + u * NW) * kTile + lane * kK;
+        warp_tiles<NW, kU>(
+            warp, ntiles,
+            [&](int t, float (&v)[kK]) { return load_oct<T, VEC, kLast>(xr, mr, cols, t, lane, v); },
+            [&](int t, float (&v)[kK], int nv) {
+                const int64_t i0 = (int64_t)t * kTile + lane * kK;
 #pragma unroll
                 for (int j = 0; j < kK; ++j) {
-                    const float e = expf(__fsub_rn(v[u][j], m));
-                    v[u][j] = norm ? __fmul_rn(e, inv) : e;
+                    const float e = expo(v[j], m);
+                    v[j] = norm ? __fmul_rn(e, inv) : e;
                 }
-                if (VEC && nv[u] == kK) {
+                if (VEC && nv == kK) {
                     uint4 o;
-                    o.x = tbk::pack_bf16x2(v[u][0], v[u][1]);
-                    o.y = tbk::pack_bf16x2(v[u][2], v[u][3]);
-                    o.z = tbk::pack_bf16x2(v[u][4], v[u][5]);
-                    o.w = tbk::pack_bf16x2(v[u][6], v[u][7]);
+                    o.x = tbk::pack_bf16x2(v[0], v[1]);
+                    o.y = tbk::pack_bf16x2(v[2], v[3]);
+                    o.z = tbk::pack_bf16x2(v[4], v[5]);
+                    o.w = tbk::pack_bf16x2(v[6], v[7]);
                     __stcs(reinterpret_cast<uint4*>(yr + i0), o);
                 } else {
-                    for (int j = 0; j < nv[u]; ++j) Elt<T>::store(yr + i0 + j, v[u][j]);
+#pragma unroll
+                    for (int j = 0; j < kK; ++j)
+                        if (j < nv) Elt<T>::store(yr + i0 + j, v[j]);
                 }
-            }
-        }
+            });
     }
 }
 
@@ -497,7 +449,7 @@ k_softmax_wide(const T* x, const T* mask, T* y, int64_t cols) {
                 if (i < cols) {
                     float v = Elt<T>::load(xr + i);
                     if (mr) v = __fadd_rn(v, Elt<T>::load(mr + i));
-                    e[j] = expf(__fsub_rn(v, m));
+                    e[j] = expo(v, m);
                 }
             }
             const int64_t left = cols - t0;
@@ -512,19 +464,19 @@ k_softmax_wide(const T* x, const T* mask, T* y, int64_t cols) {
     for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) {
         float v = Elt<T>::load(xr + i);
         if (mr) v = __fadd_rn(v, Elt<T>::load(mr + i));
-        const float e = expf(__fsub_rn(v, m));
+        const float e = expo(v, m);
         Elt<T>::store(yr + i, norm ? __fmul_rn(e, inv) : e);
     }
 }
 
-template <typename T, int NT, bool VEC>
-int launch_tiles(const T* x, const T* m, T* y, int64_t rows, int64_t cols, int ntiles,
+template <typename T, int NT, bool VEC, int KU = 2, int KU2 = 1>
+int launch_tiles(const T* x, const T* m, T* y, int64_t rows, int64_t cols, int ntiles, int nslot,
                  size_t smem, cudaStream_t s) {
-    auto kern = k_softmax_tiles<T, NT, VEC>;
+    auto kern = k_softmax_tiles<T, NT, VEC, KU, KU2>;
     if (smem > 48 * 1024)
         TB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem));
-    kern<<<(unsigned)rows, NT, smem, s>>>(x, m, y, cols, ntiles);
+    kern<<<(unsigned)rows, NT, smem, s>>>(x, m, y, cols, ntiles, nslot);
     TB_LAUNCH_CHECK("softmax kernel");
     return TB_OK;
 }
@@ -535,7 +487,10 @@ int launch(int64_t rows, int64_t cols, const void* x, const void* mask, void* y,
     const T* mp = static_cast<const T*>(mask);
     T* yp = static_cast<T*>(y);
     const int64_t ntiles = (cols + kTile - 1) / kTile;
-    const size_t smem = sizeof(float) * kSlots * kTile + (size_t)ntiles * kTileBytes + 16;
+    // slots for about one tile in four, at least 8 (a short row's crossings
+    // are few), at most kSlots
+    const int nslot = (int)std::min<int64_t>(ntiles, std::max<int64_t>(8, std::min<int64_t>(kSlots, ntiles / 4)));
+    const size_t smem = sizeof(tbsm::SlotTab) * nslot + (size_t)ntiles * kTileBytes + 16;
     if (smem > 200 * 1024) {
         k_softmax_wide<T><<<(unsigned)rows, 256, 0, s>>>(xp, mp, yp, cols);
         TB_LAUNCH_CHECK("softmax kernel");
@@ -545,11 +500,11 @@ int launch(int64_t rows, int64_t cols, const void* x, const void* mask, void* y,
                      (mask == nullptr || tbh::aligned16(mask));
     const int nt = (int)ntiles;
     if (cols <= 8192) {
-        return vec ? launch_tiles<T, 128, true>(xp, mp, yp, rows, cols, nt, smem, s)
-                   : launch_tiles<T, 128, false>(xp, mp, yp, rows, cols, nt, smem, s);
+        return vec ? launch_tiles<T, 128, true>(xp, mp, yp, rows, cols, nt, nslot, smem, s)
+                   : launch_tiles<T, 128, false>(xp, mp, yp, rows, cols, nt, nslot, smem, s);
     }
-    return vec ? launch_tiles<T, 512, true>(xp, mp, yp, rows, cols, nt, smem, s)
-               : launch_tiles<T, 512, false>(xp, mp, yp, rows, cols, nt, smem, s);
+    return vec ? launch_tiles<T, 512, true>(xp, mp, yp, rows, cols, nt, nslot, smem, s)
+               : launch_tiles<T, 512, false>(xp, mp, yp, rows, cols, nt, nslot, smem, s);
 }
 
 }  // namespace

@@ -48,8 +48,11 @@
 #include "tb_device.cuh"
 #include "tb_internal.h"
 #include "tma.cuh"
+#include "scan_tiles.cuh"
 
 namespace {
+
+using namespace tbsm;
 
 constexpr int kNT = 768;
 constexpr int kScanWarps = 3;
@@ -58,23 +61,11 @@ constexpr int kFinWarps = 6;  // finalizers: the normalising pass, beside the wo
 constexpr int kFin = kFinWarps * 32;
 constexpr int kWorkWarps = kNT / 32 - kScanWarps - kFinWarps;
 constexpr int kWork = kWorkWarps * 32;
-constexpr int kTileN = 256;
 constexpr int kMaxCols = 32768;
 constexpr int kMaxTiles = kMaxCols / kTileN;
 constexpr int kChunks = 4;  // the row arrives in four bulk copies, one mbarrier each
 constexpr int kMaxSlots = 16;
 constexpr uint64_t kStaggerNs = 7000;  // start offset of odd CTAs
-constexpr uint32_t kSat = 1u << 30;
-constexpr uint32_t kLimit = 1u << 24;
-constexpr uint32_t kExact = 1u << 16;  // meta flag: sum the tile term by term
-constexpr uint32_t kNoSlot = 0xffu;
-constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-
-// A slotted tile: its terms, kept for the scanner (the row buffer is
-// reused before the row is scanned).
-struct Slot {
-    float e[kTileN];
-};
 
 // Hand-off from the workers to a row's scanner (double-buffered).
 struct RowSummary {
@@ -85,103 +76,8 @@ struct RowSummary {
     float pad[2];
 };
 
-// e = 2^((x - m) * log2(e)) on the MUFU pipe (subnormal results flush to 0).
-__device__ __forceinline__ float expo(float x, float m) {
-    float r;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(__fmul_rn(__fsub_rn(x, m), 1.44269504f)));
-    return r;
-}
-
-// Sum over the warp of nonnegative lane values v (each < 2^31 in the
-// scaled domain), to about 2^-21 relative: the largest lane value sets a
-// power-of-two scale, each lane rounds v * scale to an integer, and one
-// redux.sync adds them.
-__device__ __forceinline__ float warp_sum_est(float v) {
-    const uint32_t mx = __reduce_max_sync(tbk::kFull, __float_as_uint(v));  // v >= 0: bits order
-    if (mx == 0u) return 0.0f;
-    if (mx >= 0x7f800000u) return __uint_as_float(0x7fc00000u);  // inf or NaN
-    const int ex = (int)(mx >> 23) - 127;                 // largest lane value in [2^ex, 2^(ex+1))
-    const int sh = 25 - ex;                               // lane values < 2^26 after scaling
-    if (sh > 126) return 0.0f;                            // below 2^-100: no binade anyway
-    const float sc = __uint_as_float((uint32_t)(sh + 127) << 23);
-    const uint32_t q = __float2uint_rn(__fmul_rn(v, sc));
-    const uint32_t tot = __reduce_add_sync(tbk::kFull, q);  // < 32 * 2^26 = 2^31
-    return __fmul_rn((float)tot, __uint_as_float((uint32_t)(127 - sh) << 23));
-}
-
 __device__ __forceinline__ void work_sync() {
     asm volatile("bar.sync 1, %0;" ::"r"(kWork) : "memory");
-}
-
-__device__ __forceinline__ bool near_pow2(float v) {
-    const uint32_t mant = __float_as_uint(v) & 0x7fffffu;
-    return mant < (1u << 13) || mant > (1u << 23) - (1u << 13);
-}
-
-// For a = t + 1.5*2^23 with 0 <= t < 2^22: rne(t) as an integer, read from
-// a's mantissa bits (an integer op instead of a float-to-int conversion).
-__device__ __forceinline__ uint32_t magic_int(float a) { return __float_as_uint(a) - 0x4B400000u; }
-
-// Grid units of one term on grid inv_u, exact for any t (slot arrays):
-// base = rne(t), or floor(t) for an exact tie; 2^25 (certainly an event)
-// for t >= 2^25 or NaN.
-__device__ __forceinline__ uint32_t units_exact(float e, float inv_u, bool* tie) {
-    const float t = __fmul_rn(e, inv_u);
-    if (t < 4194304.0f) {
-        const float a = __fadd_rn(t, kMagic);
-        const float d = __fsub_rn(t, __fsub_rn(a, kMagic));
-        *tie = fabsf(d) == 0.5f;
-        return magic_int(a) - (d < 0.0f && *tie ? 1u : 0u);
-    }
-    *tie = false;
-    if (!(t < 33554432.0f)) return 1u << 25;
-    const float fl = floorf(t);
-    *tie = __fsub_rn(t, fl) == 0.5f;
-    return *tie ? (uint32_t)fl : __float2uint_rn(t);
-}
-
-// Units added by one term given the parity of the partial sum before it.
-struct Fn {
-    uint32_t a0, a1;  // total for an even / odd running sum at the start
-};
-__device__ __forceinline__ Fn compose(Fn f, Fn g) {  // f, then g
-    Fn r;
-    r.a0 = min(f.a0 + ((f.a0 & 1u) ? g.a1 : g.a0), kSat);
-    r.a1 = min(f.a1 + (((f.a1 + 1u) & 1u) ? g.a1 : g.a0), kSat);
-    return r;
-}
-__device__ __forceinline__ Fn term_fn(float e, float inv_u) {
-    const float t = __fmul_rn(e, inv_u);
-    const float a = __fadd_rn(t, kMagic);
-    const float d = __fsub_rn(t, __fsub_rn(a, kMagic));
-    const uint32_t ri = magic_int(a);
-    if (fabsf(d) != 0.5f) return Fn{ri, ri};
-    const uint32_t base = d < 0.0f ? ri - 1u : ri;  // floor(t)
-    // round half to even: the result (start + base + extra) must be even
-    return Fn{base + (base & 1u), base + ((base + 1u) & 1u)};
-}
-// In-order reduction of the lanes' functions (lane 0 first); valid in lane 0.
-__device__ __forceinline__ Fn warp_compose(Fn f) {
-    const int lane = threadIdx.x & 31;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        Fn g;
-        g.a0 = __shfl_down_sync(tbk::kFull, f.a0, o);
-        g.a1 = __shfl_down_sync(tbk::kFull, f.a1, o);
-        if ((lane & (2 * o - 1)) == 0) f = compose(f, g);
-    }
-    return f;
-}
-
-// Saturating inclusive warp scan of u32.
-__device__ __forceinline__ uint32_t warp_incl(uint32_t v) {
-    const int lane = threadIdx.x & 31;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t n = __shfl_up_sync(tbk::kFull, v, o);
-        if (lane >= o) v = min(v + n, kSat);
-    }
-    return v;
 }
 
 struct Shared {
@@ -200,176 +96,19 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, unsigne
 }
 
 // ------------------------------------------------------------------ scanner
-// Terms of `tile` in the ordered_sum_tile layout (lane l: terms 8l .. 8l+7).
-__device__ __forceinline__ void tile_terms(const Slot* s, const float* xr, float m, int tile,
-                                           int n, float (&e)[8]) {
-    const int lane = threadIdx.x & 31;
+// Terms of a tile that has no slot, recomputed from x (still in L2).
+struct XTerms {
+    const float* xr;
+    float m;
+    __device__ __forceinline__ void operator()(int tile, int n, float (&e)[8]) const {
+        const int lane = threadIdx.x & 31;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        const int j = lane * 8 + k;
-        e[k] = 0.0f;
-        if (j < n) e[k] = s ? s->e[j] : expo(xr[(int64_t)tile * kTileN + j], m);
+        for (int k = 0; k < 8; ++k) {
+            const int j = lane * 8 + k;
+            e[k] = j < n ? expo(xr[(int64_t)tile * kTileN + j], m) : 0.0f;
+        }
     }
-}
-
-// Inclusive prefix sums of a slotted tile's grid units on one grid, in
-// registers: lane l holds those of terms 4l..4l+3 (pa) and 128+4l..128+4l+3
-// (pb), with their tie bits (bits 0-3, 4-7).  Terms past the row are 0.
-struct TilePrefix {
-    uint32_t pa[4], pb[4];
-    uint32_t tie;
 };
-__device__ __forceinline__ TilePrefix tile_prefix(const Slot* s, float inv_u) {
-    const int lane = threadIdx.x & 31;
-    const float4 a = *reinterpret_cast<const float4*>(s->e + 4 * lane);
-    const float4 c = *reinterpret_cast<const float4*>(s->e + 128 + 4 * lane);
-    const float e[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
-    uint32_t u[8];
-    TilePrefix P;
-    P.tie = 0;
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-        bool tq;
-        u[q] = units_exact(e[q], inv_u, &tq);
-        P.tie |= (uint32_t)tq << q;
-    }
-    const uint32_t ha = min(min(u[0] + u[1], kSat) + min(u[2] + u[3], kSat), kSat);
-    const uint32_t hb = min(min(u[4] + u[5], kSat) + min(u[6] + u[7], kSat), kSat);
-    const uint32_t ia = warp_incl(ha);
-    const uint32_t ib = warp_incl(hb);
-    const uint32_t tot_a = __shfl_sync(tbk::kFull, ia, 31);
-    uint32_t pa = ia - ha, pb = min(tot_a + (ib - hb), kSat);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        pa = min(pa + u[q], kSat);
-        P.pa[q] = pa;
-        pb = min(pb + u[4 + q], kSat);
-        P.pb[q] = pb;
-    }
-    return P;
-}
-// The prefix at term q (warp-uniform q in [0, 256)).
-__device__ __forceinline__ uint32_t prefix_at(const TilePrefix& P, int q) {
-    const int r = q & 3;
-    const uint32_t* v = q >= 128 ? P.pb : P.pa;
-    const uint32_t x = r == 0 ? v[0] : r == 1 ? v[1] : r == 2 ? v[2] : v[3];
-    return __shfl_sync(tbk::kFull, x, (q & 127) >> 2);
-}
-
-// Consume `tile` into the running sum, exactly.  A slotted tile on the
-// current grid: the prefix arrays of grid b (then b+1 after a crossing) find
-// each event -- the first term that is a tie or takes the sum to 2^24 units
-// -- which is one real f32 addition; the terms between events add in O(1).
-// Anything else: term by term.
-__device__ void resolve_tile(tbk::RunSum& st, const Slot* slots, int nslot, const float* xr,
-                             float m, int tile, uint32_t meta, int cols) {
-    const int lane = threadIdx.x & 31;
-    const int tb = (int)(int8_t)(meta & 0xffu);
-    const uint32_t slot = meta >> 24;
-    const Slot* s = slot < (uint32_t)nslot ? slots + slot : nullptr;
-    const int n = min(kTileN, cols - tile * kTileN);
-    int pos = 0;
-    if (s && !(meta & kExact) && st.fast && st.b == tb) {
-        int gcur = -1;
-        TilePrefix P;
-        while (pos < n && !st.nan) {
-            const int g = st.fast ? st.b - tb : -1;
-            if (g != 0 && g != 1) break;
-            if (g != gcur) {
-                P = tile_prefix(s, tbk::inv_grid(tb + g));
-                gcur = g;
-            }
-            const uint32_t P0 = pos ? prefix_at(P, pos - 1) : 0u;
-            uint32_t ea = 0, eb = 0;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int ja = 4 * lane + k, jb = 128 + 4 * lane + k;
-                if (ja >= pos && ja < n && (((P.tie >> k) & 1u) || st.S + (P.pa[k] - P0) >= kLimit))
-                    ea |= 1u << k;
-                if (jb >= pos && jb < n &&
-                    (((P.tie >> (4 + k)) & 1u) || st.S + (P.pb[k] - P0) >= kLimit))
-                    eb |= 1u << k;
-            }
-            const unsigned ba = __ballot_sync(tbk::kFull, ea != 0);
-            const unsigned bb = __ballot_sync(tbk::kFull, eb != 0);
-            if (!ba && !bb) {
-                st.S += prefix_at(P, n - 1) - P0;
-                st.s = __fmul_rn((float)st.S, st.u);
-                return;
-            }
-            int j;
-            if (ba) {
-                const int f = __ffs(ba) - 1;
-                j = 4 * f + __ffs(__shfl_sync(tbk::kFull, ea, f)) - 1;
-            } else {
-                const int f = __ffs(bb) - 1;
-                j = 128 + 4 * f + __ffs(__shfl_sync(tbk::kFull, eb, f)) - 1;
-            }
-            const uint32_t before = st.S + (j ? prefix_at(P, j - 1) - P0 : 0u);
-            st.set(__fadd_rn(__fmul_rn((float)before, st.u), s->e[j]));
-            pos = j + 1;
-        }
-        if (pos >= n || st.nan) return;
-    }
-    float e[8];
-    tile_terms(s, xr, m, tile, n, e);
-    tbk::ordered_sum_tile<8>(st, e, n, pos);
-}
-
-__device__ float scan_row(const RowSummary& R, const Slot* slots, int nslot, const float* xr,
-                          float m, int cols) {
-    const int lane = threadIdx.x & 31;
-    const int ntiles = (cols + kTileN - 1) / kTileN;
-    tbk::RunSum st;
-    st.set(R.s0);  // tile 0: summed in order by a worker
-    for (int t0 = 0; t0 < ntiles && !st.nan; t0 += 32) {
-        const int cnt = min(32, ntiles - t0);
-        uint2 dl = make_uint2(0u, 0u);
-        uint32_t meta = 0;
-        if (lane < cnt) {
-            dl = R.D[t0 + lane];
-            meta = R.meta[t0 + lane];
-        }
-        const int tb = (int)(int8_t)(meta & 0xffu);
-        int pos = t0 == 0 ? 1 : 0;
-        while (pos < cnt && !st.nan) {
-            const bool valid = lane >= pos && lane < cnt;
-            const bool ok = valid && st.fast && !(meta & kExact) && tb == st.b;
-            const Fn f = ok ? Fn{dl.x, dl.y} : Fn{0u, 0u};
-            Fn inc = f;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                Fn g;
-                g.a0 = __shfl_up_sync(tbk::kFull, inc.a0, o);
-                g.a1 = __shfl_up_sync(tbk::kFull, inc.a1, o);
-                if (lane >= o) inc = compose(g, inc);
-            }
-            Fn exc;
-            exc.a0 = __shfl_up_sync(tbk::kFull, inc.a0, 1);
-            exc.a1 = __shfl_up_sync(tbk::kFull, inc.a1, 1);
-            if (lane == 0) exc = Fn{0u, 0u};
-            const uint32_t p = st.S & 1u;
-            const uint32_t ex = p ? exc.a1 : exc.a0;
-            const uint32_t mine = ((p + ex) & 1u) ? f.a1 : f.a0;
-            const bool ev = valid && (!ok || st.S + ex + mine >= kLimit);
-            const unsigned bal = __ballot_sync(tbk::kFull, ev);
-            if (bal == 0) {
-                st.S += __shfl_sync(tbk::kFull, p ? inc.a1 : inc.a0, 31);
-                st.s = __fmul_rn((float)st.S, st.u);
-                break;
-            }
-            const int fl = __ffs(bal) - 1;
-            const uint32_t pre = __shfl_sync(tbk::kFull, ex, fl);
-            if (st.fast && pre) {
-                st.S += pre;
-                st.s = __fmul_rn((float)st.S, st.u);
-            }
-            resolve_tile(st, slots, nslot, xr, m, t0 + fl, __shfl_sync(tbk::kFull, meta, fl), cols);
-            pos = fl + 1;
-        }
-    }
-    return st.s;
-}
 
 // ------------------------------------------------------------------ kernel
 __global__ void __launch_bounds__(kNT, 1)
@@ -430,8 +169,8 @@ k_softmax_staged(const float* x, float* y, int rows, int cols, int nslot, unsign
             wait_bar(&bar_ready[sc], (uint32_t)(i / kBufs) & 1u, status, abort_v);
             const int row = (int)blockIdx.x + i * (int)gridDim.x;
             const RowSummary& R = sh.sum[sc];
-            const float sum =
-                scan_row(R, sh.slots + sc * nslot, nslot, x + (int64_t)row * cols, R.m, cols);
+            const float sum = scan_tiles(R.D, R.meta, R.s0, sh.slots + sc * nslot, nslot,
+                                         XTerms{x + (int64_t)row * cols, R.m}, cols);
             if (lane == 0) row_sum[i & 3] = sum;
             __syncwarp();
             if (lane == 0) {

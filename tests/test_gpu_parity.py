@@ -362,6 +362,49 @@ def test_softmax_in_place_and_nan_in_wide_rows(dev, monkeypatch, cluster):
     assert T.check_status() == (0, 0)
 
 
+@pytest.mark.parametrize("masked", [False, True])
+def test_softmax_special_rows_128k(dev, masked):
+    """Rows of 128256 terms (the tiled kernel, in place) with the values
+    that reach its slot tables' edge cases: NaN, all -inf, +inf, a max
+    beyond the fused exponent's range, all equal (a sum of exact integers),
+    a single spike, very spiky and near-uniform rows, tiny values; with a
+    mask of -inf entries too.  Finite rows: the in-order sum (row error
+    < 2e-6); NaN rows stay unnormalised, as in the reference."""
+    rng = np.random.default_rng(81)
+    n = 128256
+    x = rng.standard_normal((12, n), dtype=np.float32) * np.float32(3)
+    x[1, 100000] = np.float32("nan")
+    x[2, :] = -np.inf
+    x[3, 5] = np.inf
+    x[4, 77] = np.float32(3e38)
+    x[5, :] = np.float32(1e30)
+    x[6, :] = 0.0
+    x[7, :] = 0.0
+    x[7, 50000] = 5.0
+    x[8] *= np.float32(10)                          # std 30: a few terms dominate
+    x[9] = rng.standard_normal(n).astype(np.float32) * np.float32(0.01)  # near-uniform
+    x[10] = np.float32(-200) + rng.standard_normal(n).astype(np.float32)
+    mask = None
+    if masked:
+        mask = rng.standard_normal((12, n), dtype=np.float32)
+        mask[:, ::3] = -np.inf
+        mask[11, :] = -np.inf                          # a fully masked row: NaN
+    y_ref = O.softmax(x, mask, threads=8)
+    g = gpu(x, dev)
+    T.softmax(g, None if mask is None else gpu(mask, dev), y=g)
+    sync()
+    gy = to_np(g)
+    assert (np.isnan(gy) == np.isnan(y_ref)).all()
+    keep = ~np.isnan(y_ref).any(axis=1)
+    worst, _ = assert_f32(gy[keep], y_ref[keep], "softmax 128K special rows")
+    assert worst < 2e-6, f"softmax 128K special rows: row error {worst:.2e}"
+    for r in np.nonzero(~keep)[0]:
+        ok = ~np.isnan(y_ref[r])
+        if ok.any():
+            assert_f32(gy[r][ok][None], y_ref[r][ok][None], f"softmax 128K NaN row {r}")
+    assert T.check_status() == (0, 0)
+
+
 def test_staged_softmax_sum_is_the_sequential_sum(dev):
     """The shared-memory-staged path (f32, 32000 columns, many rows per CTA)
     must also return the in-order sum: row error < 2e-6, where a tree sum of
