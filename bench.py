@@ -1069,9 +1069,32 @@ def run_sharded(args, rank, world, local):
         for f in ops.values():
             f()
 
+    # The same gather two other ways, each timed alone: the NCCL exchange
+    # (host ids, a host plan, pack, grouped send/recv, scatter) and one
+    # kernel over CUDA IPC mappings of the other ranks' parts.
+    if world > 1:
+        handles = [None] * world
+        dist.all_gather_object(handles, T.p2p_export(shard))
+        addrs = [shard.data_ptr() if r == rank else T.p2p_import(*handles[r])
+                 for r in range(world)]
+    else:
+        handles, addrs = None, [shard.data_ptr()]
+    y_p2p = torch.empty_like(o["emb"])
+    y_nccl = torch.empty_like(o["emb"])
+    darr = (C.c_void_p * world)(*addrs)
+
+    def p2p():
+        T.check(L.tb_b200_embedding_sharded_p2p(T.BF16, R, c.hidden, c.vocab, T.ptr(my_ids), darr,
+                                                world, T.ptr(y_p2p), sp), "embedding_sharded_p2p")
+
+    def nccl():
+        T.check(L.tb_b200_embedding_sharded(T.BF16, NT, c.hidden, c.vocab, ids_p, C.c_void_p(win),
+                                            T.ptr(y_nccl), sp), "embedding_sharded")
+
     if args.profile_op:
+        f = {"embedding_nccl": nccl, "embedding_ipc": p2p}.get(args.profile_op)
         for _ in range(args.warmup + args.steps):
-            ops[args.profile_op]()
+            (f or ops[args.profile_op])()
         torch.cuda.synchronize()
         barrier()
         T.comm_destroy()
@@ -1111,28 +1134,6 @@ def run_sharded(args, rank, world, local):
     per_op_ms = {n: max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in evs[n]))
                  for n in names}
     barrier()
-
-    # The same gather two other ways, each timed alone: the NCCL exchange
-    # (host ids, a host plan, pack, grouped send/recv, scatter) and one
-    # kernel over CUDA IPC mappings of the other ranks' parts.
-    if world > 1:
-        handles = [None] * world
-        dist.all_gather_object(handles, T.p2p_export(shard))
-        addrs = [shard.data_ptr() if r == rank else T.p2p_import(*handles[r])
-                 for r in range(world)]
-    else:
-        handles, addrs = None, [shard.data_ptr()]
-    y_p2p = torch.empty_like(o["emb"])
-    y_nccl = torch.empty_like(o["emb"])
-    darr = (C.c_void_p * world)(*addrs)
-
-    def p2p():
-        T.check(L.tb_b200_embedding_sharded_p2p(T.BF16, R, c.hidden, c.vocab, T.ptr(my_ids), darr,
-                                                world, T.ptr(y_p2p), sp), "embedding_sharded_p2p")
-
-    def nccl():
-        T.check(L.tb_b200_embedding_sharded(T.BF16, NT, c.hidden, c.vocab, ids_p, C.c_void_p(win),
-                                            T.ptr(y_nccl), sp), "embedding_sharded")
 
     def time_alone(f, n):
         for _ in range(3):
@@ -1494,9 +1495,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile-op", choices=["embedding", "layer_chain", "softmax", "argmax"],
+    ap.add_argument("--profile-op", choices=["embedding", "layer_chain", "softmax", "argmax",
+                                             "embedding_nccl", "embedding_ipc"],
                     help="only launch this op (warmup + steps times) on --rows rows: a small "
-                         "case for ncu captures")
+                         "case for ncu captures (70b: embedding is the symmetric-memory gather, "
+                         "embedding_nccl the NCCL exchange, embedding_ipc the CUDA IPC kernel)")
     ap.add_argument("--config", choices=sorted(CONFIGS), default=DEFAULT_CONFIG,
                     help="70b (default): the Llama-70B prefill of 16384 tokens strong-scaled "
                          "over the ranks, with the vocab-sharded embedding gather and the "
@@ -1520,6 +1523,8 @@ def main():
     if args.rows is None:
         args.rows = CFG.rows
     args.warmup = max(args.warmup, 3)
+    if args.profile_op in ("embedding_nccl", "embedding_ipc") and args.config != "70b":
+        ap.error(f"--profile-op {args.profile_op} needs --config 70b")
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))

@@ -205,13 +205,15 @@ __device__ __forceinline__ float warp_max_redux(float v) {
     return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
+// One row (the whole CTA).  f32: pass 2 stores e into y (f32 output holds
+// it exactly) and pass 4 rescales y; bf16: pass 4 recomputes e from x.
 template <typename T, int NT, bool VEC, int KU, int KU2>
-__global__ void __launch_bounds__(NT, 2)
-k_softmax_tiles(const T* x, const T* mask, T* y, int64_t cols, int ntiles, int nslot) {
+__device__ __forceinline__ void tiles_row(const T* x, const T* mask, T* y, int64_t row,
+                                          int64_t cols, int ntiles, int nslot) {
     constexpr int NW = NT / 32;
     constexpr int kU = KU;    // tiles per step of a warp in passes 1 and 4
     constexpr int kU2 = KU2;  // the same in pass 2 (more registers per tile)
-    constexpr bool kStoreE = sizeof(T) == 4;  // f32 output can hold e exactly
+    constexpr bool kStoreE = sizeof(T) == 4;
     extern __shared__ __align__(16) unsigned char smem[];
     tbsm::SlotTab* slots = reinterpret_cast<tbsm::SlotTab*>(smem);  // nslot slotted tiles
     float2* tms = reinterpret_cast<float2*>(smem + sizeof(tbsm::SlotTab) * nslot);
@@ -225,7 +227,7 @@ k_softmax_tiles(const T* x, const T* mask, T* y, int64_t cols, int ntiles, int n
     __shared__ int nslots;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t base = (int64_t)blockIdx.x * cols;
+    const int64_t base = row * cols;
     const T* xr = x + base;
     const T* mr = mask ? mask + base : nullptr;
     T* yr = y + base;
@@ -403,12 +405,19 @@ k_softmax_tiles(const T* x, const T* mask, T* y, int64_t cols, int ntiles, int n
                     v[j] = norm ? __fmul_rn(e, inv) : e;
                 }
                 if (VEC && nv == kK) {
-                    uint4 o;
-                    o.x = tbk::pack_bf16x2(v[0], v[1]);
-                    o.y = tbk::pack_bf16x2(v[2], v[3]);
-                    o.z = tbk::pack_bf16x2(v[4], v[5]);
-                    o.w = tbk::pack_bf16x2(v[6], v[7]);
-                    __stcs(reinterpret_cast<uint4*>(yr + i0), o);
+                    if constexpr (sizeof(T) == 4) {
+                        __stcs(reinterpret_cast<float4*>(yr + i0),
+                               make_float4(v[0], v[1], v[2], v[3]));
+                        __stcs(reinterpret_cast<float4*>(yr + i0 + 4),
+                               make_float4(v[4], v[5], v[6], v[7]));
+                    } else {
+                        uint4 o;
+                        o.x = tbk::pack_bf16x2(v[0], v[1]);
+                        o.y = tbk::pack_bf16x2(v[2], v[3]);
+                        o.z = tbk::pack_bf16x2(v[4], v[5]);
+                        o.w = tbk::pack_bf16x2(v[6], v[7]);
+                        __stcs(reinterpret_cast<uint4*>(yr + i0), o);
+                    }
                 } else {
 #pragma unroll
                     for (int j = 0; j < kK; ++j)
@@ -416,6 +425,14 @@ k_softmax_tiles(const T* x, const T* mask, T* y, int64_t cols, int ntiles, int n
                 }
             });
     }
+}
+
+// Row blockIdx.x.  (A persistent form looping over rows made the compiler
+// spill the row's working set to local memory.)
+template <typename T, int NT, bool VEC, int KU, int KU2>
+__global__ void __launch_bounds__(NT, 2)
+k_softmax_tiles(const T* x, const T* mask, T* y, int64_t cols, int ntiles, int nslot) {
+    tiles_row<T, NT, VEC, KU, KU2>(x, mask, y, blockIdx.x, cols, ntiles, nslot);
 }
 
 // Fallback for rows wider than the tile table: one warp runs the ordered
