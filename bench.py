@@ -107,7 +107,14 @@ TRAFFIC_PER_ROW = {
         "softmax": (192851456 + 74482944) / 1024,
         "argmax": 530358016 / 4096,
     },
-    "70b": {},
+    # captured on one GPU: softmax/argmax over 1024 x 128256 logits, the
+    # layer chain over 2048 token rows, the gather of 8192 tokens
+    "70b": {
+        "embedding": (130690304 + 84914432) / 8192,
+        "layer_chain": (340854784 + 167031552) / 2048,
+        "softmax": (1304488960 + 886223616) / 1024,
+        "argmax": (525479680 + 4182784) / 1024,
+    },
 }
 TRAFFIC_SOURCE = "ncu capture of the kernel (DRAM bytes read + written per row, scaled to the " \
                  "launch's rows)"
