@@ -1339,7 +1339,7 @@ SWEEP_ROWS = [1 << k for k in range(10, 21)]
 SWEEP_WIDTHS = [2048, 4096, 8192, 16384]
 SWEEP_LOGIT_ROWS = [1, 16, 256, 4096]
 SWEEP_VOCAB = 128256
-SWEEP_REPS = 5
+SWEEP_REPS = 5  # timed launches per point (at least; --steps raises it, up to 20)
 
 
 def run_sweep(args, rank, world, local):
@@ -1347,7 +1347,8 @@ def run_sweep(args, rank, world, local):
     [rows, w] elements for the sweep's rows and widths, f32 and bf16, then
     softmax and argmax over [rows, 128256] f32 logits.  A point's rows are
     split over the ranks (tb_b200_partition); its time is the median over
-    SWEEP_REPS launches of the max over ranks.  L2 is flushed (a 512 MB
+    max(SWEEP_REPS, min(--steps, 20)) launches, after --warmup untimed ones,
+    of the max over ranks.  L2 is flushed (a 512 MB
     write) before every timed launch whose buffers would fit in 4x L2.
     Points whose buffers exceed the memory budget are listed as skipped."""
     import torch
@@ -1374,11 +1375,13 @@ def run_sweep(args, rank, world, local):
         dist.all_reduce(x, op=dist.ReduceOp.MAX)
         return float(x.item())
 
+    reps = max(SWEEP_REPS, min(args.steps, 20))
+
     def time_point(launch, footprint):
-        for _ in range(2):
+        for _ in range(args.warmup):
             launch()
         times = []
-        for _ in range(SWEEP_REPS):
+        for _ in range(reps):
             if footprint < 4 * l2:
                 flush.fill_(1)
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -1473,7 +1476,7 @@ def run_sweep(args, rank, world, local):
              for p_ in done if p_["frac"] < 0.8]
     return {
         "metric": METRIC, "value": round(total_b / total_ms / 1e6, 1), "unit": "GB/s",
-        "n_gpus": world, "steps": SWEEP_REPS, "warmup": 2,
+        "n_gpus": world, "steps": reps, "warmup": args.warmup,
         "ms_per_step": round(total_ms, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32 and bf16 (f32 arithmetic)",
         "data": "synthetic (N(0,1) activations, N(0,3) logits)",
