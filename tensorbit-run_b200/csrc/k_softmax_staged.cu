@@ -1,6 +1,6 @@
 // k_softmax_staged.cu -- f32 row softmax for rows of up to 32768 terms:
-// each row staged once in shared memory, the reference's in-order sum
-// scanned by dedicated warps while the next row streams in.
+// each row's exponentials staged once in shared memory, the reference's
+// in-order sum scanned by dedicated warps while the next rows go on.
 //
 // Reference arithmetic (tb_cpu_softmax_f32, src/ops/softmax.c:4-32):
 //   m = max x (strict '>', from -inf);  e_i = expf(x_i - m);
@@ -18,17 +18,15 @@
 //               go on.  They share one warp scheduler.
 //   6 warps     finalizers: y = e * (1/sum) of each scanned row, e recomputed
 //               from x (still in L2), streaming stores.
-//   15 warps    workers, per row:
-//     load   bulk asynchronous copies of the row in four chunks, one
-//            mbarrier each -- the copy engine keeps the row in flight, HBM
-//            is read once; the next row's copy is issued as soon as the
-//            units pass below is done with the buffer, and that row is
-//            prefetched to L2 at the start of this one.
-//     max    row max over the staged row.
-//     exp    e = ex2(...) in place, and a sum estimate per 256-term tile.
+//   15 warps    workers, per row (the row is prefetched to L2 one row
+//               ahead, so HBM is read once):
+//     exp    e = ex2(...) from x in L2 into the row buffer, and a sum
+//            estimate per 256-term tile.
 //     est    running-sum estimate at each tile start -> predicted binade b_t;
 //            tiles likely to cross a binade (or near a power of two) get a
-//            slot: a copy of their terms for the scanner.
+//            slot: a copy of their terms for the scanner.  Beside it, one
+//            warp sums tile 0 in order and 13 warps take the next row's max
+//            from L2, so no row waits for its max.
 //     units  per tile, the integer sum of rne(e / u_b) as a function of the
 //            running sum's parity at the tile start: (D0, D1).  Only exact
 //            ties (e/u = k + 1/2) make them differ; round-to-even then
@@ -41,7 +39,10 @@
 //   ballot (the crossing term is one real f32 addition, the rest of the tile
 //   O(1) on the next grid), otherwise term by term (ordered_sum_tile).
 // Every wait is bounded (tma.cuh); a timeout raises TB_B200_FLAG_WAIT_TIMEOUT,
-// after which the CTA skips its remaining waits and copies and ends.
+// after which the CTA skips its remaining waits and ends.  (An earlier form
+// copied each row into shared memory with bulk copies: the copy of the next
+// row could only start once the buffer was free, and its landing was on
+// every row's critical path.)
 #include <math.h>
 
 #include "ordered_sum.cuh"
@@ -63,7 +64,6 @@ constexpr int kWorkWarps = kNT / 32 - kScanWarps - kFinWarps;
 constexpr int kWork = kWorkWarps * 32;
 constexpr int kMaxCols = 32768;
 constexpr int kMaxTiles = kMaxCols / kTileN;
-constexpr int kChunks = 4;  // the row arrives in four bulk copies, one mbarrier each
 constexpr int kMaxSlots = 16;
 constexpr uint64_t kStaggerNs = 7000;  // start offset of odd CTAs
 
@@ -114,8 +114,8 @@ struct XTerms {
 __global__ void __launch_bounds__(kNT, 1)
 k_softmax_staged(const float* x, float* y, int rows, int cols, int nslot, unsigned* status) {
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ __align__(8) uint64_t bar_x[kChunks], bar_ready[kBufs], bar_done[kBufs];
-    __shared__ float red[kWorkWarps];
+    __shared__ __align__(8) uint64_t bar_ready[kBufs], bar_done[kBufs];
+    __shared__ float red[kWorkWarps];      // the next row's max, per worker warp
     __shared__ float row_sum[4];           // ordered sum of row i at i & 3 (scanner -> finalizers)
     __shared__ float row_m[4];             // row max of row i at i & 3 (workers -> finalizers)
     __shared__ __align__(8) uint64_t bar_fin[4];  // finalizers have read row_sum/row_m of row i
@@ -131,13 +131,9 @@ k_softmax_staged(const float* x, float* y, int rows, int cols, int nslot, unsign
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nloc = rows > (int)blockIdx.x ? (rows - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
     const uint32_t rowbytes = (uint32_t)cols * 4u;
-    // chunk bytes: a whole number of tiles (1 KB each)
-    const uint32_t cb = ((rowbytes + kChunks - 1) / kChunks + 1023u) / 1024u * 1024u;
-    const int tpc = (int)(cb / 1024u);  // tiles per chunk
     volatile int* abort_v = &abort_flag;
 
     if (threadIdx.x == 0) {
-        for (int c = 0; c < kChunks; ++c) tbk::mbar_init(&bar_x[c], 1);
         for (int k = 0; k < kBufs; ++k) {
             tbk::mbar_init(&bar_ready[k], 1);
             tbk::mbar_init(&bar_done[k], 1);
@@ -147,16 +143,6 @@ k_softmax_staged(const float* x, float* y, int rows, int cols, int nslot, unsign
         tbk::fence_mbar_init();
     }
     __syncthreads();
-
-    auto issue_chunk = [&](int i, int c, uint64_t pol) {  // one thread: chunk c of local row i
-        const float* src = x + (int64_t)((int)blockIdx.x + i * (int)gridDim.x) * cols;
-        const uint32_t lo = min(rowbytes, c * cb), hi = min(rowbytes, (c + 1) * cb);
-        tbk::mbar_expect_tx(&bar_x[c], hi - lo);
-        if (hi > lo)  // x stays in L2 until the finalizers read it again
-            tbk::bulk_g2s_hint(reinterpret_cast<unsigned char*>(sh.xbuf) + lo,
-                               reinterpret_cast<const unsigned char*>(src) + lo, hi - lo, &bar_x[c],
-                               pol);
-    };
 
     // Scanners are warps 0, 4, 8: one warp scheduler (warp id mod 4) runs
     // them beside a single worker warp, so their latency-bound chains are
@@ -243,76 +229,89 @@ k_softmax_staged(const float* x, float* y, int rows, int cols, int nslot, unsign
     const int ww = nw - kFinWarps;  // worker index 0..kWorkWarps-1
     const int wt = ww * 32 + lane;
     const uint64_t pol_last = tbk::policy_evict_last();
-    if (wt == 0 && nloc > 0)
-        for (int c = 0; c < kChunks; ++c) issue_chunk(0, c, pol_last);
+    const int nfull = cols / kTileN;
+    auto row_x = [&](int i) { return x + ((int64_t)blockIdx.x + (int64_t)i * gridDim.x) * cols; };
+    // The max of a row, read from global memory (L2), over the tiles of
+    // worker warps w0 .. w0 + nwk - 1: the warp's part, into red[ww].
+    // Four tiles' loads are in flight per lane before their maxima.
+    auto part_max = [&](const float* xr, int w0, int nwk) {
+        constexpr int kU = 4;
+        float mx = -INFINITY;
+        if (ww >= w0 && ww < w0 + nwk) {
+            for (int t = ww - w0; t < ntiles; t += kU * nwk) {
+                float4 v[2 * kU];
+#pragma unroll
+                for (int u = 0; u < kU; ++u) {
+                    const int tu = t + u * nwk;
+                    const float* xt = xr + (int64_t)tu * kTileN;
+                    const int n = tu < ntiles ? min(kTileN, cols - tu * kTileN) : 0;
+                    v[2 * u] = v[2 * u + 1] = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+                    if (4 * lane < n) v[2 * u] = *reinterpret_cast<const float4*>(xt + 4 * lane);
+                    if (128 + 4 * lane < n)
+                        v[2 * u + 1] = *reinterpret_cast<const float4*>(xt + 128 + 4 * lane);
+                }
+#pragma unroll
+                for (int q = 0; q < 2 * kU; ++q)
+                    mx = fmaxf(mx, fmaxf(fmaxf(v[q].x, v[q].y), fmaxf(v[q].z, v[q].w)));
+            }
+            mx = tbk::warp_max(mx);
+        }
+        if (lane == 0) red[ww] = mx;
+    };
+    if (nloc > 0) {  // row 0's max, by every worker
+        if (wt == 0) tbk::prefetch_l2_hint(row_x(0), rowbytes, pol_last);
+        part_max(row_x(0), 0, kWorkWarps);
+        work_sync();
+    }
     for (int i = 0; i < nloc; ++i) {
-        // The next row heads for L2 while this one is worked on: its bulk
-        // copy, issued after this row's units pass, then reads L2.
+        // The next row heads for L2 while this one is worked on: its max is
+        // read during this row's estimate, its terms at the start of the next.
         if (wt == 0 && i + 1 < nloc && !*abort_v)
-            tbk::prefetch_l2_hint(x + ((int64_t)blockIdx.x + (int64_t)(i + 1) * gridDim.x) * cols,
-                                  rowbytes, pol_last);
+            tbk::prefetch_l2_hint(row_x(i + 1), rowbytes, pol_last);
         auto tp = [&](int t) -> float* { return sh.xbuf + (size_t)t * kTileN; };
         {
             const int k = i % kBufs;
             RowSummary& R = sh.sum[k];
             Slot* SL = sh.slots + k * nslot;
-            const uint32_t par = (uint32_t)i & 1u;
-            // ---- max (each warp waits for the chunks of its own tiles)
-            float mx = -INFINITY;
-            int waited = -1;
-            for (int t = ww; t < ntiles; t += kWorkWarps) {
-                const int c = t / tpc;
-                for (; waited < c; ++waited) wait_bar(&bar_x[waited + 1], par, status, abort_v);
-                const float* xt = tp(t);
-                const int n = min(kTileN, cols - t * kTileN);
-                if (n == kTileN || 4 * lane < n) {
-                    const float4 a = *reinterpret_cast<const float4*>(xt + 4 * lane);
-                    mx = fmaxf(mx, fmaxf(fmaxf(a.x, a.y), fmaxf(a.z, a.w)));
-                }
-                if (n == kTileN || 128 + 4 * lane < n) {
-                    const float4 b = *reinterpret_cast<const float4*>(xt + 128 + 4 * lane);
-                    mx = fmaxf(mx, fmaxf(fmaxf(b.x, b.y), fmaxf(b.z, b.w)));
-                }
-            }
-            // every chunk's phase must be seen complete before its next copy
-            for (; waited < kChunks - 1; ++waited) wait_bar(&bar_x[waited + 1], par, status, abort_v);
-            mx = tbk::warp_max(mx);
-            if (lane == 0) red[ww] = mx;
-            work_sync();
             float m = red[0];
 #pragma unroll
             for (int w = 1; w < kWorkWarps; ++w) m = fmaxf(m, red[w]);
-            // ---- exp in place + tile sums (full tiles unconditional; the
-            //      last tile may be partial)
-            const int nfull = cols / kTileN;
-            for (int t = ww; t < ntiles; t += kWorkWarps) {
-                float* xt = tp(t);
-                float s = 0.0f;
-                if (t < nfull) {
-                    float4 a = *reinterpret_cast<float4*>(xt + 4 * lane);
-                    float4 b = *reinterpret_cast<float4*>(xt + 128 + 4 * lane);
+            // ---- e into the row buffer, from x in L2, + tile sums (full tiles
+            //      unconditional; the last tile may be partial)
+            const float* xr = row_x(i);
+            for (int t0 = ww; t0 < ntiles; t0 += 2 * kWorkWarps) {
+                float4 v[4];  // two tiles' loads in flight per lane
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int t = t0 + u * kWorkWarps;
+                    const float* gt = xr + (int64_t)t * kTileN;
+                    const int n = t < ntiles ? min(kTileN, cols - t * kTileN) : 0;
+                    v[2 * u] = v[2 * u + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (4 * lane < n) v[2 * u] = *reinterpret_cast<const float4*>(gt + 4 * lane);
+                    if (128 + 4 * lane < n)
+                        v[2 * u + 1] = *reinterpret_cast<const float4*>(gt + 128 + 4 * lane);
+                }
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int t = t0 + u * kWorkWarps;
+                    if (t >= ntiles) break;  // warp-uniform
+                    const int n = min(kTileN, cols - t * kTileN);
+                    float* xt = tp(t);
+                    float4 a = v[2 * u], b = v[2 * u + 1];
                     a.x = expo(a.x, m); a.y = expo(a.y, m); a.z = expo(a.z, m); a.w = expo(a.w, m);
                     b.x = expo(b.x, m); b.y = expo(b.y, m); b.z = expo(b.z, m); b.w = expo(b.w, m);
-                    *reinterpret_cast<float4*>(xt + 4 * lane) = a;
-                    *reinterpret_cast<float4*>(xt + 128 + 4 * lane) = b;
-                    s = ((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w));
-                } else {
-                    const int n = cols - t * kTileN;
+                    float s = 0.0f;
                     if (4 * lane < n) {
-                        float4 a = *reinterpret_cast<float4*>(xt + 4 * lane);
-                        a.x = expo(a.x, m); a.y = expo(a.y, m); a.z = expo(a.z, m); a.w = expo(a.w, m);
                         *reinterpret_cast<float4*>(xt + 4 * lane) = a;
                         s = (a.x + a.y) + (a.z + a.w);
                     }
                     if (128 + 4 * lane < n) {
-                        float4 b = *reinterpret_cast<float4*>(xt + 128 + 4 * lane);
-                        b.x = expo(b.x, m); b.y = expo(b.y, m); b.z = expo(b.z, m); b.w = expo(b.w, m);
                         *reinterpret_cast<float4*>(xt + 128 + 4 * lane) = b;
                         s += (b.x + b.y) + (b.z + b.w);
                     }
+                    s = warp_sum_est(s);
+                    if (lane == 0) sh.tsum[t] = s;
                 }
-                s = warp_sum_est(s);
-                if (lane == 0) sh.tsum[t] = s;
             }
             // Buffer k last held row i - kBufs: its scan must be over.  The
             // finalizers must have taken row i-3's sum and max: then ring slot
@@ -393,86 +392,82 @@ k_softmax_staged(const float* x, float* y, int rows, int cols, int nslot, unsign
                     row_m[i & 3] = m;
                 }
             }
+            // ---- the next row's max, from L2, by the workers the estimate and
+            //      tile 0 leave free (warps 1 .. kWorkWarps - 2)
+            if (i + 1 < nloc)
+                part_max(row_x(i + 1), 1, kWorkWarps - 2);
             work_sync();
             // ---- units: (D0, D1) per tile; a slotted tile's terms go to its slot
-            for (int t = ww; t < ntiles; t += kWorkWarps) {
-                const float* xt = tp(t);
-                const uint32_t meta = R.meta[t];
-                const int b = (int)(int8_t)(meta & 0xffu);
-                const uint32_t slot = meta >> 24;
-                float4 a, c;
-                if (t < nfull) {
-                    a = *reinterpret_cast<const float4*>(xt + 4 * lane);
-                    c = *reinterpret_cast<const float4*>(xt + 128 + 4 * lane);
-                } else {
-                    const int n = cols - t * kTileN;
-                    a = make_float4(0.f, 0.f, 0.f, 0.f);
-                    c = a;
-                    if (4 * lane < n) a = *reinterpret_cast<const float4*>(xt + 4 * lane);
-                    if (128 + 4 * lane < n) c = *reinterpret_cast<const float4*>(xt + 128 + 4 * lane);
-                }
-                if (slot < (uint32_t)nslot) {  // warp-uniform; terms past cols are 0
-                    Slot& S = SL[slot];
-                    *reinterpret_cast<float4*>(S.e + 4 * lane) = a;
-                    *reinterpret_cast<float4*>(S.e + 128 + 4 * lane) = c;
-                }
-                const float e[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
-                const float iu = tbk::inv_grid(b == tbk::kNoBinade ? 0 : b);
-                float acc = 0.0f, dm = 0.0f;
+            {
+                for (int t = ww; t < ntiles; t += kWorkWarps) {
+                    const float* xt = tp(t);
+                    const uint32_t meta = R.meta[t];
+                    const int b = (int)(int8_t)(meta & 0xffu);
+                    const uint32_t slot = meta >> 24;
+                    float4 a, c;
+                    if (t < nfull) {
+                        a = *reinterpret_cast<const float4*>(xt + 4 * lane);
+                        c = *reinterpret_cast<const float4*>(xt + 128 + 4 * lane);
+                    } else {
+                        const int n = cols - t * kTileN;
+                        a = make_float4(0.f, 0.f, 0.f, 0.f);
+                        c = a;
+                        if (4 * lane < n) a = *reinterpret_cast<const float4*>(xt + 4 * lane);
+                        if (128 + 4 * lane < n) c = *reinterpret_cast<const float4*>(xt + 128 + 4 * lane);
+                    }
+                    if (slot < (uint32_t)nslot) {  // warp-uniform; terms past cols are 0
+                        Slot& S = SL[slot];
+                        *reinterpret_cast<float4*>(S.e + 4 * lane) = a;
+                        *reinterpret_cast<float4*>(S.e + 128 + 4 * lane) = c;
+                    }
+                    const float e[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+                    const float iu = tbk::inv_grid(b == tbk::kNoBinade ? 0 : b);
+                    float acc = 0.0f, dm = 0.0f;
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    const float tt = __fmul_rn(e[q], iu);
-                    const float r = __fsub_rn(__fadd_rn(tt, kMagic), kMagic);
-                    acc = __fadd_rn(acc, r);
-                    dm = fmaxf(dm, fabsf(__fsub_rn(tt, r)));
-                }
-                // acc < 2^22 - 1 implies every t < 2^22 - 1/2: the magic
-                // rounding was exact; NaN fails the test too.
-                const bool big = __any_sync(tbk::kFull, !(acc < 4194303.0f));
-                const bool tie = __any_sync(tbk::kFull, dm == 0.5f);
-                const uint32_t sum_u =
-                    __reduce_add_sync(tbk::kFull, magic_int(__fadd_rn(fminf(acc, 4194303.0f), kMagic)));
-                uint2 D = make_uint2(sum_u, sum_u);
-                uint32_t flags = 0;
-                if (b == tbk::kNoBinade) {
-                    D = make_uint2(0u, 0u);
-                    flags = kExact;
-                } else if (big) {
-                    D = make_uint2(kSat, kSat);
-                } else if (tie) {
-                    Fn fa{0u, 0u}, fb{0u, 0u};
+                    for (int q = 0; q < 8; ++q) {
+                        const float tt = __fmul_rn(e[q], iu);
+                        const float r = __fsub_rn(__fadd_rn(tt, kMagic), kMagic);
+                        acc = __fadd_rn(acc, r);
+                        dm = fmaxf(dm, fabsf(__fsub_rn(tt, r)));
+                    }
+                    // acc < 2^22 - 1 implies every t < 2^22 - 1/2: the magic
+                    // rounding was exact; NaN fails the test too.
+                    const bool big = __any_sync(tbk::kFull, !(acc < 4194303.0f));
+                    const bool tie = __any_sync(tbk::kFull, dm == 0.5f);
+                    const uint32_t sum_u =
+                        __reduce_add_sync(tbk::kFull, magic_int(__fadd_rn(fminf(acc, 4194303.0f), kMagic)));
+                    uint2 D = make_uint2(sum_u, sum_u);
+                    uint32_t flags = 0;
+                    if (b == tbk::kNoBinade) {
+                        D = make_uint2(0u, 0u);
+                        flags = kExact;
+                    } else if (big) {
+                        D = make_uint2(kSat, kSat);
+                    } else if (tie) {
+                        Fn fa{0u, 0u}, fb{0u, 0u};
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) fa = compose(fa, term_fn(e[q], iu));
+                        for (int q = 0; q < 4; ++q) fa = compose(fa, term_fn(e[q], iu));
 #pragma unroll
-                    for (int q = 4; q < 8; ++q) fb = compose(fb, term_fn(e[q], iu));
-                    fa = warp_compose(fa);
-                    fb = warp_compose(fb);
-                    const Fn ft = compose(fa, fb);
-                    D = make_uint2(ft.a0, ft.a1);
-                }
-                if (lane == 0) {
-                    R.D[t] = D;
-                    if (flags) R.meta[t] = meta | flags;
+                        for (int q = 4; q < 8; ++q) fb = compose(fb, term_fn(e[q], iu));
+                        fa = warp_compose(fa);
+                        fb = warp_compose(fb);
+                        const Fn ft = compose(fa, fb);
+                        D = make_uint2(ft.a0, ft.a1);
+                    }
+                    if (lane == 0) {
+                        R.D[t] = D;
+                        if (flags) R.meta[t] = meta | flags;
+                    }
                 }
             }
             work_sync();
-            // The row buffer is free: the next row's copy starts now.  The
-            // summaries are complete: hand the row to its scanner.
+            // The summaries are complete: hand the row to its scanner.
             if (wt == 0) {
-                if (i + 1 < nloc && !*abort_v) {
-                    tbk::fence_proxy_async_shared();
-                    for (int c = 0; c < kChunks; ++c) issue_chunk(i + 1, c, pol_last);
-                }
                 __threadfence_block();
                 tbk::mbar_arrive(&bar_ready[k]);
             }
         }
     }
-    // No copy may still be writing this CTA's shared memory when it exits
-    // (possible only after a timeout): a last bounded wait on each chunk.
-    if (wt == 0 && nloc > 0)
-        for (int c = 0; c < kChunks; ++c)
-            tbk::mbar_wait(&bar_x[c], (uint32_t)(nloc - 1) & 1u, status, 200000000ull);
 }
 
 // Shared memory besides the row buffer: summaries, tile sums, slots.
