@@ -104,7 +104,7 @@ TRAFFIC_PER_ROW = {
     "7b": {
         "embedding": 32137856 / 4096,
         "layer_chain": 485573888 / 4096,
-        "softmax": (192851456 + 74482944) / 1024,
+        "softmax": (200159488 + 75085568) / 1024,
         "argmax": 530358016 / 4096,
     },
     # captured on one GPU: softmax/argmax over 1024 x 128256 logits, the
