@@ -67,11 +67,14 @@ typedef struct {
 } TbNormParams;
 
 /* N:M of a sparse linear layer (include/tensorbit/run/ops.h:23-26 in the
- * engine; the CPU adapter reads it from the op's params). */
+ * engine; the CPU adapter reads it from the op's params).  In the engine,
+ * ops.h is included first and its definition stands. */
+#ifndef TENSORBIT_RUN_OPS_H
 typedef struct {
     int nm_n;
     int nm_m;
 } TbLinearParams;
+#endif
 
 typedef struct {
     float scale;

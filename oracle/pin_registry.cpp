@@ -39,6 +39,8 @@ int tb_cpu_rope_dispatch(void*, const void**, int, const void*);
 int tb_cpu_residual_add_dispatch(void*, const void**, int, const void*);
 int tb_cpu_embedding_dispatch(void*, const void**, int, const void*);
 int tb_cpu_conv2d_dispatch(void*, const void**, int, const void*);
+// The engine-side slots of the added ops (tensorbit-run_b200/engine/cpu_rowops.c).
+void tb_cpu_rowops_fill(TbBackend* cpu);
 
 int tb_backend_cpu_init(void) {
     TbBackend cpu;
@@ -58,6 +60,7 @@ int tb_backend_cpu_init(void) {
     cpu.ops[TB_OP_RESIDUAL_ADD] = tb_cpu_residual_add_dispatch;
     cpu.ops[TB_OP_EMBEDDING] = tb_cpu_embedding_dispatch;
     cpu.ops[TB_OP_CONV2D] = tb_cpu_conv2d_dispatch;
+    tb_cpu_rowops_fill(&cpu);
     return tb_backend_register(&cpu);
 }
 
@@ -85,6 +88,81 @@ int pin_registry_rms_norm_host(float* y, const float* x, const float* w, size_t 
     Tensor tx = Tensor::wrap(const_cast<float*>(x), {n}, Dtype::kF32, DeviceLocation::kHost);
     Tensor tw = Tensor::wrap(const_cast<float*>(w), {n}, Dtype::kF32, DeviceLocation::kHost);
     return rms_norm(ty, tx, tw, eps);
+}
+
+// The added ops through tb_dispatch_* on host f32 tensors of [rows, cols]:
+// they must reach the CPU backend's composition slots.
+static TbTensor host2(void* p, size_t rows, size_t cols, TbDtype dt = TB_DTYPE_F32) {
+    TbTensor t;
+    std::memset(&t, 0, sizeof t);
+    t.data = p;
+    t.rank = 2;
+    t.shape[0] = rows;
+    t.shape[1] = cols;
+    t.dtype = dt;
+    t.device = TB_DEVICE_CPU;
+    return t;
+}
+static TbTensor host3(void* p, size_t a, size_t b, size_t c) {
+    TbTensor t = host2(p, a, b);
+    t.rank = 3;
+    t.shape[2] = c;
+    return t;
+}
+
+int pin_registry_residual_rms_norm_host(float* y, float* h, const float* x, const float* r,
+                                        const float* w, size_t rows, size_t cols, float eps) {
+    TbTensor ty = host2(y, rows, cols), th = host2(h, rows, cols);
+    TbTensor tx = host2(const_cast<float*>(x), rows, cols);
+    TbTensor tr = host2(const_cast<float*>(r), rows, cols);
+    TbTensor tw = host2(const_cast<float*>(w), 1, cols);
+    tw.rank = 1;
+    tw.shape[0] = cols;
+    return tb_dispatch_residual_rms_norm(&ty, &th, &tx, &tr, &tw, eps);
+}
+
+int pin_registry_swiglu_host(float* out, const float* g, const float* u, size_t rows, size_t cols) {
+    TbTensor to = host2(out, rows, cols), tg = host2(const_cast<float*>(g), rows, cols);
+    TbTensor tu = host2(const_cast<float*>(u), rows, cols);
+    return tb_dispatch_swiglu(&to, &tg, &tu);
+}
+
+int pin_registry_argmax_host(int32_t* out, const float* x, size_t rows, size_t cols) {
+    TbTensor tx = host2(const_cast<float*>(x), rows, cols);
+    TbTensor to = host2(out, rows, 1, TB_DTYPE_I32);
+    to.rank = 1;
+    to.shape[0] = rows;
+    return tb_dispatch_argmax(&to, &tx);
+}
+
+int pin_registry_rope_rows_host(float* q, float* k, const int32_t* pos, size_t rows, size_t hq,
+                                size_t hkv, size_t d, float theta) {
+    TbTensor tq = host3(q, rows, hq, d), tk = host3(k, rows, hkv, d);
+    return tb_dispatch_rope_rows(&tq, &tk, pos, theta, (int)d, 0);
+}
+
+int pin_registry_layer_chain_host(float* y, float* h, float* act, const float* x, const float* r,
+                                  const float* w, float* q, float* k, const float* g,
+                                  const float* u, const int32_t* pos, size_t rows, size_t hidden,
+                                  size_t hq, size_t hkv, size_t d, size_t inter, float eps,
+                                  float theta) {
+    TbTensor ty = host2(y, rows, hidden), th = host2(h, rows, hidden);
+    TbTensor ta = host2(act, rows, inter);
+    TbTensor tx = host2(const_cast<float*>(x), rows, hidden);
+    TbTensor tr = host2(const_cast<float*>(r), rows, hidden);
+    TbTensor tw = host2(const_cast<float*>(w), 1, hidden);
+    tw.rank = 1;
+    tw.shape[0] = hidden;
+    TbTensor tq = host3(q, rows, hq, d), tk = host3(k, rows, hkv, d);
+    TbTensor tg = host2(const_cast<float*>(g), rows, inter);
+    TbTensor tu = host2(const_cast<float*>(u), rows, inter);
+    TbLayerChainParams p;
+    p.eps = eps;
+    p.positions = pos;
+    p.theta = theta;
+    p.head_dim = (int)d;
+    p.max_position = 0;
+    return tb_dispatch_layer_chain(&ty, &th, &ta, &tx, &tr, &tw, &tq, &tk, &tg, &tu, &p);
 }
 
 }  // extern "C"

@@ -347,8 +347,12 @@ def test_engine_backend_registry_builds_against_the_b200_header():
     libtb_b200.so (oracle/_ref/libpinregistry.so).  Its init registers "cpu"
     and "b200"; device-aware routing picks "b200" for CUDA tensors and
     "cpu" for host tensors; the engine's C++ rms_norm wrapper on host
-    tensors reaches the reference's CPU kernel.  In a fresh process: the
-    registry is a process-wide singleton."""
+    tensors reaches the reference's CPU kernel.  The engine's CPU adapters
+    are compiled against the swapped header too, and the five added ops
+    reach the CPU backend's compositions (tensorbit-run_b200/engine/
+    cpu_rowops.c) for host tensors, bit-exact with the oracle over the
+    reference's kernels.  In a fresh process: the registry is a process-wide
+    singleton."""
     import subprocess
     import sys
     code = r'''
@@ -361,6 +365,12 @@ L = C.CDLL(sys.argv[1])
 L.pin_registry_best.restype = C.c_char_p
 L.pin_registry_has.argtypes = [C.c_char_p]
 L.pin_registry_rms_norm_host.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_float]
+V, Z, F = C.c_void_p, C.c_size_t, C.c_float
+L.pin_registry_residual_rms_norm_host.argtypes = [V] * 5 + [Z, Z, F]
+L.pin_registry_swiglu_host.argtypes = [V] * 3 + [Z, Z]
+L.pin_registry_argmax_host.argtypes = [V] * 2 + [Z, Z]
+L.pin_registry_rope_rows_host.argtypes = [V] * 3 + [Z] * 4 + [F]
+L.pin_registry_layer_chain_host.argtypes = [V] * 11 + [Z] * 6 + [F, F]
 assert L.pin_registry_init() == 2
 assert L.pin_registry_init() == 2  # init is once per process
 assert L.pin_registry_has(b"cpu") and L.pin_registry_has(b"b200")
@@ -369,6 +379,7 @@ for op in ("RMS_NORM", "RESIDUAL_ADD", "GELU", "SILU", "SOFTMAX", "ROPE", "EMBED
     assert L.pin_registry_best(T.OP[op], 0) == b"cpu", op
 for op in ("RESIDUAL_RMS_NORM", "SWIGLU", "ARGMAX", "ROPE_ROWS", "LAYER_CHAIN"):
     assert L.pin_registry_best(T.OP[op], 1) == b"b200", op
+    assert L.pin_registry_best(T.OP[op], 0) == b"cpu", op  # engine/cpu_rowops.c
 assert L.pin_registry_best(T.OP["LAYER_NORM"], 1) == b"cpu"  # no b200 slot: the cpu one
 rng = np.random.default_rng(9)
 x = rng.standard_normal(4096).astype(np.float32)
@@ -376,6 +387,43 @@ w = (1 + 0.1 * rng.standard_normal(4096)).astype(np.float32)
 y = np.zeros_like(x)
 assert L.pin_registry_rms_norm_host(y.ctypes.data, x.ctypes.data, w.ctypes.data, x.size, 1e-5) == 0
 assert np.array_equal(y, O.rms_norm_vec(x, w, 1e-5))
+# the added ops on host tensors reach the CPU compositions of the engine's
+# kernels: bit-exact with the oracle over the reference's own kernels
+R, H, I, HQ, HKV, D = 6, 256, 704, 4, 2, 64
+f = lambda *sh: rng.standard_normal(sh).astype(np.float32)
+P = lambda a: a.ctypes.data
+x2, r2, g2, u2 = f(R, H), f(R, H), f(R, I), f(R, I)
+w2 = (1 + 0.1 * f(H)).astype(np.float32)
+q3, k3 = f(R, HQ, D), f(R, HKV, D)
+pos = np.array([0, 1, 7, 100, 2047, 5], np.int32)
+h_want, y_want = O.residual_rms_norm(x2, r2, w2, 1e-5, impl=O.REF)
+h, yy = np.zeros_like(x2), np.zeros_like(x2)
+assert L.pin_registry_residual_rms_norm_host(C.c_void_p(P(yy)), C.c_void_p(P(h)), C.c_void_p(P(x2)),
+                                             C.c_void_p(P(r2)), C.c_void_p(P(w2)), R, H,
+                                             C.c_float(1e-5)) == 0
+assert np.array_equal(h, h_want) and np.array_equal(yy, y_want)
+act = np.zeros_like(g2)
+assert L.pin_registry_swiglu_host(C.c_void_p(P(act)), C.c_void_p(P(g2)), C.c_void_p(P(u2)), R, I) == 0
+assert np.array_equal(act, O.swiglu(g2, u2, impl=O.REF))
+lg = f(R, 1001)
+lg[2, :] = 1.0  # ties: the first maximum
+lg[3, 0] = np.float32("nan")  # NaN at 0 keeps 0
+tok = np.full(R, -1, np.int32)
+assert L.pin_registry_argmax_host(C.c_void_p(P(tok)), C.c_void_p(P(lg)), R, 1001) == 0
+assert np.array_equal(tok, O.argmax(lg, impl=O.REF))
+qw, kw = O.rope(q3, k3, pos, 1e4, impl=O.REF)
+q, k = q3.copy(), k3.copy()
+assert L.pin_registry_rope_rows_host(C.c_void_p(P(q)), C.c_void_p(P(k)), C.c_void_p(P(pos)), R,
+                                     HQ, HKV, D, C.c_float(1e4)) == 0
+assert np.array_equal(q, qw) and np.array_equal(k, kw)
+q, k = q3.copy(), k3.copy()
+h, yy, act = np.zeros_like(x2), np.zeros_like(x2), np.zeros_like(g2)
+assert L.pin_registry_layer_chain_host(*[C.c_void_p(P(a)) for a in (yy, h, act, x2, r2, w2, q, k,
+                                                                      g2, u2, pos)],
+                                       R, H, HQ, HKV, D, I, C.c_float(1e-5), C.c_float(1e4)) == 0
+assert np.array_equal(h, h_want) and np.array_equal(yy, y_want)
+assert np.array_equal(q, qw) and np.array_equal(k, kw)
+assert np.array_equal(act, O.swiglu(g2, u2, impl=O.REF))
 print("ok")
 '''
     out = subprocess.run([sys.executable, "-c", code, PIN_REGISTRY_SO, ROOT,
