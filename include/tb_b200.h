@@ -224,8 +224,8 @@ int tb_b200_embedding_host_ids(int dtype, int64_t n_tokens, int64_t dim, int64_t
  * statically sized device array inside the library, held by every GPU that
  * loads it until the process exits.  At most TB_B200_STATIC_MAX_TOKENS ids
  * per call; more returns TB_ERR_INVALID_SHAPE with nothing queued.  The
- * first call on a device looks up the array's device address once (make it
- * before any stream capture on that device).  All calls share the array and
+ * first call on a device looks up the array's device address once
+ * (cudaGetSymbolAddress); later calls reuse it.  All calls share the array and
  * each starts by clearing the status word: calls whose work can overlap on
  * the GPU (different streams, no ordering between them) race on it.  The ids
  * are copied from ids_host on `stream`: from pageable memory the copy has
