@@ -272,7 +272,8 @@ def run_reference(args, world):
     v = round(nbytes / sec / 1e9, 3)
     return {"metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "strong" if args.config == "70b" else "weak", "vs_baseline": None,
+            "dtype": "bf16",
             "data": "synthetic (seeded, reference config distributions)", "impl": "reference",
             "config": {"workload": WORKLOAD, "rows_sampled": rows, "rows_per_step": CFG.rows},
             "rows_per_s": round(rows / sec, 1),
