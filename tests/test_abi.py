@@ -124,6 +124,25 @@ def test_p2p_entry_points_check_arguments_before_device_work():
     assert f(0, 0, 16, 100, None, None, 2, None, None) == 0  # no tokens: nothing to do
 
 
+def test_empty_inputs_are_no_ops():
+    """Zero rows (or zero elements) is nothing to do: every row op returns
+    TB_OK before it looks for a device or touches a pointer, as the
+    reference's loops do nothing for n = 0."""
+    L = T.lib()
+    N, F = None, C.c_float
+    assert L.tb_b200_softmax(T.F32, 0, 10, N, N, N, N) == 0
+    assert L.tb_b200_softmax(T.BF16, 5, 0, N, N, N, N) == 0
+    assert L.tb_b200_argmax(T.F32, 0, 10, N, N, N) == 0
+    assert L.tb_b200_silu(T.F32, 0, N, N, N) == 0
+    assert L.tb_b200_gelu(T.BF16, 0, N, N, N) == 0
+    assert L.tb_b200_swiglu(T.F32, 0, N, N, N, N) == 0
+    assert L.tb_b200_residual_add(T.F32, 0, N, N, N, N) == 0
+    assert L.tb_b200_rms_norm(T.F32, 0, 4, N, N, N, F(1e-5), N) == 0
+    assert L.tb_b200_residual_rms_norm(T.BF16, 0, 4, N, N, N, N, N, F(1e-5), N) == 0
+    assert L.tb_b200_embedding(T.F32, 0, 16, 100, N, N, N, N) == 0
+    assert L.tb_b200_rope_rows(T.F32, 0, 4, 4, 64, N, N, N, F(1e4), N, 0, N) == 0
+
+
 def test_partition_rule():
     lo, hi = C.c_int64(), C.c_int64()
     for total, parts in [(16384, 8), (10, 3), (5, 8), (128256, 7)]:
