@@ -116,6 +116,15 @@ TRAFFIC_PER_ROW = {
         "argmax": (525479680 + 4182784) / 1024,
     },
 }
+# What bounds each op of the 70b step, for the line's "limiter".
+LIMITER_NOTE = {
+    "softmax": "the in-order row sum needs the row three times; two 501 KB rows per SM in "
+               "flight exceed the L2, so DRAM moves ~2.1x the algorithmic bytes, and the "
+               "per-tile reduction chains are latency-bound",
+    "layer_chain": "HBM bandwidth (~0.9 of the copy peak)",
+    "argmax": "HBM bandwidth (read-only stream at the copy peak)",
+    "embedding": "HBM on one GPU; NVLink peer reads with more GPUs",
+}
 TRAFFIC_SOURCE = "ncu capture of the kernel (DRAM bytes read + written per row, scaled to the " \
                  "launch's rows)"
 
@@ -1300,6 +1309,12 @@ def run_sharded(args, rank, world, local):
         "rows_per_s": round(NT / (ms / 1e3), 1),
         "per_op": per_op,
         "largest_share": dom,
+        "limiter": {
+            "op": dom, "share_of_step": round(per_op_ms[dom] / step_sum, 3),
+            "why": LIMITER_NOTE.get(dom, "HBM bandwidth"),
+            "with_n": ("the per-GPU rows shrink as 1/N while the gather's share read over "
+                       "NVLink grows as (N-1)/N" if world > 1 else
+                       "one GPU: the gather reads local HBM only")},
         "gather": {"in_step": "one kernel over NCCL symmetric memory "
                               "(tb_b200_embedding_sharded_window)",
                    "window_ms": round(win_ms, 4), "nccl_sendrecv_ms": round(nccl_ms, 4),
