@@ -33,8 +33,9 @@
 //           (terms from y, or recomputed from x for bf16).
 //   pass 4  y = e * (1/sum).
 // HBM: one read of x, one write of y; the re-reads hit L2 (two rows per SM
-// in flight), helped by evict-first hints on the last read of x and
-// streaming stores of y.  Rows wider than the tile table (> 2.7M terms) use
+// in flight), helped by evict-last hints on pass 1's reads of x (pass 2
+// reads them again), evict-first hints on the last read of x, and streaming
+// stores of y.  Rows wider than the tile table (> 2.7M terms) use
 // one warp for the whole ordered sum.
 #include <math.h>
 
@@ -44,6 +45,7 @@
 #include "scan_tiles.cuh"
 #include "tb_device.cuh"
 #include "tb_internal.h"
+#include "tma.cuh"
 
 namespace {
 
@@ -56,11 +58,15 @@ static_assert(kTile == tbsm::kTileN, "tile size shared with scan_tiles.cuh");
 constexpr int kTileBytes = 12;   // shared bytes per tile (see k_softmax_tiles)
 constexpr int kSlots = 24;       // tiles whose terms are kept in shared memory
 
-enum Cache { kKeep = 0, kLast = 1 };
+// L2 policy of a load: default, streaming (last use), or evict-last (f32
+// only: pass 1's loads of x, which pass 2 reads again).
+enum Cache { kKeep = 0, kLast = 1, kHold = 2 };
 
 template <int CACHE>
 __device__ __forceinline__ float4 ld4(const float* p) {
     if constexpr (CACHE == kLast) return __ldcs(reinterpret_cast<const float4*>(p));
+    if constexpr (CACHE == kHold)
+        return tbk::ld_f4_hint(reinterpret_cast<const float4*>(p), tbk::policy_evict_last());
     return *reinterpret_cast<const float4*>(p);
 }
 template <int CACHE>
@@ -235,7 +241,7 @@ __device__ __forceinline__ void tiles_row(const T* x, const T* mask, T* y, int64
     // ---- pass 1: tile max and tile sum estimate
     warp_tiles<NW, kU>(
         warp, ntiles,
-        [&](int t, float (&v)[kK]) { return load_oct<T, VEC>(xr, mr, cols, t, lane, v); },
+        [&](int t, float (&v)[kK]) { return load_oct<T, VEC, kHold>(xr, mr, cols, t, lane, v); },
         [&](int t, float (&v)[kK], int nv) {
             float tm = -INFINITY;
 #pragma unroll
