@@ -112,7 +112,7 @@ TRAFFIC_PER_ROW = {
     "70b": {
         "embedding": (130690304 + 84914432) / 8192,
         "layer_chain": (340854784 + 167031552) / 2048,
-        "softmax": (1295032320 + 920313344) / 1024,
+        "softmax": (1178672384 + 467714048) / 1024,
         "argmax": (525479680 + 4182784) / 1024,
     },
 }

@@ -20,7 +20,7 @@
 //           Tiles likely to need term-by-term work (the first tile, a
 //           predicted binade change, an estimate near a power of two) get a
 //           shared-memory slot for their terms.
-//   pass 2  e_i (stored into y for f32 output); per tile the integer sum D
+//   pass 2  e_i; per tile the integer sum D
 //           of rne(e/u) on the grid of b_t; a tile with an exact tie or a
 //           term of 2^22 units or more is flagged (kStop) and takes a free
 //           slot.  A slotted tile keeps its terms and the prefix sums of
@@ -30,13 +30,18 @@
 //           redux per 32 tiles, each slotted or flagged tile resolved with
 //           a ballot per event over its prefix table, a misprediction
 //           located with a scan, a tile without a slot summed term by term
-//           (terms from y, or recomputed from x for bf16).
-//   pass 4  y = e * (1/sum).
-// HBM: one read of x, one write of y; the re-reads hit L2 (two rows per SM
-// in flight), helped by evict-last hints on pass 1's reads of x (pass 2
-// reads them again), evict-first hints on the last read of x, and streaming
-// stores of y.  Rows wider than the tile table (> 2.7M terms) use
-// one warp for the whole ordered sum.
+//           (terms recomputed from x).
+//   pass 4  y = e * (1/sum), e recomputed from x.
+// HBM: one read of x, one write of y; passes 2 and 4 read x again from L2
+// (two rows per SM in flight, 152 MB, a little more than L2 holds), helped
+// by evict-last hints on pass 1's reads of x, evict-first hints on pass 4's
+// (the last), and streaming stores of y.  Pass 2 walks the row from its end,
+// passes 1 and 4 from its start: each pass begins with the tiles the one
+// before touched last, so the lines L2 has kept longest are not the ones
+// needed first.
+// e is never stored: a store of e into y and its re-read in pass 4 would
+// double the row data each CTA keeps live in L2.  Rows wider than the tile
+// table (> 2.7M terms) use one warp for the whole ordered sum.
 #include <math.h>
 
 #include <algorithm>
@@ -59,7 +64,7 @@ constexpr int kTileBytes = 12;   // shared bytes per tile (see k_softmax_tiles)
 constexpr int kSlots = 24;       // tiles whose terms are kept in shared memory
 
 // L2 policy of a load: default, streaming (last use), or evict-last (f32
-// only: pass 1's loads of x, which pass 2 reads again).
+// only: pass 1's loads of x, which passes 2 and 4 read again).
 enum Cache { kKeep = 0, kLast = 1, kHold = 2 };
 
 template <int CACHE>
@@ -145,54 +150,47 @@ __device__ __forceinline__ V block_excl_scan(V local, V* carry) {
     return base + incl - local;
 }
 
-// Terms of a tile without a slot, for the scanner: from y, where pass 2
-// stored e (f32 output), else recomputed from x (+ mask).
-template <typename T, bool VEC, bool FROM_Y>
+// Terms of a tile without a slot, for the scanner: recomputed from x (+ mask).
+template <typename T, bool VEC>
 struct RowTerms {
     const T* xr;
     const T* mr;
-    const T* yr;
     int64_t cols;
     float m;
     __device__ __forceinline__ void operator()(int tile, int n, float (&e)[kK]) const {
         const int lane = threadIdx.x & 31;
-        const int64_t i0 = (int64_t)tile * kTile + lane * kK;
-        if constexpr (FROM_Y) {
+        float v[kK];
+        load_oct<T, VEC>(xr, mr, cols, tile, lane, v);
 #pragma unroll
-            for (int j = 0; j < kK; ++j) e[j] = lane * kK + j < n ? Elt<T>::load(yr + i0 + j) : 0.0f;
-        } else {
-            float v[kK];
-            load_oct<T, VEC>(xr, mr, cols, tile, lane, v);
-#pragma unroll
-            for (int j = 0; j < kK; ++j) e[j] = lane * kK + j < n ? expo(v[j], m) : 0.0f;
-        }
+        for (int j = 0; j < kK; ++j) e[j] = lane * kK + j < n ? expo(v[j], m) : 0.0f;
     }
 };
 
-// A warp's tiles warp, warp + NW, ... in steps of KU tiles, each step's
-// loads issued before the previous step is processed (two register sets):
-// load(t, v) fills the lane's kK terms of tile t and returns how many are in
-// the row; proc(t, v, nv) may overwrite v.
-template <int NW, int KU, class Load, class Proc>
+// A warp's tiles warp, warp + NW, ... (REV: counted from the row's end) in
+// steps of KU tiles, each step's loads issued before the previous step is
+// processed (two register sets): load(t, v) fills the lane's kK terms of
+// tile t and returns how many are in the row; proc(t, v, nv) may overwrite v.
+template <int NW, int KU, bool REV = false, class Load, class Proc>
 __device__ __forceinline__ void warp_tiles(int warp, int ntiles, const Load& load,
                                            const Proc& proc) {
+    auto at = [&](int t) { return REV ? ntiles - 1 - t : t; };
     float a[KU][kK], b[KU][kK];
     int na[KU], nb[KU];
 #pragma unroll
     for (int u = 0; u < KU; ++u) {
         const int t = warp + u * NW;
-        na[u] = t < ntiles ? load(t, a[u]) : 0;
+        na[u] = t < ntiles ? load(at(t), a[u]) : 0;
     }
     for (int tb = warp; tb < ntiles; tb += NW * KU) {
 #pragma unroll
         for (int u = 0; u < KU; ++u) {
             const int t = tb + (KU + u) * NW;
-            nb[u] = t < ntiles ? load(t, b[u]) : 0;
+            nb[u] = t < ntiles ? load(at(t), b[u]) : 0;
         }
 #pragma unroll
         for (int u = 0; u < KU; ++u) {
             const int t = tb + u * NW;
-            if (t < ntiles) proc(t, a[u], na[u]);  // warp-uniform
+            if (t < ntiles) proc(at(t), a[u], na[u]);  // warp-uniform
         }
 #pragma unroll
         for (int u = 0; u < KU; ++u) {
@@ -211,15 +209,15 @@ __device__ __forceinline__ float warp_max_redux(float v) {
     return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
-// One row (the whole CTA).  f32: pass 2 stores e into y (f32 output holds
-// it exactly) and pass 4 rescales y; bf16: pass 4 recomputes e from x.
+// One row (the whole CTA).  Pass 4 recomputes e from x (the same
+// expression, so the same bits): x is the only row-sized data a CTA keeps
+// live in L2.
 template <typename T, int NT, bool VEC, int KU, int KU2>
 __device__ __forceinline__ void tiles_row(const T* x, const T* mask, T* y, int64_t row,
                                           int64_t cols, int ntiles, int nslot) {
     constexpr int NW = NT / 32;
     constexpr int kU = KU;    // tiles per step of a warp in passes 1 and 4
     constexpr int kU2 = KU2;  // the same in pass 2 (more registers per tile)
-    constexpr bool kStoreE = sizeof(T) == 4;
     extern __shared__ __align__(16) unsigned char smem[];
     tbsm::SlotTab* slots = reinterpret_cast<tbsm::SlotTab*>(smem);  // nslot slotted tiles
     float2* tms = reinterpret_cast<float2*>(smem + sizeof(tbsm::SlotTab) * nslot);
@@ -298,25 +296,14 @@ __device__ __forceinline__ void tiles_row(const T* x, const T* mask, T* y, int64
     __syncthreads();  // tms fully consumed: tD may now overwrite it
 
     // ---- pass 2: e, the tiles' units, slots, tile 0's in-order sum
-    warp_tiles<NW, kU2>(
+    warp_tiles<NW, kU2, true>(  // last tile first: see the file comment
         warp, ntiles,
         [&](int t, float (&v)[kK]) {
-            return load_oct<T, VEC, kStoreE ? kLast : kKeep>(xr, mr, cols, t, lane, v);
+            return load_oct<T, VEC>(xr, mr, cols, t, lane, v);
         },
         [&](int t, float (&e)[kK], int nv) {
 #pragma unroll
             for (int j = 0; j < kK; ++j) e[j] = j < nv ? expo(e[j], m) : 0.0f;
-            const int64_t i0 = (int64_t)t * kTile + lane * kK;
-            if constexpr (kStoreE) {
-                if (VEC && nv == kK) {
-                    *reinterpret_cast<float4*>(yr + i0) = make_float4(e[0], e[1], e[2], e[3]);
-                    *reinterpret_cast<float4*>(yr + i0 + 4) = make_float4(e[4], e[5], e[6], e[7]);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < kK; ++j)
-                        if (j < nv) Elt<T>::store(yr + i0 + j, e[j]);
-                }
-            }
             uint32_t meta = tmeta[t];
             const int b = (int)(int8_t)(meta & 0xffu);
             const float iu = tbk::inv_grid(b == tbk::kNoBinade ? 0 : b);
@@ -371,7 +358,7 @@ __device__ __forceinline__ void tiles_row(const T* x, const T* mask, T* y, int64
     // ---- pass 3: the ordered sum over tiles (warp 0)
     if (warp == 0) {
         const float s = tbsm::scan_tiles_tab(tD, tmeta, tile0_sum, slots, nslot,
-                                             RowTerms<T, VEC, kStoreE>{xr, mr, yr, cols, m},
+                                             RowTerms<T, VEC>{xr, mr, cols, m},
                                              (int)cols);
         if (lane == 0) row_sum = s;
     }
@@ -381,25 +368,7 @@ __device__ __forceinline__ void tiles_row(const T* x, const T* mask, T* y, int64
     const float sum = row_sum;
     const bool norm = sum > 0.0f;
     const float inv = __fdiv_rn(1.0f, sum);
-    if constexpr (kStoreE) {
-        if (!norm) return;  // y already holds e (softmax.c:24)
-        warp_tiles<NW, kU>(
-            warp, ntiles,
-            [&](int t, float (&v)[kK]) { return load_oct<T, VEC, kLast>(yr, nullptr, cols, t, lane, v); },
-            [&](int t, float (&v)[kK], int nv) {
-                const int64_t i0 = (int64_t)t * kTile + lane * kK;
-#pragma unroll
-                for (int j = 0; j < kK; ++j) v[j] = __fmul_rn(v[j], inv);
-                if (VEC && nv == kK) {
-                    __stcs(reinterpret_cast<float4*>(yr + i0), make_float4(v[0], v[1], v[2], v[3]));
-                    __stcs(reinterpret_cast<float4*>(yr + i0 + 4), make_float4(v[4], v[5], v[6], v[7]));
-                } else {
-#pragma unroll
-                    for (int j = 0; j < kK; ++j)
-                        if (j < nv) Elt<T>::store(yr + i0 + j, v[j]);
-                }
-            });
-    } else {
+    {
         warp_tiles<NW, kU>(
             warp, ntiles,
             [&](int t, float (&v)[kK]) { return load_oct<T, VEC, kLast>(xr, mr, cols, t, lane, v); },
