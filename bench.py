@@ -118,9 +118,9 @@ TRAFFIC_PER_ROW = {
 }
 # What bounds each op of the 70b step, for the line's "limiter".
 LIMITER_NOTE = {
-    "softmax": "the in-order row sum needs the row three times; two 501 KB rows per SM in "
-               "flight exceed the L2, so DRAM moves ~2.1x the algorithmic bytes, and the "
-               "per-tile reduction chains are latency-bound",
+    "softmax": "the in-order row sum reads the row three times; two 501 KB rows per SM in "
+               "flight are a little more than the L2 holds, so DRAM moves ~1.6x the "
+               "algorithmic bytes, and the per-tile reduction chains bound the issue rate",
     "layer_chain": "HBM bandwidth (~0.9 of the copy peak)",
     "argmax": "HBM bandwidth (read-only stream at the copy peak)",
     "embedding": "HBM on one GPU; NVLink peer reads with more GPUs",
